@@ -1,0 +1,30 @@
+"""aoa_kv_b200 — B200 (sm_100a) sparse-decode path of AOA-KV / Quest.
+
+Public surface, named after the reference's quest.utils
+(kernels/aoa_kv/quest/utils/__init__.py:11-23):
+
+    TensorLayout, KvCache, InferenceController, BatchDecodeWithPagedKVCacheWrapper,
+    append_kv, decode_estimate, decode_topk, decode_sparse_attn,
+    prefill_forward, apply_rope_in_place, rms_norm_forward (not built here)
+
+plus ``topk_filtering`` (the raw top-k op) and
+``InferenceController.decode_step`` (append + estimate + top-k + decode in one
+library call). The kernels live in libaoakv.so (C ABI: include/aoakv.h).
+"""
+from . import _lib
+from ._lib import AoaKvError, check_device, device_error
+from .controller import InferenceController, KvCache, KvPool, TensorLayout
+from .decode_wrapper import BatchDecodeWithPagedKVCacheWrapper
+from .ops import (append_kv, apply_rope_in_place, decode_estimate, decode_sparse_attn,
+                  decode_topk, prefill_forward, rms_norm_forward, topk_filtering)
+
+__all__ = [
+    "TensorLayout", "KvCache", "KvPool", "InferenceController",
+    "BatchDecodeWithPagedKVCacheWrapper", "append_kv", "prefill_forward", "decode_estimate",
+    "decode_topk", "decode_sparse_attn", "rms_norm_forward", "apply_rope_in_place",
+    "topk_filtering", "AoaKvError", "check_device", "device_error",
+]
+
+
+def library_path() -> str:
+    return str(_lib.LIB_PATH)

@@ -1,0 +1,151 @@
+// Shared device helpers and host plumbing for libaoakv (sm_100a only).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/aoakv.h"
+
+namespace aoakv {
+
+// ---------------------------------------------------------------- host side
+// Records `msg` as the calling thread's last error and returns `code`.
+int set_error(int code, const std::string& msg);
+// Converts a CUDA status into AOAKV_ERR_CUDA with context, or AOAKV_OK.
+int cuda_status(cudaError_t st, const char* what);
+// Device pointer of the library's device-side error word on the current
+// device (looked up once per device).
+int* dev_error_ptr();
+// Number of SMs of the current device (cached per device).
+int num_sms();
+
+#define AOAKV_CHECK_ARG(cond, msg)                                   \
+  do {                                                               \
+    if (!(cond)) return ::aoakv::set_error(AOAKV_ERR_INVALID_ARG, msg); \
+  } while (0)
+
+#define AOAKV_CUDA_TRY(expr, what)                                   \
+  do {                                                               \
+    cudaError_t _st = (expr);                                        \
+    if (_st != cudaSuccess) return ::aoakv::cuda_status(_st, what);  \
+  } while (0)
+
+// --------------------------------------------------------------- device side
+// First device error wins; later ones are dropped.
+__device__ __forceinline__ void raise_dev_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+// 16-byte streaming load that bypasses L1 (data read exactly once).
+__device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void u4_to_f8(const uint4& u, float f[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+// Monotone map float -> uint32: a > b  <=>  key(a) > key(b) and -0 == +0
+// (IEEE equality, as torch.topk compares); NaN -> 0, which ranks below
+// -inf (key 0x007fffff).
+__device__ __forceinline__ uint32_t float_to_key(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) return 0u;
+  if (u == 0x80000000u) u = 0u;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float key_to_float(uint32_t k) {
+  uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+// ------------------------------------------------- mbarrier + TMA (sm_90+)
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar,
+                                                      uint32_t bytes) {
+  asm volatile(
+      "mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+          smem_addr(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase. Returns false (and records
+// AOAKV_DEV_ERR_TIMEOUT) if the phase did not complete within ~2^26 polls.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar,
+                                                  uint32_t parity, int* err) {
+  for (uint32_t i = 0; i < (1u << 26); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i > 64) __nanosleep(32);
+  }
+  raise_dev_error(err, AOAKV_DEV_ERR_TIMEOUT);
+  return false;
+}
+
+// 3-D tiled TMA load global -> shared, completion counted on `bar`.
+// Coordinates are element indices (c0 innermost).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map,
+                                            int c0, int c1, int c2,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::"
+      "bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map))
+               : "memory");
+}
+
+// Programmatic dependent launch: wait for the previous kernel in the stream
+// (no-op when launched without the PDL attribute) / allow the next to start.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+}  // namespace aoakv

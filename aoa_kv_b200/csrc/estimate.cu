@@ -1,0 +1,112 @@
+// a3 stand-alone entry point: aoakv_estimate_attn_score.
+#include <cmath>
+
+#include "estimate.cuh"
+#include "plan.h"
+
+namespace aoakv {
+namespace {
+
+template <int D>
+__global__ void __launch_bounds__(kEstThreads) estimate_kernel(EstimateArgs a) {
+  extern __shared__ float q_s[];
+  stage_q<D>(a.q, q_s, a.H);
+  __syncthreads();
+  constexpr int RPS = kEstThreads / (D / 8);
+  const int64_t n_rows = static_cast<int64_t>(a.n_score) * a.H;
+  estimate_rows<D>(a, q_s, static_cast<int64_t>(blockIdx.x) * RPS * kEstUnroll,
+                   static_cast<int64_t>(gridDim.x) * RPS * kEstUnroll, n_rows);
+}
+
+}  // namespace
+
+// Grid for a sweep over n_rows (page, head) rows: enough CTAs that each does
+// about one unrolled sweep, capped at 8 resident CTAs per SM.
+int estimate_grid(int64_t n_rows, int D) {
+  const int64_t rows_per_cta = static_cast<int64_t>(kEstThreads / (D / 8)) * kEstUnroll;
+  int64_t g = (n_rows + rows_per_cta - 1) / rows_per_cta;
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+int launch_estimate(const EstimateArgs& a, int D, cudaStream_t s) {
+  const int64_t n_rows = static_cast<int64_t>(a.n_score) * a.H;
+  if (n_rows == 0) return AOAKV_OK;
+  const size_t smem = static_cast<size_t>(a.H) * D * sizeof(float);
+  const int grid = estimate_grid(n_rows, D);
+  if (D == 128) {
+    if (smem > 48 * 1024)
+      AOAKV_CUDA_TRY(cudaFuncSetAttribute(estimate_kernel<128>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(smem)),
+                     "estimate smem attribute");
+    estimate_kernel<128><<<grid, kEstThreads, smem, s>>>(a);
+  } else {
+    if (smem > 48 * 1024)
+      AOAKV_CUDA_TRY(cudaFuncSetAttribute(estimate_kernel<64>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(smem)),
+                     "estimate smem attribute");
+    estimate_kernel<64><<<grid, kEstThreads, smem, s>>>(a);
+  }
+  AOAKV_CUDA_TRY(cudaGetLastError(), "estimate launch");
+  return AOAKV_OK;
+}
+
+}  // namespace aoakv
+
+using namespace aoakv;
+
+extern "C" int aoakv_estimate_attn_score(
+    const void* q, void* out, int32_t out_dtype, int64_t out_row_stride,
+    const void* metadata_data, const int32_t* metadata_indices,
+    int32_t num_metadata_pages, int32_t metadata_last_page_len,
+    int32_t metadata_capacity_pages, const int32_t* kv_indices,
+    int32_t kv_capacity_pages, const void* v_log_norm, int32_t num_heads,
+    int32_t head_dim, int32_t page_size, int32_t layout, int32_t score_mode,
+    void* stream) {
+  AOAKV_CHECK_ARG(q && out && metadata_data && metadata_indices,
+                  "estimate: NULL pointer argument");
+  if (layout != AOAKV_LAYOUT_NHD)
+    return set_error(AOAKV_ERR_UNSUPPORTED, "estimate: only the NHD layout is built");
+  AOAKV_CHECK_ARG(head_dim == 64 || head_dim == 128, "estimate: head_dim must be 64 or 128");
+  AOAKV_CHECK_ARG(num_heads >= 1 && num_heads * head_dim * 4 <= 200 * 1024,
+                  "estimate: num_heads out of range");
+  AOAKV_CHECK_ARG(page_size >= 1 && page_size <= 1024, "estimate: page_size out of range");
+  AOAKV_CHECK_ARG(num_metadata_pages >= 1, "estimate: num_metadata_pages must be >= 1");
+  AOAKV_CHECK_ARG(metadata_last_page_len >= 1 && metadata_last_page_len <= page_size,
+                  "estimate: metadata_last_page_len must be in [1, page_size]");
+  AOAKV_CHECK_ARG(metadata_capacity_pages >= num_metadata_pages,
+                  "estimate: metadata capacity below num_metadata_pages");
+  AOAKV_CHECK_ARG(out_dtype == AOAKV_DTYPE_F16 || out_dtype == AOAKV_DTYPE_F32,
+                  "estimate: out_dtype must be F16 or F32");
+  AOAKV_CHECK_ARG(score_mode == AOAKV_SCORE_QUEST || score_mode == AOAKV_SCORE_AOAKV,
+                  "estimate: score_mode must be QUEST or AOAKV");
+  const int64_t n_kv = static_cast<int64_t>(num_metadata_pages - 1) * page_size +
+                       metadata_last_page_len;
+  AOAKV_CHECK_ARG(out_row_stride >= n_kv - 1, "estimate: out_row_stride below N-1");
+  if (score_mode == AOAKV_SCORE_AOAKV) {
+    AOAKV_CHECK_ARG(v_log_norm != nullptr, "estimate: AOAKV mode needs v_log_norm");
+    AOAKV_CHECK_ARG(kv_capacity_pages >= 1, "estimate: kv_capacity_pages must be >= 1");
+  }
+  EstimateArgs a;
+  a.q = static_cast<const __half*>(q);
+  a.meta = static_cast<const __half*>(metadata_data);
+  a.meta_indices = metadata_indices;
+  a.kv_indices = kv_indices;
+  a.vlog = static_cast<const __half*>(v_log_norm);
+  a.out = out;
+  a.out_stride = out_row_stride;
+  a.out_f32 = out_dtype == AOAKV_DTYPE_F32;
+  a.n_score = static_cast<int>(n_kv - 1);
+  a.H = num_heads;
+  a.P = page_size;
+  a.meta_cap = metadata_capacity_pages;
+  a.kv_cap = kv_capacity_pages;
+  a.mode = score_mode;
+  a.two_rsqrt_d = 2.f / std::sqrt(static_cast<float>(head_dim));
+  a.err = dev_error_ptr();
+  return launch_estimate(a, head_dim, static_cast<cudaStream_t>(stream));
+}

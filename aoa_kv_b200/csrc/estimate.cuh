@@ -1,0 +1,119 @@
+// a3 page scorer, shared by the stand-alone estimate entry point and the
+// per-layer step.
+//
+// Reference: kernels/aoa_kv/kernels/include/decode/decode_attn.cuh:143-199
+// (compute_max_possible: s = sum_i max(q_i*kmax_i, q_i*kmin_i), AOA score
+// 2*s*rsqrt(d) + 2*v_log_norm, :193) and :263-443 (the kernel that streams
+// the metadata cache, excluding the last page via last_page_len-1, :297-306);
+// filtering/filter_util.py:968-1018 and :314-367 state the same quantity.
+//
+// Design: the metadata of one KV page for all heads is H*D fp16 contiguous
+// (max slot) plus the same at +P*H*D (min slot), so a flat sweep over
+// (page, head) rows reads HBM strictly sequentially. D/8 lanes own one row
+// with one 16-byte streaming load per slot; U rows per thread are loaded
+// before any arithmetic so every SM keeps ~100 KB in flight; a lane-group
+// xor-shuffle finishes each dot product. Scores are fp32 internally.
+#pragma once
+
+#include "common.cuh"
+
+namespace aoakv {
+
+struct EstimateArgs {
+  const __half* q;            // [H, D]
+  const __half* meta;         // [meta_cap, 2, P, H, D]
+  const int32_t* meta_indices;
+  const int32_t* kv_indices;  // physical KV page of logical page p (AOA mode)
+  const __half* vlog;         // [kv_cap, H]
+  void* out;                  // out[h * out_stride + p]
+  int64_t out_stride;
+  int out_f32;
+  int n_score;                // pages scored: N - 1
+  int H, P;
+  int meta_cap, kv_cap;
+  int mode;                   // AOAKV_SCORE_*
+  float two_rsqrt_d;
+  int* err;
+};
+
+constexpr int kEstThreads = 256;
+constexpr int kEstUnroll = 4;
+
+template <int D>
+__device__ __forceinline__ void estimate_rows(const EstimateArgs& a,
+                                              const float* q_s, int64_t row0,
+                                              int64_t row_step, int64_t n_rows) {
+  constexpr int L = D / 8;
+  constexpr int RPS = kEstThreads / L;  // rows per sweep of the CTA
+  const int lane = threadIdx.x % L;
+  const int sub = threadIdx.x / L;
+  const size_t HD = static_cast<size_t>(a.H) * D;
+  const size_t slot = static_cast<size_t>(a.P) * HD;  // max slot -> min slot
+  for (int64_t base = row0; base < n_rows; base += row_step) {
+    uint4 mx[kEstUnroll], mn[kEstUnroll];
+    int hh[kEstUnroll], pp[kEstUnroll];
+    bool ok[kEstUnroll];
+#pragma unroll
+    for (int u = 0; u < kEstUnroll; ++u) {
+      const int64_t r = base + static_cast<int64_t>(u) * RPS + sub;
+      ok[u] = r < n_rows;
+      const int p = ok[u] ? static_cast<int>(r / a.H) : 0;
+      const int h = ok[u] ? static_cast<int>(r % a.H) : 0;
+      pp[u] = p;
+      hh[u] = h;
+      int mpid = ok[u] ? __ldg(a.meta_indices + p / a.P) : 0;
+      if (ok[u] && (mpid < 0 || mpid >= a.meta_cap)) {
+        raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
+        ok[u] = false;
+      }
+      if (ok[u]) {
+        const __half* row = a.meta + (static_cast<size_t>(mpid) * 2 * a.P + p % a.P) * HD +
+                            static_cast<size_t>(h) * D + lane * 8;
+        mx[u] = ld_stream_u4(row);
+        mn[u] = ld_stream_u4(row + slot);
+      } else {
+        mx[u] = make_uint4(0, 0, 0, 0);
+        mn[u] = make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kEstUnroll; ++u) {
+      float fa[8], fb[8];
+      u4_to_f8(mx[u], fa);
+      u4_to_f8(mn[u], fb);
+      const float4 q0 = *reinterpret_cast<const float4*>(q_s + hh[u] * D + lane * 8);
+      const float4 q1 = *reinterpret_cast<const float4*>(q_s + hh[u] * D + lane * 8 + 4);
+      const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += fmaxf(qv[i] * fa[i], qv[i] * fb[i]);
+#pragma unroll
+      for (int off = L / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+      if (ok[u] && lane == 0) {
+        float score = s;
+        if (a.mode == AOAKV_SCORE_AOAKV) {
+          const int pid = a.kv_indices ? __ldg(a.kv_indices + pp[u]) : pp[u];
+          float vl = 0.f;
+          if (pid < 0 || pid >= a.kv_cap)
+            raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
+          else
+            vl = __half2float(a.vlog[static_cast<size_t>(pid) * a.H + hh[u]]);
+          score = a.two_rsqrt_d * s + 2.f * vl;
+        }
+        const size_t o = static_cast<size_t>(hh[u]) * a.out_stride + pp[u];
+        if (a.out_f32)
+          static_cast<float*>(a.out)[o] = score;
+        else
+          static_cast<__half*>(a.out)[o] = __float2half_rn(score);
+      }
+    }
+  }
+}
+
+// Stages q (fp16 [H, D]) into shared memory as fp32.
+template <int D>
+__device__ __forceinline__ void stage_q(const __half* q, float* q_s, int H) {
+  for (int i = threadIdx.x; i < H * D; i += blockDim.x) q_s[i] = __half2float(q[i]);
+}
+
+}  // namespace aoakv

@@ -1,0 +1,454 @@
+#!/usr/bin/env python
+"""Headline benchmark: sparse-decode µs/layer @ 32K context, 1K budget.
+
+Workload (BASELINE config "32K ctx, B=1024" with config 2's inputs): one
+request, 32 heads MHA, head_dim 128, fp16 paged KV with page_size 16, context
+32768 tokens (N = 2048 pages), budget 1024 tokens (64 pages: 63 selected +
+the last page), AOA-KV value-aware scoring; K ~ N(0,1) * LogNormal(0,1)
+per-channel scale, q, V ~ N(0,1), seed 1; synthetic data.
+
+A "step" is one decode token through L = 32 layers (each layer has its own
+KV cache, metadata and v_log_norm): per layer the library appends the token
+and runs estimate -> top-k -> sparse decode. The 32 layers touch
+32 x 50.5 MB > L2 (126 MB) per step, so no layer finds its data in L2.
+
+  value     device time per layer-step, whole job: max-over-ranks time of K
+            CUDA-graph replays of the 32-layer step / (K * 32 * n_gpus)
+  e2e       the same through InferenceController.decode_step with q, k, v
+            copied from pinned host memory and o copied back every layer
+  roofline  the dominant kernel (page-score estimate) timed alone with CUDA
+            events: algorithmic bytes per launch / average launch time
+
+With --gpus N (torchrun, one process per GPU) every rank serves its own
+request (request sharding, no collective): scaling "weak".
+--impl reference times the reference's CPU simulation path (the numpy port
+in oracle/sim.py of filter_util.py + quest_attention.py) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "sparse-decode µs/layer @32K ctx, 1K budget; % of B200 HBM roofline"
+H, D, P = 32, 128, 16
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--ctx", type=int, default=32768)
+    ap.add_argument("--budget", type=int, default=1024, help="token budget")
+    ap.add_argument("--method", choices=["aoakv", "quest"], default="aoakv")
+    ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="CPU-baseline sample budget (rank 0, N=1)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def workload_config(a, n_gpus):
+    n_pages = (a.ctx + P - 1) // P
+    return {
+        "workload": f"1 request/GPU, {a.layers}-layer decode step, ctx {a.ctx}, budget {a.budget}",
+        "context_tokens": a.ctx, "token_budget": a.budget, "page_size": P, "num_heads": H,
+        "head_dim": D, "layers_per_step": a.layers, "score_mode": a.method, "sink_first_page": False,
+        "pages_scored": n_pages - 1, "pages_attended": min(a.budget // P, n_pages),
+        "inputs": "K~N(0,1)*LogNormal(0,1)[h,d], q,V~N(0,1), seed %d" % a.seed,
+        "l2": "inputs larger than L2: %d layers x %.1f MB touched per step" % (
+            a.layers, step_bytes(a) / 1e6),
+        "accumulate": "fp32", "parallelism": f"request-sharded x{n_gpus}, no collective",
+    }
+
+
+def step_bytes(a) -> int:
+    """Algorithmic bytes of one layer-step: metadata of the
+    N-1 scored pages, their v_log_norm (aoakv), the k attended pages' K and V,
+    and q + o."""
+    n = (a.ctx + P - 1) // P
+    k = min(a.budget // P, n)
+    b = (n - 1) * H * 2 * D * 2 + k * P * H * D * 2 * 2 + 2 * H * D * 2
+    if a.method == "aoakv":
+        b += (n - 1) * H * 2
+    return b
+
+
+def estimate_bytes(a) -> int:
+    """Algorithmic bytes of one estimate launch: metadata + v_log_norm of the
+    N-1 scored pages, q, and the fp32 scores written."""
+    n = (a.ctx + P - 1) // P
+    b = (n - 1) * H * 2 * D * 2 + H * D * 2 + (n - 1) * H * 4
+    if a.method == "aoakv":
+        b += (n - 1) * H * 2
+    return b
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples (100 ms) of the benchmark's GPU while it runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.samples = []
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", gpu_id], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+        except (OSError, ValueError):
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append((time.monotonic(), parts))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0, t1):
+        rows = [p for t, p in self.samples if t0 <= t <= t1] or [p for _, p in self.samples]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def gpu_query_id(dev_index: int) -> str:
+    import torch
+    try:
+        p = torch.cuda.get_device_properties(dev_index)
+        return "%08X:%02X:%02X.0" % (p.pci_domain_id, p.pci_bus_id, p.pci_device_id)
+    except Exception:  # noqa: BLE001 - fall back to the ordinal
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        return vis.split(",")[dev_index] if vis else str(dev_index)
+
+
+# ------------------------------------------------------------- CPU baseline
+def cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return int(max(n))
+    except Exception:  # noqa: BLE001
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_sim_setup(a):
+    import numpy as np
+    from oracle import sim
+    g = np.random.default_rng(a.seed)
+    S = a.ctx
+    q = g.standard_normal((H, D), dtype=np.float32).astype(np.float16).astype(np.float32)
+    scale = np.exp(g.standard_normal((H, D), dtype=np.float32))
+    K = (g.standard_normal((H, S, D), dtype=np.float32) * scale[:, None]).astype(np.float16)
+    V = g.standard_normal((H, S, D), dtype=np.float32).astype(np.float16)
+    st = sim.SimLayerState(K[:, :-1].astype(np.float32), V[:, :-1].astype(np.float32), P)
+    return st, q, K[:, -1].astype(np.float32), V[:, -1].astype(np.float32)
+
+
+def cpu_sim_steps(a, n_steps, budget_s=None):
+    """Times the reference simulation's decode step for one layer (one unit of
+    the metric) on the host cores; returns per-step seconds."""
+    import copy
+
+    from oracle import sim
+    st0, q, k, v = cpu_sim_setup(a)
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(n_steps):
+        st = copy.copy(st0)  # decode_step rebinds arrays; the prefill state is reused
+        t0 = time.perf_counter()
+        sim.decode_step(st, q, k, v, a.budget, a.method, True, expand=True)
+        times.append(time.perf_counter() - t0)
+        if budget_s and time.perf_counter() - t_start > budget_s:
+            break
+    return times
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    n_gpus = int(os.environ.get("WORLD_SIZE", str(a.gpus)))
+    if rank != 0:
+        return
+    for _ in range(max(0, min(a.warmup, 3))):
+        cpu_sim_steps(a, 1)
+    times = cpu_sim_steps(a, a.steps)
+    us = statistics.median(times) * 1e6
+    cores = cpu_threads()
+    line = {
+        "metric": METRIC, "value": round(us, 3), "unit": "us", "impl": "reference",
+        "n_gpus": n_gpus, "steps": len(times), "warmup": a.warmup, "ms_per_step": round(us / 1e3, 3),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload_config(a, n_gpus),
+        "cpu_baseline": {"value": round(us, 3), "unit": "us", "cores": cores, "kind": "port",
+                         "sample": f"{len(times)} single-layer decode steps of the simulation "
+                                   f"(oracle/sim.py restating filter_util.py + quest_attention.py), "
+                                   f"ctx {a.ctx}, budget {a.budget}, {a.method}, fixed=True, median"},
+        "e2e": {"value": round(us, 3), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- our arm
+def setup_layers(a, dev):
+    import torch
+
+    import aoa_kv_b200 as ak
+    gen = torch.Generator(device=dev).manual_seed(a.seed)
+    ctl = ak.InferenceController(a.layers, H, D, P, a.budget // P, a.ctx + P, torch.float16, dev,
+                                 method=a.method)
+    S = a.ctx
+    ctl.prepare_metadata(S - 1)
+    ctl.begin_forward(S - 1)
+    news = []
+    for layer in range(a.layers):
+        scale = torch.exp(torch.randn(H, D, device=dev, generator=gen))
+        K = (torch.randn(S, H, D, device=dev, generator=gen) * scale).half()
+        V = torch.randn(S, H, D, device=dev, generator=gen).half()
+        q = torch.randn(1, H, D, device=dev, generator=gen).half()
+        ak.append_kv(K[:-1].contiguous(), V[:-1].contiguous(), ctl, layer)
+        news.append((q, K[-1:].contiguous(), V[-1:].contiguous()))
+        del K, V
+    ctl.end_forward()
+    ctl.prepare_metadata(1)
+    ctl.begin_forward(1)
+    torch.cuda.synchronize()
+    return ctl, news
+
+
+def run_ours(a):
+    import torch
+    import torch.distributed as dist
+
+    import aoa_kv_b200 as ak
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    ak._lib.load()
+
+    ctl, news = setup_layers(a, dev)
+    outs = [torch.empty(1, H, D, dtype=torch.float16, device=dev) for _ in range(a.layers)]
+
+    def one_step():
+        for layer, (q, k, v) in enumerate(news):
+            ctl.decode_step(q, k, v, layer, out=outs[layer])
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        one_step()  # first calls set kernel attributes outside capture
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        one_step()
+    torch.cuda.synchronize()
+    ak.check_device()
+
+    sampler = ClockSampler(gpu_query_id(local)) if rank == 0 else None
+    t_soak = time.monotonic()
+    for _ in range(a.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    # keep the GPU busy ~1 s so the clock sampler sees it under this load
+    t_end = time.monotonic() + 1.0
+    while time.monotonic() < t_end:
+        for _ in range(20):
+            graph.replay()
+        torch.cuda.synchronize()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0.record()
+    for _ in range(a.steps):
+        graph.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_timed_end = time.monotonic()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ak.check_device()
+    us_layer_job = ms * 1e3 / (a.steps * a.layers * world)
+    us_layer_gpu = ms * 1e3 / (a.steps * a.layers)
+
+    # --- dominant kernel alone: the page-score estimate (fp32 scores)
+    n = (a.ctx + P - 1) // P
+    scores = torch.empty(H, n, dtype=torch.float32, device=dev)
+
+    def est_all():
+        for layer, (q, _, _) in enumerate(news):
+            meta = ctl.metadata_cache.buf_layer(layer)
+            ak._lib.call("aoakv_estimate_attn_score", q.data_ptr(), scores.data_ptr(), 1, n,
+                         meta.data_ptr(), ctl.metadata_indices.data_ptr(),
+                         len(ctl.metadata_cache.indicies), ctl.metadata_cache.last_page_len,
+                         meta.shape[0], ctl.kv_indices_with_last.data_ptr(),
+                         ctl.kv_cache.pool.capacity, ctl.v_log_norm_layer(layer).data_ptr(), H, D,
+                         P, 0, ctl.score_mode, torch.cuda.current_stream().cuda_stream)
+    with torch.cuda.stream(s):
+        est_all()
+    torch.cuda.synchronize()
+    g_est = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_est):
+        est_all()
+    for _ in range(3):
+        g_est.replay()
+    reps = max(5, a.steps // 2)
+    torch.cuda.synchronize()
+    ev0.record()
+    for _ in range(reps):
+        g_est.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    est_us = ev0.elapsed_time(ev1) * 1e3 / (reps * a.layers)
+
+    # --- e2e through the public API with host buffers
+    e2e = None
+    if not a.no_e2e:
+        pin = [(t[0].cpu().pin_memory(), t[1].cpu().pin_memory(), t[2].cpu().pin_memory())
+               for t in news]
+        host_o = torch.empty(a.layers, 1, H, D, dtype=torch.float16).pin_memory()
+        dq = [(torch.empty_like(t[0]), torch.empty_like(t[1]), torch.empty_like(t[2])) for t in news]
+
+        def e2e_step():
+            for layer in range(a.layers):
+                qd, kd, vd = dq[layer]
+                qh, kh, vh = pin[layer]
+                qd.copy_(qh, non_blocking=True)
+                kd.copy_(kh, non_blocking=True)
+                vd.copy_(vh, non_blocking=True)
+                o = ctl.decode_step(qd, kd, vd, layer, out=outs[layer])
+                host_o[layer].copy_(o, non_blocking=True)
+        for _ in range(a.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ev0.record()
+        for _ in range(a.steps):
+            e2e_step()
+        ev1.record()
+        torch.cuda.synchronize()
+        ems = ev0.elapsed_time(ev1)
+        if world > 1:
+            t = torch.tensor([ems], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        e2e = {"value": round(ems * 1e3 / (a.steps * a.layers * world), 3), "unit": "us",
+               "h2d_bytes_per_step": a.layers * 3 * H * D * 2,
+               "d2h_bytes_per_step": a.layers * H * D * 2,
+               "api": "InferenceController.decode_step (ctypes -> aoakv_decode_step), no graph"}
+
+    if sampler:
+        sampler.stop()
+    clocks = sampler.summary(t_soak, t_timed_end) if sampler else None
+
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    peak = float(peaks.get("hbm_gbs") or 6650.0)
+    peak_src = "measured" if peaks.get("hbm_gbs") else "fallback"
+    eb = estimate_bytes(a)
+    ach = eb / (est_us * 1e-6) / 1e9
+    sb = step_bytes(a)
+    step_ach = sb / (us_layer_gpu * 1e-6) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        times = cpu_sim_steps(a, 50, budget_s=a.cpu_seconds)
+        cpu_us = statistics.median(times) * 1e6
+        cpu = {"value": round(cpu_us, 1), "unit": "us", "cores": cpu_threads(), "kind": "port",
+               "sample": f"{len(times)} single-layer decode steps of the reference simulation "
+                         f"(oracle/sim.py: filter_util.py + quest_attention.py decode branch) at "
+                         f"ctx {a.ctx}, budget {a.budget}, {a.method}, fixed=True; median"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(us_layer_job, 3), "unit": "us", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic", "config": workload_config(a, world),
+            "per_gpu_us_per_layer": round(us_layer_gpu, 3),
+            "roofline": {"bound": "hbm", "kernel": "estimate (page scorer)",
+                         "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(ach / peak, 4), "traffic": None,
+                         "algorithmic_bytes": eb, "avg_launch_us": round(est_us, 3),
+                         "peak_source": peak_src},
+            "step_roofline": {"bytes_per_layer_step": sb, "achieved": round(step_ach, 1),
+                              "unit": "GB/s", "frac": round(step_ach / peak, 4),
+                              "ideal_us": round(sb / (peak * 1e9) * 1e6, 3)},
+            "e2e": e2e, "gpu_launches": 4 * a.layers * a.steps, "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    del graph, g_est
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

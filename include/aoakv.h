@@ -1,0 +1,214 @@
+/*
+ * aoakv.h — C ABI of libaoakv.so, the B200 (sm_100a) sparse-decode path of
+ * AOA-KV / Quest: page-metadata append, page-score estimate, top-k page
+ * filter and split-KV sparse paged decode.
+ *
+ * Conventions shared by every entry point
+ *   - Pointers are device pointers unless stated otherwise. No torch types.
+ *   - KV data and metadata are fp16 and use the reference's NHD paged layout,
+ *     one layer slice per call:
+ *         kv_data       [kv_capacity_pages, 2, page_size, num_heads, head_dim]
+ *         metadata_data [metadata_capacity_pages, 2, page_size, num_heads, head_dim]
+ *     Entry j of metadata page m describes KV page m*page_size + j; its K slot
+ *     holds the per-channel key maximum, its V slot the per-channel minimum.
+ *         v_log_norm    [kv_capacity_pages, num_heads] fp16,
+ *                       log(||mean_t V[page, t, head, :]||_2 + 1e-6), written
+ *                       when a page becomes full.
+ *   - Page ids are int32 physical page ids; every id is range-checked against
+ *     the capacity argument. A bad id found on the device does not fault: the
+ *     kernel skips it and records AOAKV_DEV_ERR_BAD_PAGE, which
+ *     aoakv_get_device_error() returns.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Work is
+ *     stream-ordered; no entry point synchronises the device or allocates
+ *     device memory. Callers own every buffer, including workspaces.
+ *   - Return value: AOAKV_OK or an AOAKV_ERR_* code; aoakv_last_error()
+ *     returns a message for the calling thread's last failure.
+ *   - head_dim must be 64 or 128; layout must be AOAKV_LAYOUT_NHD.
+ */
+#ifndef AOAKV_H_
+#define AOAKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AOAKV_API __attribute__((visibility("default")))
+#else
+#define AOAKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  AOAKV_OK = 0,
+  AOAKV_ERR_INVALID_ARG = 1,   /* bad shape, size, pointer or flag */
+  AOAKV_ERR_UNSUPPORTED = 2,   /* valid but not built (e.g. HND layout) */
+  AOAKV_ERR_CUDA = 3,          /* a CUDA runtime call failed */
+  AOAKV_ERR_WORKSPACE = 4,     /* workspace missing or too small */
+};
+
+/* Device-side error codes (aoakv_get_device_error). */
+enum {
+  AOAKV_DEV_OK = 0,
+  AOAKV_DEV_ERR_BAD_PAGE = 1,  /* a page id outside [0, capacity) was skipped */
+  AOAKV_DEV_ERR_TIMEOUT = 2,   /* a bounded device-side wait gave up */
+};
+
+enum { AOAKV_DTYPE_F16 = 0, AOAKV_DTYPE_F32 = 1 };
+enum { AOAKV_LAYOUT_NHD = 0, AOAKV_LAYOUT_HND = 1 };
+/* score_mode: QUEST = sum_i max(q_i*kmax_i, q_i*kmin_i);
+ *             AOAKV = 2*QUEST/sqrt(head_dim) + 2*v_log_norm[page, head]. */
+enum { AOAKV_SCORE_QUEST = 0, AOAKV_SCORE_AOAKV = 1 };
+
+/* Message for the calling thread's last non-OK return ("" if none). */
+AOAKV_API const char* aoakv_last_error(void);
+
+/* ABI version (major*10000 + minor*100 + patch). */
+AOAKV_API int aoakv_version(void);
+
+/* Reads (and with clear != 0 resets) the device-side error word of the
+ * current device. Synchronises the current device. */
+AOAKV_API int aoakv_get_device_error(int32_t* code_out, int32_t clear);
+
+/* a1 — replaces append_kv_cache_decode
+ *   (kernels/aoa_kv/quest/ops/csrc/bsk_ops.h:71-86, page.cu:6-105,
+ *    kernel decode_page.cuh:392-506).
+ * Appends one token k,v [1, num_heads, head_dim] at position
+ * (num_kv_pages-1)*page_size + kv_last_page_len - 1, i.e. after the caller
+ * has reserved the slot. Updates the last page's running key max/min
+ * (initialised to -/+65504 when the token opens a page) and, when the token
+ * fills the page, writes v_log_norm[kv_indices[num_kv_pages-1], :].
+ * metadata_last_page_len must equal ((num_kv_pages-1) % page_size) + 1 and
+ * num_metadata_pages must equal ceil(num_kv_pages / page_size). */
+AOAKV_API int aoakv_append_kv_cache_decode(
+    const void* k, const void* v,
+    void* kv_data, const int32_t* kv_indices, int32_t num_kv_pages,
+    int32_t kv_last_page_len, int32_t kv_capacity_pages,
+    void* metadata_data, const int32_t* metadata_indices,
+    int32_t num_metadata_pages, int32_t metadata_last_page_len,
+    int32_t metadata_capacity_pages,
+    void* v_log_norm,
+    int32_t num_heads, int32_t head_dim, int32_t page_size, int32_t layout,
+    void* stream);
+
+/* a2 — replaces append_kv_cache_prefill
+ *   (bsk_ops.h:55-69, page.cu:107-222, kernel decode_page.cuh:522-692).
+ * Appends seq_len tokens k,v [seq_len, num_heads, head_dim]; they occupy the
+ * last seq_len positions of the sequence described by the page table.
+ * Every page the tokens touch gets its key max/min merged; every page that
+ * ends up full gets its v_log_norm. */
+AOAKV_API int aoakv_append_kv_cache_prefill(
+    const void* k, const void* v, int32_t seq_len,
+    void* kv_data, const int32_t* kv_indices, int32_t num_kv_pages,
+    int32_t kv_last_page_len, int32_t kv_capacity_pages,
+    void* metadata_data, const int32_t* metadata_indices,
+    int32_t num_metadata_pages, int32_t metadata_last_page_len,
+    int32_t metadata_capacity_pages,
+    void* v_log_norm,
+    int32_t num_heads, int32_t head_dim, int32_t page_size, int32_t layout,
+    void* stream);
+
+/* a3 — replaces estimate_attn_score
+ *   (bsk_ops.h:43-53, estimate.cu:6-90, kernel decode_attn.cuh:263-443 with
+ *    compute_max_possible :143-199).
+ * Scores the N-1 complete pages (N = (num_metadata_pages-1)*page_size +
+ * metadata_last_page_len; the last KV page is excluded) for every head:
+ *   out[h * out_row_stride + p], p in [0, N-1), dtype out_dtype.
+ * AOAKV mode reads v_log_norm[kv_indices[p], h] (the page's own norm; the
+ * reference reads the norm of page kv_indices-of-metadata-page p/page_size,
+ * decode_attn.cuh:185-190, which this library does not reproduce).
+ * kv_indices NULL means physical page id == logical page id (a fresh
+ * reference KvPool allocates pages in that order); QUEST mode ignores it. */
+AOAKV_API int aoakv_estimate_attn_score(
+    const void* q, void* out, int32_t out_dtype, int64_t out_row_stride,
+    const void* metadata_data, const int32_t* metadata_indices,
+    int32_t num_metadata_pages, int32_t metadata_last_page_len,
+    int32_t metadata_capacity_pages,
+    const int32_t* kv_indices, int32_t kv_capacity_pages,
+    const void* v_log_norm,
+    int32_t num_heads, int32_t head_dim, int32_t page_size, int32_t layout,
+    int32_t score_mode, void* stream);
+
+/* a4 — replaces topk_filtering
+ *   (bsk_ops.h:35-41, topk.cu:7-46, decode_select_k.cuh:25-61 which runs
+ *    RAFT radix_topk_one_block_kernel).
+ * For each of num_rows rows selects the k largest of num_pages scores
+ * (scores_dtype f16 or f32). Ties break toward the lower position; NaN
+ * ranks below every number. With sink_first_page != 0 position 0 is always
+ * selected (the simulation's fixed sink page) and the other k-1 come from
+ * positions 1..num_pages-1. Results are written in ascending position order:
+ *   out_indices[r*out_indices_row_stride + i] = in_indices[r*in_row_stride + pos]
+ *   (pos itself when in_indices is NULL; in_row_stride may be 0 to share
+ *    one index row), out_values likewise (may be NULL; same dtype as
+ *    scores). Requires 1 <= k <= num_pages <= 49152. No scratch buffer. */
+AOAKV_API int aoakv_topk_filtering(
+    const void* scores, int32_t scores_dtype, int64_t scores_row_stride,
+    const int32_t* in_indices, int64_t in_indices_row_stride,
+    int32_t num_rows, int32_t num_pages, int32_t k,
+    void* out_values, int64_t out_values_row_stride,
+    int32_t* out_indices, int64_t out_indices_row_stride,
+    int32_t sink_first_page, void* stream);
+
+/* a5 — workspace for aoakv_sparse_decode (replaces the temporary buffers of
+ * BatchDecodeHandler::BeginForward, decode_handler.cuh:73-121). The caller
+ * allocates it once, zero-fills it once, and may reuse it for every call on
+ * one stream; calls keep it zeroed. */
+AOAKV_API int aoakv_decode_workspace_size(int32_t num_heads, int32_t head_dim,
+                                int32_t max_pages_per_head, size_t* bytes);
+
+/* a5 — replaces BatchDecodeWithPagedKVCachePyTorchWrapper::Forward
+ *   (bsk_ops.h:96-125, approx_attn.cu:69-151, kernels decode_attn.cuh:469-688
+ *    and :937-1047 plus FlashInfer VariableLengthMergeStates).
+ * o[h] = softmax(q[h].K^T * sm_scale) V over head h's num_selected pages
+ * indices[h*indices_row_stride + i] (stride 0 shares one row) plus the last
+ * page last_page_idx holding last_page_len tokens. q, o: [num_heads,
+ * head_dim] fp16. sm_scale <= 0 means 1/sqrt(head_dim). Pages are gathered
+ * with TMA; partial softmax states of page chunks merge by log-sum-exp
+ * inside the same kernel. */
+AOAKV_API int aoakv_sparse_decode(
+    const void* q, void* o,
+    const void* kv_data, int32_t kv_capacity_pages,
+    const int32_t* indices, int64_t indices_row_stride, int32_t num_selected,
+    int32_t last_page_idx, int32_t last_page_len,
+    int32_t num_heads, int32_t head_dim, int32_t page_size, int32_t layout,
+    float sm_scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Whole per-layer decode step for one request: a1 append of (k_new, v_new),
+ * a3 estimate, a4 top-k and a5 sparse decode, as the reference's
+ * QuestAttention.forward decode branch issues them
+ * (kernels/aoa_kv/quest/models/QuestAttention.py:99-157).
+ * num_kv_pages / kv_last_page_len describe the sequence INCLUDING the new
+ * token. page_budget counts pages including the always-attended last page:
+ *   sink_first_page == 0 (kernel-tree rule, controller.py:124, utils:237):
+ *       k = min(page_budget, N); top-(k-1) of pages 0..N-2, plus page N-1.
+ *   sink_first_page != 0 (simulation rule, filter_util.py:226-231,373-377):
+ *       k = min(max(3, page_budget), N); page 0, top-(k-2) of 1..N-2, N-1.
+ *   If N <= k every page is attended and no scoring runs.
+ * selected_out (optional, [num_heads, B] with B = page_budget, or
+ * max(3, page_budget) with the sink) receives the attended page ids per head
+ * in slot order (last page after the selected ones); unused slots are -1.
+ * The workspace is sized by aoakv_step_workspace_size, zero-filled once by
+ * the caller, and kept zeroed by every call. */
+AOAKV_API int aoakv_step_workspace_size(int32_t num_heads, int32_t head_dim,
+                              int32_t max_pages, int32_t max_page_budget,
+                              size_t* bytes);
+
+AOAKV_API int aoakv_decode_step(
+    const void* q, const void* k_new, const void* v_new, void* o,
+    void* kv_data, const int32_t* kv_indices, int32_t num_kv_pages,
+    int32_t kv_last_page_len, int32_t kv_capacity_pages,
+    void* metadata_data, const int32_t* metadata_indices,
+    int32_t metadata_capacity_pages,
+    void* v_log_norm,
+    int32_t num_heads, int32_t head_dim, int32_t page_size,
+    int32_t page_budget, int32_t score_mode, int32_t sink_first_page,
+    int32_t* selected_out, void* workspace, size_t workspace_bytes,
+    void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* AOAKV_H_ */

@@ -1,0 +1,187 @@
+"""GPU parity of each kernel against the CPU oracle (semantics B), through the
+C ABI. Bit-exact where the work is exact (KV copies, key max/min, top-k
+selection on identical scores); fp tolerances stated per test."""
+import numpy as np
+import pytest
+import torch
+
+from aoa_kv_b200 import _lib
+from gen import gen_qkv
+from gpu_util import GpuLayer, ptr, stream
+from oracle import kernel_tree as kt
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+# ----------------------------------------------------------------- a1 / a2
+@pytest.mark.parametrize("D", [128, 64])
+@pytest.mark.parametrize("S0", [0, 5, 15, 16, 37, 300])
+def test_append_prefill_matches_oracle(cuda, D, S0):
+    """Prefill of 45 tokens after S0 existing ones (ragged starts and ends)."""
+    H, P, cap = 8, 16, 64
+    lay = GpuLayer(cap, H, D, P, seed=S0 + D)
+    q, K, V = gen_qkv(100 + S0, H, S0 + 45, D, "outlier")
+    if S0:
+        lay.fill(K[:S0], V[:S0])
+    ref = lay.snapshot()
+    S = S0 + 45
+    n, last = (S + P - 1) // P, (S - 1) % P + 1
+    lay.append_prefill(_dev(K[S0:]), _dev(V[S0:]), n, last)
+    kt.append_prefill(ref, lay.kv_idx_np, lay.meta_idx_np, n, last, K[S0:], V[S0:])
+    torch.cuda.synchronize()
+    got = lay.snapshot()
+    assert np.array_equal(got.kv, ref.kv)
+    assert np.array_equal(got.meta, ref.meta)
+    np.testing.assert_allclose(got.vlog.astype(np.float32), ref.vlog.astype(np.float32),
+                               rtol=0, atol=2e-3)
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("entry", [0, 1, 7, 14, 15])
+def test_append_decode_matches_oracle(cuda, entry):
+    """One decode token landing at page entry `entry` (0 opens a page, 15 fills it)."""
+    H, D, P, cap = 32, 128, 16, 64
+    lay = GpuLayer(cap, H, D, P, seed=entry)
+    S = 5 * P + entry + 1
+    q, K, V = gen_qkv(200 + entry, H, S, D)
+    lay.fill(K[:-1], V[:-1])
+    ref = lay.snapshot()
+    n, last = (S + P - 1) // P, (S - 1) % P + 1
+    lay.append_decode(_dev(K[-1]), _dev(V[-1]), n, last)
+    kt.append_decode(ref, lay.kv_idx_np, lay.meta_idx_np, n, last, K[-1], V[-1])
+    torch.cuda.synchronize()
+    got = lay.snapshot()
+    assert np.array_equal(got.kv, ref.kv)
+    assert np.array_equal(got.meta, ref.meta)
+    np.testing.assert_allclose(got.vlog.astype(np.float32), ref.vlog.astype(np.float32),
+                               rtol=0, atol=2e-3)
+
+
+# ----------------------------------------------------------------------- a3
+@pytest.mark.parametrize("mode", ["quest", "aoakv"])
+@pytest.mark.parametrize("S", [17, 33, 300, 8192 + 5])
+@pytest.mark.parametrize("out_f32", [True, False])
+def test_estimate_matches_oracle(cuda, mode, S, out_f32):
+    H, D, P = 32, 128, 16
+    n = (S + P - 1) // P
+    lay = GpuLayer(n + 3, H, D, P, seed=S)
+    q, K, V = gen_qkv(300 + S, H, S, D, "outlier")
+    lay.fill(K, V)
+    torch.cuda.synchronize()
+    ref = lay.snapshot()
+    qd = _dev(q)
+    out = torch.full((H, n - 1), float("nan"), device="cuda",
+                     dtype=torch.float32 if out_f32 else torch.float16)
+    _lib.call("aoakv_estimate_attn_score", ptr(qd), ptr(out), 1 if out_f32 else 0, n - 1,
+              ptr(lay.meta), ptr(lay.meta_idx), (n + P - 1) // P, (n - 1) % P + 1, lay.mcap,
+              ptr(lay.kv_idx), lay.cap, ptr(lay.vlog), H, D, P, 0,
+              _lib.SCORE_AOAKV if mode == "aoakv" else _lib.SCORE_QUEST, stream())
+    want = kt.estimate(q, ref, lay.meta_idx_np, lay.kv_idx_np, n, mode)
+    got = out.float().cpu().numpy()
+    if out_f32:
+        np.testing.assert_allclose(got, want, rtol=2e-5, atol=2e-4)
+    else:  # one fp16 rounding of the fp32 score
+        np.testing.assert_allclose(got, want.astype(np.float16).astype(np.float32),
+                                   rtol=2e-3, atol=2e-3)
+
+
+# ----------------------------------------------------------------------- a4
+@pytest.mark.parametrize("n,k", [(1, 1), (7, 3), (63, 63), (511, 63), (2047, 63), (2047, 1),
+                                 (8191, 255), (49152, 1000), (100, 99)])
+@pytest.mark.parametrize("f32", [True, False])
+@pytest.mark.parametrize("sink", [False, True])
+def test_topk_exact(cuda, n, k, f32, sink):
+    rows = 32
+    g = np.random.default_rng(n * 7 + k)
+    s = g.standard_normal((rows, n), dtype=np.float32) * 10
+    s[:, ::5] = np.round(s[:, ::5])           # ties
+    if n > 10:
+        s[3, 4] = np.nan
+        s[5, :] = 1.0                          # an all-tie row
+    if not f32:
+        s = s.astype(np.float16).astype(np.float32)
+    idx = np.stack([g.permutation(10 * n)[:n] for _ in range(rows)]).astype(np.int32)
+    sd = torch.from_numpy(s).cuda().to(torch.float32 if f32 else torch.float16)
+    idd = torch.from_numpy(idx).cuda()
+    out_i = torch.full((rows, k), -7, dtype=torch.int32, device="cuda")
+    out_v = torch.empty((rows, k), dtype=sd.dtype, device="cuda")
+    _lib.call("aoakv_topk_filtering", ptr(sd), 1 if f32 else 0, n, ptr(idd), n, rows, n, k,
+              ptr(out_v), k, ptr(out_i), k, int(sink), stream())
+    pos = kt.topk_positions(s, k, sink)
+    want_i = np.take_along_axis(idx, pos, axis=1)
+    assert np.array_equal(out_i.cpu().numpy(), want_i)
+    got_v = out_v.float().cpu().numpy()
+    want_v = np.take_along_axis(s, pos, axis=1)
+    assert np.array_equal(np.isnan(got_v), np.isnan(want_v))
+    assert np.array_equal(np.nan_to_num(got_v), np.nan_to_num(want_v))
+
+
+def test_topk_shared_index_row_and_positions(cuda):
+    rows, n, k = 4, 300, 20
+    s = torch.randn(rows, n, device="cuda")
+    shared = torch.arange(1000, 1000 + n, dtype=torch.int32, device="cuda")
+    o1 = torch.empty(rows, k, dtype=torch.int32, device="cuda")
+    o2 = torch.empty(rows, k, dtype=torch.int32, device="cuda")
+    _lib.call("aoakv_topk_filtering", ptr(s), 1, n, ptr(shared), 0, rows, n, k, None, 0, ptr(o1),
+              k, 0, stream())
+    _lib.call("aoakv_topk_filtering", ptr(s), 1, n, None, 0, rows, n, k, None, 0, ptr(o2), k, 0,
+              stream())
+    assert torch.equal(o1 - 1000, o2)
+    pos = kt.topk_positions(s.cpu().numpy(), k)
+    assert np.array_equal(o2.cpu().numpy(), pos)
+
+
+# ----------------------------------------------------------------------- a5
+@pytest.mark.parametrize("D", [128, 64])
+@pytest.mark.parametrize("n_sel", [0, 1, 3, 8, 63, 255])
+@pytest.mark.parametrize("last_len", [1, 7, 16])
+def test_sparse_decode_matches_oracle(cuda, D, n_sel, last_len):
+    H, P, cap = 32, 16, 600
+    lay = GpuLayer(cap, H, D, P, seed=n_sel + last_len)
+    g = np.random.default_rng(n_sel * 31 + last_len)
+    sel = np.stack([g.permutation(cap - 1)[:n_sel] for _ in range(H)]).astype(np.int32)
+    last = cap - 1
+    q = g.standard_normal((H, D), dtype=np.float32).astype(np.float16) * np.float16(3)
+    ref = lay.snapshot()
+    qd, o = _dev(q), torch.empty(H, D, dtype=torch.float16, device="cuda")
+    seld = torch.from_numpy(sel).cuda() if n_sel else None
+    ws_n = _lib.size_query("aoakv_decode_workspace_size", H, D, n_sel)
+    ws = torch.zeros(ws_n, dtype=torch.uint8, device="cuda")
+    for _ in range(2):  # second call reuses the workspace (tickets re-armed)
+        _lib.call("aoakv_sparse_decode", ptr(qd), ptr(o), ptr(lay.kv), cap, ptr(seld), n_sel, n_sel,
+                  last, last_len, H, D, P, 0, 0.0, ptr(ws), ws_n, stream())
+        want = kt.sparse_decode(q, ref, sel, last, last_len)
+        got = o.float().cpu().numpy()
+        assert np.abs(got - want).max() < 2e-3
+    assert _lib.device_error() == 0
+
+
+def test_sparse_decode_shared_row_and_bad_page(cuda):
+    """Stride-0 index row (dense decode over a shared page list), then a page
+    id beyond capacity: skipped and reported, no fault."""
+    H, D, P, cap = 8, 128, 16, 64
+    lay = GpuLayer(cap, H, D, P, seed=3)
+    ref = lay.snapshot()
+    rows = np.arange(40, dtype=np.int32)
+    q = np.random.default_rng(1).standard_normal((H, D), dtype=np.float32).astype(np.float16)
+    qd, o = _dev(q), torch.empty(H, D, dtype=torch.float16, device="cuda")
+    ws_n = _lib.size_query("aoakv_decode_workspace_size", H, D, 40)
+    ws = torch.zeros(ws_n, dtype=torch.uint8, device="cuda")
+    _lib.call("aoakv_sparse_decode", ptr(qd), ptr(o), ptr(lay.kv), cap, ptr(_dev(rows)), 0, 40, 50,
+              9, H, D, P, 0, 0.0, ptr(ws), ws_n, stream())
+    want = kt.sparse_decode(q, ref, rows, 50, 9)
+    assert np.abs(o.float().cpu().numpy() - want).max() < 2e-3
+    assert _lib.device_error() == 0
+    bad = rows.copy()
+    bad[3] = cap + 5
+    _lib.call("aoakv_sparse_decode", ptr(qd), ptr(o), ptr(lay.kv), cap, ptr(_dev(bad)), 0, 40, 50,
+              9, H, D, P, 0, 0.0, ptr(ws), ws_n, stream())
+    keep = np.delete(rows, 3)
+    want = kt.sparse_decode(q, ref, keep, 50, 9)
+    assert np.abs(o.float().cpu().numpy() - want).max() < 2e-3
+    assert _lib.device_error() == 1  # AOAKV_DEV_ERR_BAD_PAGE, then cleared
+    assert _lib.device_error() == 0

@@ -1,0 +1,139 @@
+"""GPU parity of the whole per-layer step (append -> estimate -> top-k ->
+sparse decode) against both oracles:
+  * semantics B (kernel tree, sink_first_page=0) — oracle.kernel_tree.step;
+  * semantics A (the reference simulation, fixed=True) — oracle.sim.decode_step
+    with sink_first_page=1.
+Selections must match exactly except for near-ties (1e-3 relative); the
+attention output must be within max-abs 2e-3 of the oracle (fp16 output)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from aoa_kv_b200 import _lib
+from gen import gen_qkv
+from gpu_util import GpuLayer, ptr, stream
+from helpers import selection_mismatch
+from oracle import kernel_tree as kt
+from oracle import sim
+
+pytestmark = pytest.mark.gpu
+
+
+def run_step(lay, q, k, v, n, last, budget, mode, sink):
+    H, D, P = lay.H, lay.D, lay.P
+    cols = max(3, budget) if sink else budget
+    ws_n = _lib.size_query("aoakv_step_workspace_size", H, D, lay.cap, cols)
+    ws = torch.zeros(ws_n, dtype=torch.uint8, device="cuda")
+    sel = torch.full((H, cols), -9, dtype=torch.int32, device="cuda")
+    o = torch.empty(H, D, dtype=torch.float16, device="cuda")
+    qd, kd, vd = (torch.from_numpy(x).cuda() for x in (q, k, v))
+    _lib.call("aoakv_decode_step", ptr(qd), ptr(kd), ptr(vd), ptr(o), ptr(lay.kv), ptr(lay.kv_idx),
+              n, last, lay.cap, ptr(lay.meta), ptr(lay.meta_idx), lay.mcap, ptr(lay.vlog), H, D, P,
+              budget, _lib.SCORE_AOAKV if mode == "aoakv" else _lib.SCORE_QUEST, int(sink),
+              ptr(sel), ptr(ws), ws_n, stream())
+    torch.cuda.synchronize()
+    return o.float().cpu().numpy(), sel.cpu().numpy()
+
+
+def logical(sel_phys, kv_idx, n):
+    inv = {int(p): i for i, p in enumerate(kv_idx[:n])}
+    return [sorted(inv[int(p)] for p in row if p >= 0) for row in sel_phys]
+
+
+CASES_B = [(8192, 64, "outlier"), (32768, 64, "outlier"), (1000, 16, "normal"),
+           (5000, 1, "normal"), (300, 64, "normal"), (4097, 2, "outlier"), (33, 64, "normal")]
+
+
+@pytest.mark.parametrize("mode", ["aoakv", "quest"])
+@pytest.mark.parametrize("S,budget,dist", CASES_B)
+def test_step_matches_kernel_tree(cuda, mode, S, budget, dist):
+    H, D, P = 32, 128, 16
+    q, K, V = gen_qkv(S + budget, H, S, D, dist)
+    n, last = (S + P - 1) // P, (S - 1) % P + 1
+    lay = GpuLayer(n + 2, H, D, P, seed=S)
+    lay.fill(K[:-1], V[:-1])
+    torch.cuda.synchronize()
+    ref = lay.snapshot()
+    got_o, got_sel = run_step(lay, q, K[-1], V[-1], n, last, budget, mode, sink=False)
+    want_o, want_sel = kt.step(q, K[-1], V[-1], ref, lay.kv_idx_np, lay.meta_idx_np, n, last,
+                               budget, mode, sink=False)
+    k = min(budget, n)
+    assert all(len(r) == k for r in logical(got_sel, lay.kv_idx_np, n))
+    assert np.all(got_sel[:, k:] == -1)
+    assert np.all(got_sel[:, k - 1] == lay.kv_idx_np[n - 1])  # last page last
+    g_log = np.array(logical(got_sel, lay.kv_idx_np, n))
+    w_log = np.array(logical(want_sel, lay.kv_idx_np, n))
+    if n > k and k > 1:
+        scores = kt.estimate(q, ref, lay.meta_idx_np, lay.kv_idx_np, n, mode)
+        scores = np.concatenate([scores, np.full((H, 1), np.inf, np.float32)], axis=1)
+        assert not selection_mismatch(g_log, w_log, scores)
+    else:
+        assert np.array_equal(g_log, w_log)
+    # output vs the oracle's decode over the pages the GPU chose
+    phys = [[int(p) for p in row[: k - 1]] for row in got_sel]
+    o_ref = kt.sparse_decode(q, ref, np.array(phys, dtype=np.int64).reshape(H, k - 1),
+                             int(lay.kv_idx_np[n - 1]), last)
+    assert np.abs(got_o - o_ref).max() < 2e-3
+    if np.array_equal(g_log, w_log):
+        assert np.abs(got_o - want_o).max() < 2e-3
+    assert _lib.device_error() == 0
+
+
+CASES_A = [(8192, 1024, "outlier"), (4096 + 7, 1024, "normal"), (2048, 256, "outlier"),
+           (528, 64, "normal"), (40, 1024, "normal"), (3000, 32, "normal")]
+
+
+@pytest.mark.parametrize("method", ["aoakv", "quest"])
+@pytest.mark.parametrize("S,B,dist", CASES_A)
+def test_step_sink_matches_reference_simulation(cuda, method, S, B, dist):
+    H, D, P = 32, 128, 16
+    q, K, V = gen_qkv(7 * S + B, H, S, D, dist)
+    n, last = (S + P - 1) // P, (S - 1) % P + 1
+    lay = GpuLayer(n + 2, H, D, P, seed=S + 1, permute=True)
+    lay.fill(K[:-1], V[:-1])
+    Kh, Vh = K.astype(np.float32).transpose(1, 0, 2), V.astype(np.float32).transpose(1, 0, 2)
+    st = sim.SimLayerState(Kh[:, :-1], Vh[:, :-1], P)
+    out_s, sel_s, sc_s = sim.decode_step(st, q.astype(np.float32), Kh[:, -1], Vh[:, -1], B,
+                                         method, True, expand=False)
+    budget_pages = min(S, B) // P
+    got_o, got_sel = run_step(lay, q, K[-1], V[-1], n, last, budget_pages, method, sink=True)
+    g_log = np.array(logical(got_sel, lay.kv_idx_np, n))
+    assert g_log.shape == sel_s.shape
+    assert not selection_mismatch(g_log, sel_s, sc_s)
+    mask = sim.token_mask(g_log, S, P)
+    o_ref = sim.masked_decode(q.astype(np.float32), st.K, st.V, mask)
+    assert np.abs(got_o - o_ref).max() < 2e-3
+    if np.array_equal(g_log, sel_s):
+        assert np.abs(got_o - out_s).max() < 2e-3
+
+
+def test_step_repeated_calls_keep_workspace_clean(cuda):
+    """Ten consecutive steps (tokens appended each time, one page boundary
+    crossed) against the oracle: the tickets in the workspace re-arm."""
+    H, D, P, B = 32, 128, 16, 16
+    S0 = 2000
+    q, K, V = gen_qkv(77, H, S0 + 10, D, "outlier")
+    cap = (S0 + 10 + P - 1) // P + 1
+    lay = GpuLayer(cap, H, D, P, seed=9)
+    lay.fill(K[:S0], V[:S0])
+    torch.cuda.synchronize()
+    ref = lay.snapshot()
+    ws_n = _lib.size_query("aoakv_step_workspace_size", H, D, cap, B)
+    ws = torch.zeros(ws_n, dtype=torch.uint8, device="cuda")
+    o = torch.empty(H, D, dtype=torch.float16, device="cuda")
+    qd = torch.from_numpy(q).cuda()
+    for t in range(S0, S0 + 10):
+        S = t + 1
+        n, last = (S + P - 1) // P, (S - 1) % P + 1
+        kd, vd = torch.from_numpy(K[t]).cuda(), torch.from_numpy(V[t]).cuda()
+        _lib.call("aoakv_decode_step", ptr(qd), ptr(kd), ptr(vd), ptr(o), ptr(lay.kv),
+                  ptr(lay.kv_idx), n, last, cap, ptr(lay.meta), ptr(lay.meta_idx), lay.mcap,
+                  ptr(lay.vlog), H, D, P, B, _lib.SCORE_AOAKV, 0, None, ptr(ws), ws_n, stream())
+        want_o, _ = kt.step(q, K[t], V[t], ref, lay.kv_idx_np, lay.meta_idx_np, n, last, B,
+                            "aoakv", False)
+        torch.cuda.synchronize()
+        assert np.abs(o.float().cpu().numpy() - want_o).max() < 2e-3, t
+    cnt = ws[: H * 4].view(torch.int32)
+    assert int(cnt.abs().sum()) == 0
