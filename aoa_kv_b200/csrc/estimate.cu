@@ -13,19 +13,19 @@ __global__ void __launch_bounds__(kEstThreads) estimate_kernel(EstimateArgs a) {
   stage_q<D>(a.q, q_s, a.H);
   __syncthreads();
   constexpr int RPS = kEstThreads / (D / 8);
-  const int64_t n_rows = static_cast<int64_t>(a.n_score) * a.H;
-  estimate_rows<D>(a, q_s, static_cast<int64_t>(blockIdx.x) * RPS * kEstUnroll,
-                   static_cast<int64_t>(gridDim.x) * RPS * kEstUnroll, n_rows);
+  estimate_rows<D>(a, q_s, blockIdx.x * RPS * kEstUnroll, gridDim.x * RPS * kEstUnroll,
+                   a.n_score * a.H);
 }
 
 }  // namespace
 
-// Grid for a sweep over n_rows (page, head) rows: enough CTAs that each does
-// about one unrolled sweep, capped at 8 resident CTAs per SM.
+// Grid for a sweep over n_rows (page, head) rows: one resident wave (4 CTAs
+// of 256 threads per SM at 64 registers), each CTA looping over sweeps so the
+// q staging is paid once per CTA.
 int estimate_grid(int64_t n_rows, int D) {
   const int64_t rows_per_cta = static_cast<int64_t>(kEstThreads / (D / 8)) * kEstUnroll;
   int64_t g = (n_rows + rows_per_cta - 1) / rows_per_cta;
-  const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 4;
   if (g > cap) g = cap;
   if (g < 1) g = 1;
   return static_cast<int>(g);
@@ -87,6 +87,7 @@ extern "C" int aoakv_estimate_attn_score(
   const int64_t n_kv = static_cast<int64_t>(num_metadata_pages - 1) * page_size +
                        metadata_last_page_len;
   AOAKV_CHECK_ARG(out_row_stride >= n_kv - 1, "estimate: out_row_stride below N-1");
+  AOAKV_CHECK_ARG((n_kv - 1) * num_heads < (1LL << 31), "estimate: too many (page, head) rows");
   if (score_mode == AOAKV_SCORE_AOAKV) {
     AOAKV_CHECK_ARG(v_log_norm != nullptr, "estimate: AOAKV mode needs v_log_norm");
     AOAKV_CHECK_ARG(kv_capacity_pages >= 1, "estimate: kv_capacity_pages must be >= 1");

@@ -41,24 +41,24 @@ constexpr int kEstUnroll = 4;
 
 template <int D>
 __device__ __forceinline__ void estimate_rows(const EstimateArgs& a,
-                                              const float* q_s, int64_t row0,
-                                              int64_t row_step, int64_t n_rows) {
+                                              const float* q_s, int row0,
+                                              int row_step, int n_rows) {
   constexpr int L = D / 8;
   constexpr int RPS = kEstThreads / L;  // rows per sweep of the CTA
   const int lane = threadIdx.x % L;
   const int sub = threadIdx.x / L;
   const size_t HD = static_cast<size_t>(a.H) * D;
   const size_t slot = static_cast<size_t>(a.P) * HD;  // max slot -> min slot
-  for (int64_t base = row0; base < n_rows; base += row_step) {
+  for (int base = row0; base < n_rows; base += row_step) {
     uint4 mx[kEstUnroll], mn[kEstUnroll];
     int hh[kEstUnroll], pp[kEstUnroll];
     bool ok[kEstUnroll];
 #pragma unroll
     for (int u = 0; u < kEstUnroll; ++u) {
-      const int64_t r = base + static_cast<int64_t>(u) * RPS + sub;
+      const int r = base + u * RPS + sub;
       ok[u] = r < n_rows;
-      const int p = ok[u] ? static_cast<int>(r / a.H) : 0;
-      const int h = ok[u] ? static_cast<int>(r % a.H) : 0;
+      const int p = ok[u] ? r / a.H : 0;
+      const int h = ok[u] ? r - p * a.H : 0;
       pp[u] = p;
       hh[u] = h;
       int mpid = ok[u] ? __ldg(a.meta_indices + p / a.P) : 0;
@@ -110,10 +110,18 @@ __device__ __forceinline__ void estimate_rows(const EstimateArgs& a,
   }
 }
 
-// Stages q (fp16 [H, D]) into shared memory as fp32.
+// Stages q (fp16 [H, D]) into shared memory as fp32, 16 bytes per load so a
+// CTA needs one or two round trips to L2 however many heads there are.
 template <int D>
 __device__ __forceinline__ void stage_q(const __half* q, float* q_s, int H) {
-  for (int i = threadIdx.x; i < H * D; i += blockDim.x) q_s[i] = __half2float(q[i]);
+  const int n8 = H * D / 8;
+  for (int i = threadIdx.x; i < n8; i += blockDim.x) {
+    float f[8];
+    u4_to_f8(__ldg(reinterpret_cast<const uint4*>(q) + i), f);
+    float4* dst = reinterpret_cast<float4*>(q_s + i * 8);
+    dst[0] = make_float4(f[0], f[1], f[2], f[3]);
+    dst[1] = make_float4(f[4], f[5], f[6], f[7]);
+  }
 }
 
 }  // namespace aoakv

@@ -54,9 +54,18 @@ __device__ __forceinline__ void radix_select(const uint32_t* keys, int n, int k,
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) sm.hist[i] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const uint32_t key = keys[i];
-      if ((key & mask) == prefix) atomicAdd(&sm.hist[(key >> shift) & 255u], 1u);
+    // Warp-aggregated histogram: scores of similar magnitude share their top
+    // key bits, so equal digits are grouped per warp (one atomic per group).
+    for (int base = 0; base < n; base += blockDim.x) {
+      const int i = base + threadIdx.x;
+      uint32_t d = 256u;  // sentinel: not counted
+      if (i < n) {
+        const uint32_t key = keys[i];
+        if ((key & mask) == prefix) d = (key >> shift) & 255u;
+      }
+      const uint32_t peers = __match_any_sync(0xffffffffu, d);
+      if (d < 256u && (threadIdx.x & 31) == __ffs(peers) - 1)
+        atomicAdd(&sm.hist[d], static_cast<uint32_t>(__popc(peers)));
     }
     __syncthreads();
     if (threadIdx.x < 32) {

@@ -59,6 +59,8 @@ def parse():
                     help="CPU-baseline sample budget (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--soak-seconds", type=float, default=1.0,
+                    help="graph replays before the timed region so the clock sampler sees load")
     return ap.parse_args()
 
 
@@ -297,8 +299,8 @@ def run_ours(a):
     for _ in range(a.warmup):
         graph.replay()
     torch.cuda.synchronize()
-    # keep the GPU busy ~1 s so the clock sampler sees it under this load
-    t_end = time.monotonic() + 1.0
+    # keep the GPU busy so the clock sampler sees it under this load
+    t_end = time.monotonic() + a.soak_seconds
     while time.monotonic() < t_end:
         for _ in range(20):
             graph.replay()
