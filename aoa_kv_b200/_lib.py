@@ -43,6 +43,7 @@ SIGNATURES = {
     "aoakv_sparse_decode": [_c_p, _c_p, _c_p, _c_i32, _c_p, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32,
                             _c_i32, _c_i32, _c_i32, _c_f, _c_p, _c_size, _c_p],
     "aoakv_step_workspace_size": [_c_i32, _c_i32, _c_i32, _c_i32, _c_sizep],
+    "aoakv_step_launches": [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_ip],
     "aoakv_decode_step": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p,
                           _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p,
                           _c_size, _c_p],

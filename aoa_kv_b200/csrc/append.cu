@@ -137,10 +137,17 @@ __global__ void __launch_bounds__(128) append_decode_kernel(AppendArgs a) {
   }
   if (entry + 1 == a.P) {  // uniform across the grid
     float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (ok) {
-      for (int e = 0; e + 1 < a.P; ++e)
-        acc8(s, *reinterpret_cast<const uint4*>(
-                    a.kv + row_off(pid, 1, e, h, a.H, a.P, D) + lane * 8));
+    if (ok) {  // the page's earlier V rows: 8 loads in flight, summed in order
+      for (int e0 = 0; e0 + 1 < a.P; e0 += 8) {
+        uint4 r[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (e0 + u + 1 < a.P)
+            r[u] = ld_stream_u4(a.kv + row_off(pid, 1, e0 + u, h, a.H, a.P, D) + lane * 8);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (e0 + u + 1 < a.P) acc8(s, r[u]);
+      }
       acc8(s, vv);
     }
     float l2 = group_sum<L>(mean_sq_norm(s, 1.f / a.P));

@@ -10,10 +10,10 @@
 //
 // Design: thread 0 issues one 3-D TMA box per K and V page tile (box
 // {D, 1, P} over the view [rows = page*2*P + kv*P + entry][H][D]), every tile
-// of the chunk up front, each completing on its own mbarrier. A warp owns a
-// page slot; lane l owns channels [l*D/32, (l+1)*D/32). Eight token dot
-// products finish with a 9-shuffle reduce-scatter (lane l ends with token
-// (l >> 2) & 7), then one online-softmax update per 8 tokens. Partial states
+// of the chunk up front, each completing on its own mbarrier. A warp owns one
+// 8-token group of one page slot; lane l owns channels [l*D/32, (l+1)*D/32).
+// The eight dot products finish with a 9-shuffle reduce-scatter (lane l ends
+// with token (l >> 2) & 7), then one online-softmax update. Partial states
 // merge across warps in shared memory and across chunks through a workspace;
 // the last CTA of a head (atomic ticket) writes the output and re-arms the
 // ticket, so no second launch and no host work is needed.
@@ -26,7 +26,7 @@ namespace aoakv {
 constexpr int kDecThreads = 128;
 constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kDecMaxChunk = 8;
-constexpr int kDecHeader = 128;  // 8 mbarriers (64 B) + 8 token counts (32 B)
+constexpr int kDecHeader = 128;  // 8 mbarriers (64 B) + 8 token counts (32 B) + flag
 
 struct DecodeArgs {
   const __half* q;             // [H, D]
@@ -45,14 +45,15 @@ struct DecodeArgs {
   int* err;
 };
 
-__host__ __device__ constexpr int dec_merge_bytes(int D) {
-  return kDecWarps * (D + 2) * 4;
+__host__ __device__ constexpr int dec_merge_bytes(int D, int nw = kDecWarps) {
+  return nw * (D + 2) * 4;
 }
-__host__ __device__ constexpr int dec_tile_offset(int D) {
-  return (kDecHeader + dec_merge_bytes(D) + 127) / 128 * 128;
+__host__ __device__ constexpr int dec_tile_offset(int D, int nw = kDecWarps) {
+  return (kDecHeader + dec_merge_bytes(D, nw) + 127) / 128 * 128;
 }
-__host__ __device__ constexpr size_t dec_smem_bytes(int D, int P, int chunk) {
-  return static_cast<size_t>(dec_tile_offset(D)) +
+__host__ __device__ constexpr size_t dec_smem_bytes(int D, int P, int chunk,
+                                                   int nw = kDecWarps) {
+  return static_cast<size_t>(dec_tile_offset(D, nw)) +
          static_cast<size_t>(chunk) * 2 * P * D * 2;
 }
 
@@ -75,21 +76,29 @@ __device__ __forceinline__ void load_row(const __half* p, float f[CPL]) {
   }
 }
 
-// Issues the TMA loads of unit (h, c). Thread 0 only. Returns nothing; slot
-// token counts land in tok[] (0 = skipped slot).
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async;" ::: "memory");
+}
+
+// Issues the TMA loads of unit (h, c). Thread 0 only. Slot token counts land
+// in tok[] (0 = skipped slot: bad page id or none). Selected page ids come
+// from a.indices, or from the shared window win[slot - win_lo] when given.
 __device__ __forceinline__ void decode_issue(const DecodeArgs& a,
                                              const CUtensorMap* tmap, int h,
                                              int c, uint64_t* bars, int* tok,
-                                             __half* tiles, int D) {
+                                             __half* tiles, int D,
+                                             const int* win = nullptr, int win_lo = 0) {
   const int n_slots = a.n_sel + 1;
   const int s0 = c * a.chunk_pages;
   const int ns = min(n_slots, s0 + a.chunk_pages) - s0;
   const int tile = a.P * D;
+  fence_proxy_async();  // prior generic smem/global accesses before async-proxy ones
   for (int j = 0; j < ns; ++j) {
     const int slot = s0 + j;
     int pid, nt;
     if (slot < a.n_sel) {
-      pid = __ldcg(a.indices + static_cast<size_t>(h) * a.idx_stride + slot);
+      pid = win ? win[slot - win_lo]
+                : __ldcg(a.indices + static_cast<size_t>(h) * a.idx_stride + slot);
       nt = a.P;
     } else {
       pid = a.last_page_ptr ? __ldcg(a.last_page_ptr) : a.last_page;
@@ -108,20 +117,92 @@ __device__ __forceinline__ void decode_issue(const DecodeArgs& a,
   }
 }
 
-// Computes unit (h, c) after decode_issue and a __syncthreads(). `parity` is
-// the mbarrier phase this unit's loads complete. Writes either the final
-// output (single chunk) or a partial state, and merges when last.
+// Online-softmax update of one warp's (m, l, o) with tokens [t0, t0+8) of
+// the page tile K/V that hold nt valid tokens (rows >= nt are ignored).
 template <int D>
-__device__ __forceinline__ void decode_compute(const DecodeArgs& a, int h, int c,
-                                               uint64_t* bars, const int* tok,
-                                               const __half* tiles, float* mrg,
-                                               int* flag_s, uint32_t parity) {
+__device__ __forceinline__ void attend8(const __half* K, const __half* V, int t0, int nt,
+                                        int P, const float* qv, float& m, float& l,
+                                        float* o) {
+  constexpr int CPL = D / 32;
+  const int lane = threadIdx.x & 31;
+  float part[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    part[u] = 0.f;
+    if (t0 + u < P) {
+      float kf[CPL];
+      load_row<CPL>(K + (t0 + u) * D + lane * CPL, kf);
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) part[u] = fmaf(qv[i], kf[i], part[u]);
+    }
+  }
+  // reduce-scatter 8 sums over 32 lanes: lane keeps token (lane>>2)&7
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+  float r4[4], r2[2], r1;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = b4 ? part[i] : part[4 + i];
+    const float keep = b4 ? part[4 + i] : part[i];
+    r4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = b3 ? r4[i] : r4[2 + i];
+    const float keep = b3 ? r4[2 + i] : r4[i];
+    r2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  {
+    const float send = b2 ? r2[0] : r2[1];
+    const float keep = b2 ? r2[1] : r2[0];
+    r1 = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
+  r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
+  const bool valid = t0 + ((lane >> 2) & 7) < nt;
+  const float sv = valid ? r1 : -INFINITY;
+  float gmax = fmaxf(sv, __shfl_xor_sync(0xffffffffu, sv, 4));
+  gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, 8));
+  gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, 16));
+  const float m_new = fmaxf(m, gmax);  // finite: token t0 is valid
+  const float alpha = fast_exp2(m - m_new);
+  const float p = valid ? fast_exp2(sv - m_new) : 0.f;
+  float ps = p + __shfl_xor_sync(0xffffffffu, p, 4);
+  ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+  ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+  l = l * alpha + ps;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) o[i] *= alpha;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const float pu = __shfl_sync(0xffffffffu, p, u * 4);
+    if (t0 + u < nt) {  // never touch rows past the valid tokens (may be NaN)
+      float vf[CPL];
+      load_row<CPL>(V + (t0 + u) * D + lane * CPL, vf);
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) o[i] = fmaf(pu, vf[i], o[i]);
+    }
+  }
+  m = m_new;
+}
+
+// Computes unit (h, c) after decode_issue and a __syncthreads(), with NW
+// warps (blockDim.x == 32 * NW). Work items are (slot, 8-token group) pairs.
+// Barrier j completes the phase (phase_bits >> j) & 1. Writes the final
+// output (single chunk) or a partial state and merges when last; the
+// finishing CTA also zeroes *rearm (if given) for the next call.
+template <int D, int NW>
+__device__ __forceinline__ void decode_compute_multi(const DecodeArgs& a, int h, int c,
+                                                     uint64_t* bars, const int* tok,
+                                                     const __half* tiles, float* mrg,
+                                                     int* flag_s, uint32_t phase_bits,
+                                                     uint32_t* rearm) {
   constexpr int CPL = D / 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_slots = a.n_sel + 1;
   const int s0 = c * a.chunk_pages;
   const int ns = min(n_slots, s0 + a.chunk_pages) - s0;
   const int tile = a.P * D;
+  const int groups = (a.P + 7) / 8;
 
   float qv[CPL];
   load_row<CPL>(a.q + static_cast<size_t>(h) * D + lane * CPL, qv);
@@ -132,73 +213,13 @@ __device__ __forceinline__ void decode_compute(const DecodeArgs& a, int h, int c
 #pragma unroll
   for (int i = 0; i < CPL; ++i) o[i] = 0.f;
 
-  const int my_tok = (lane >> 2) & 7;
-  for (int j = warp; j < ns; j += kDecWarps) {
+  for (int it = warp; it < ns * groups; it += NW) {
+    const int j = it / groups, t0 = (it % groups) * 8;
     const int nt = tok[j];
-    if (nt == 0) continue;
-    if (!mbar_wait_bounded(&bars[j], parity, a.err)) continue;
+    if (t0 >= nt) continue;
+    if (!mbar_wait_bounded(&bars[j], (phase_bits >> j) & 1u, a.err)) continue;
     const __half* K = tiles + (2 * j) * tile;
-    const __half* V = K + tile;
-    for (int t0 = 0; t0 < nt; t0 += 8) {
-      float part[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        part[u] = 0.f;
-        if (t0 + u < a.P) {
-          float kf[CPL];
-          load_row<CPL>(K + (t0 + u) * D + lane * CPL, kf);
-#pragma unroll
-          for (int i = 0; i < CPL; ++i) part[u] = fmaf(qv[i], kf[i], part[u]);
-        }
-      }
-      // reduce-scatter 8 sums over 32 lanes: lane keeps token (lane>>2)&7
-      const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
-      float r4[4], r2[2], r1;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float send = b4 ? part[i] : part[4 + i];
-        const float keep = b4 ? part[4 + i] : part[i];
-        r4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-      }
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const float send = b3 ? r4[i] : r4[2 + i];
-        const float keep = b3 ? r4[2 + i] : r4[i];
-        r2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-      }
-      {
-        const float send = b2 ? r2[0] : r2[1];
-        const float keep = b2 ? r2[1] : r2[0];
-        r1 = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-      }
-      r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
-      r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
-      const bool valid = t0 + my_tok < nt;
-      const float sv = valid ? r1 : -INFINITY;
-      float gmax = fmaxf(sv, __shfl_xor_sync(0xffffffffu, sv, 4));
-      gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, 8));
-      gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, 16));
-      const float m_new = fmaxf(m, gmax);
-      const float alpha = fast_exp2(m - m_new);
-      const float p = valid ? fast_exp2(sv - m_new) : 0.f;
-      float ps = p + __shfl_xor_sync(0xffffffffu, p, 4);
-      ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-      ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-      l = l * alpha + ps;
-#pragma unroll
-      for (int i = 0; i < CPL; ++i) o[i] *= alpha;
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float pu = __shfl_sync(0xffffffffu, p, u * 4);
-        if (t0 + u < nt) {
-          float vf[CPL];
-          load_row<CPL>(V + (t0 + u) * D + lane * CPL, vf);
-#pragma unroll
-          for (int i = 0; i < CPL; ++i) o[i] = fmaf(pu, vf[i], o[i]);
-        }
-      }
-      m = m_new;
-    }
+    attend8<D>(K, K + tile, t0, nt, a.P, qv, m, l, o);
   }
 
   // ---- merge the warps of this CTA
@@ -214,10 +235,10 @@ __device__ __forceinline__ void decode_compute(const DecodeArgs& a, int h, int c
   const int d = threadIdx.x;
   if (d < D) {
 #pragma unroll
-    for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, mrg[w * (D + 2) + D]);
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, mrg[w * (D + 2) + D]);
     if (M != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < kDecWarps; ++w) {
+      for (int w = 0; w < NW; ++w) {
         const float sc = fast_exp2(mrg[w * (D + 2) + D] - M);
         Ls += sc * mrg[w * (D + 2) + D + 1];
         O += sc * mrg[w * (D + 2) + d];
@@ -227,6 +248,7 @@ __device__ __forceinline__ void decode_compute(const DecodeArgs& a, int h, int c
   if (a.n_chunks == 1) {
     if (d < D)
       a.o[static_cast<size_t>(h) * D + d] = __float2half_rn(Ls > 0.f ? O / Ls : 0.f);
+    if (rearm && threadIdx.x == 0) *rearm = 0u;
     __syncthreads();
     return;
   }
@@ -256,9 +278,22 @@ __device__ __forceinline__ void decode_compute(const DecodeArgs& a, int h, int c
       }
       a.o[static_cast<size_t>(h) * D + d] = __float2half_rn(LL > 0.f ? OO / LL : 0.f);
     }
-    if (threadIdx.x == 0) a.ws_cnt[h] = 0;
+    if (threadIdx.x == 0) {
+      a.ws_cnt[h] = 0;
+      if (rearm) *rearm = 0u;
+    }
   }
   __syncthreads();
+}
+
+// The stand-alone decode: one unit per CTA of kDecWarps warps, phase 0.
+template <int D>
+__device__ __forceinline__ void decode_compute(const DecodeArgs& a, int h, int c,
+                                               uint64_t* bars, const int* tok,
+                                               const __half* tiles, float* mrg,
+                                               int* flag_s, uint32_t parity) {
+  decode_compute_multi<D, kDecWarps>(a, h, c, bars, tok, tiles, mrg, flag_s,
+                                     parity ? 0xffffffffu : 0u, nullptr);
 }
 
 }  // namespace aoakv

@@ -17,7 +17,38 @@ __global__ void __launch_bounds__(kEstThreads) estimate_kernel(EstimateArgs a) {
                    a.n_score * a.H);
 }
 
+constexpr int kHsUnroll = 4;
+
+template <int D>
+__global__ void __launch_bounds__(1024) estimate_hs_kernel(EstimateArgs a) {
+  int b, e;
+  page_range(a.n_score, blockIdx.x, gridDim.x, &b, &e);
+  estimate_pages_hs<D, kHsUnroll>(a, b, e);
+}
+
 }  // namespace
+
+// Head-stationary grid: enough CTAs of H*D/8 threads to cover every SM
+// (up to 2048 threads per SM), each with a contiguous page range.
+int launch_estimate_hs(const EstimateArgs& a, int D, cudaStream_t s) {
+  const int threads = a.H * (D / 8);
+  int per_sm = 0;
+  const void* fn = D == 128 ? reinterpret_cast<const void*>(estimate_hs_kernel<128>)
+                            : reinterpret_cast<const void*>(estimate_hs_kernel<64>);
+  AOAKV_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0),
+                 "estimate occupancy");
+  int grid = num_sms() * (per_sm < 1 ? 1 : per_sm);
+  const int min_pages = 2;  // at least a couple of pages per CTA
+  if (grid > (a.n_score + min_pages - 1) / min_pages)
+    grid = (a.n_score + min_pages - 1) / min_pages;
+  if (grid < 1) grid = 1;
+  if (D == 128)
+    estimate_hs_kernel<128><<<grid, threads, 0, s>>>(a);
+  else
+    estimate_hs_kernel<64><<<grid, threads, 0, s>>>(a);
+  AOAKV_CUDA_TRY(cudaGetLastError(), "estimate launch");
+  return AOAKV_OK;
+}
 
 // Grid for a sweep over n_rows (page, head) rows: one resident wave (4 CTAs
 // of 256 threads per SM at 64 registers), each CTA looping over sweeps so the
@@ -34,6 +65,8 @@ int estimate_grid(int64_t n_rows, int D) {
 int launch_estimate(const EstimateArgs& a, int D, cudaStream_t s) {
   const int64_t n_rows = static_cast<int64_t>(a.n_score) * a.H;
   if (n_rows == 0) return AOAKV_OK;
+  const int hs_threads = a.H * (D / 8);
+  if (hs_threads % 32 == 0 && hs_threads <= 1024) return launch_estimate_hs(a, D, s);
   const size_t smem = static_cast<size_t>(a.H) * D * sizeof(float);
   const int grid = estimate_grid(n_rows, D);
   if (D == 128) {

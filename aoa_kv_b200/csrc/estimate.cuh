@@ -39,12 +39,14 @@ struct EstimateArgs {
 constexpr int kEstThreads = 256;
 constexpr int kEstUnroll = 4;
 
-template <int D>
-__device__ __forceinline__ void estimate_rows(const EstimateArgs& a,
-                                              const float* q_s, int row0,
-                                              int row_step, int n_rows) {
+// Rows row0, row0 + row_step, ... (each a sweep of U * THREADS/L rows) of the
+// flattened (page, head) space; THREADS = blockDim.x.
+template <int D, int THREADS>
+__device__ __forceinline__ void estimate_rows_t(const EstimateArgs& a,
+                                                const float* q_s, int row0,
+                                                int row_step, int n_rows) {
   constexpr int L = D / 8;
-  constexpr int RPS = kEstThreads / L;  // rows per sweep of the CTA
+  constexpr int RPS = THREADS / L;  // rows per sweep of the CTA
   const int lane = threadIdx.x % L;
   const int sub = threadIdx.x / L;
   const size_t HD = static_cast<size_t>(a.H) * D;
@@ -108,6 +110,99 @@ __device__ __forceinline__ void estimate_rows(const EstimateArgs& a,
       }
     }
   }
+}
+
+template <int D>
+__device__ __forceinline__ void estimate_rows(const EstimateArgs& a, const float* q_s,
+                                              int row0, int row_step, int n_rows) {
+  estimate_rows_t<D, kEstThreads>(a, q_s, row0, row_step, n_rows);
+}
+
+// Head-stationary sweep over the pages [p_begin, p_end), used when
+// blockDim.x == H * D/8: thread t keeps head t/(D/8), channels
+// 8*(t % (D/8)) .. +8, so q stays in registers. Because max(q*kmax, q*kmin)
+// == q * (q > 0 ? kmax : kmin) whenever kmax >= kmin (which the append
+// maintains), each channel costs one bit-select of the fp16 operand, one
+// conversion and one FMA; the page's metadata rows, its v_log_norm and the
+// page-table entries are all loaded before any arithmetic.
+template <int D, int U>
+__device__ __forceinline__ void estimate_pages_hs(const EstimateArgs& a, int p_begin,
+                                                  int p_end) {
+  constexpr int L = D / 8;
+  const int h = threadIdx.x / L, lane = threadIdx.x % L;
+  float qv[8];
+  uint32_t msk[4];
+  u4_to_f8(__ldg(reinterpret_cast<const uint4*>(a.q + static_cast<size_t>(h) * D + lane * 8)),
+           qv);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    msk[i] = (qv[2 * i] > 0.f ? 0x0000ffffu : 0u) | (qv[2 * i + 1] > 0.f ? 0xffff0000u : 0u);
+  const bool aoa = a.mode == AOAKV_SCORE_AOAKV;
+  const size_t HD = static_cast<size_t>(a.H) * D;
+  const size_t slot = static_cast<size_t>(a.P) * HD;
+  const size_t col = static_cast<size_t>(h) * D + lane * 8;
+  for (int p0 = p_begin; p0 < p_end; p0 += U) {
+    uint4 mx[U], mn[U];
+    float vl[U];
+    bool ok[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int p = p0 + u;
+      ok[u] = p < p_end;
+      int mpid = 0, pid = 0;
+      if (ok[u]) {
+        mpid = __ldg(a.meta_indices + p / a.P);
+        pid = !aoa ? 0 : (a.kv_indices ? __ldg(a.kv_indices + p) : p);
+        if (mpid < 0 || mpid >= a.meta_cap || pid < 0 || (aoa && pid >= a.kv_cap)) {
+          raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
+          ok[u] = false;
+        }
+      }
+      mx[u] = make_uint4(0, 0, 0, 0);
+      mn[u] = make_uint4(0, 0, 0, 0);
+      vl[u] = 0.f;
+      if (ok[u]) {
+        const __half* row = a.meta + (static_cast<size_t>(mpid) * 2 * a.P + p % a.P) * HD + col;
+        mx[u] = ld_stream_u4(row);
+        mn[u] = ld_stream_u4(row + slot);
+        if (aoa) vl[u] = __half2float(a.vlog[static_cast<size_t>(pid) * a.H + h]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      uint4 sel;
+      sel.x = (mx[u].x & msk[0]) | (mn[u].x & ~msk[0]);
+      sel.y = (mx[u].y & msk[1]) | (mn[u].y & ~msk[1]);
+      sel.z = (mx[u].z & msk[2]) | (mn[u].z & ~msk[2]);
+      sel.w = (mx[u].w & msk[3]) | (mn[u].w & ~msk[3]);
+      float f[8];
+      u4_to_f8(sel, f);
+      float s0 = qv[0] * f[0], s1 = qv[1] * f[1];
+#pragma unroll
+      for (int i = 2; i < 8; i += 2) {
+        s0 = fmaf(qv[i], f[i], s0);
+        s1 = fmaf(qv[i + 1], f[i + 1], s1);
+      }
+      float s = s0 + s1;
+#pragma unroll
+      for (int off = L / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+      if (ok[u] && lane == 0) {
+        const float score = aoa ? a.two_rsqrt_d * s + 2.f * vl[u] : s;
+        const size_t o = static_cast<size_t>(h) * a.out_stride + (p0 + u);
+        if (a.out_f32)
+          static_cast<float*>(a.out)[o] = score;
+        else
+          static_cast<__half*>(a.out)[o] = __float2half_rn(score);
+      }
+    }
+  }
+}
+
+// Contiguous page range [*b, *e) of CTA `cta` out of `ctas` over n pages.
+__device__ __forceinline__ void page_range(int n, int cta, int ctas, int* b, int* e) {
+  const int per = (n + ctas - 1) / ctas;
+  *b = min(n, cta * per);
+  *e = min(n, *b + per);
 }
 
 // Stages q (fp16 [H, D]) into shared memory as fp32, 16 bytes per load so a

@@ -9,9 +9,12 @@
 // filtering/filter_util.py:226-231 and :373-377 (page 0 and the last page
 // forced, k = min(max(3, budget), N)).
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
 
 #include "decode.cuh"
 #include "estimate.cuh"
+#include "fused.h"
 #include "plan.h"
 #include "topk.cuh"
 
@@ -35,22 +38,33 @@ __global__ void fill_selected_kernel(int32_t* out, int budget, const int32_t* id
   }
 }
 
+// Workspace: [sync words][decode partials][fp32 scores][selected ids]. The
+// sync words and the decode tickets must be zero between calls.
 struct StepWs {
-  size_t scores_off, idx_off, dec_off, total;
+  size_t sync_off, dec_off, scores_off, idx_off, total;
 };
 
 StepWs step_ws_layout(int H, int D, int max_pages, int max_budget) {
   auto up = [](size_t x) { return (x + 255) / 256 * 256; };
   const int max_slots = max_budget < 3 ? 3 : max_budget;
   StepWs w;
-  w.dec_off = 0;
-  size_t off = up(decode_ws_bytes(H, D, max_slots));
+  w.sync_off = 0;
+  size_t off = up(fused_sync_bytes(H));
+  w.dec_off = off;
+  off += up(decode_ws_bytes(H, D, max_slots));
   w.scores_off = off;
   off += up(static_cast<size_t>(H) * max_pages * 4);
   w.idx_off = off;
   off += up(static_cast<size_t>(H) * max_slots * 4);
   w.total = off;
   return w;
+}
+
+// AOAKV_STEP_IMPL=chain selects the four-launch path instead of the fused
+// cooperative kernel (read on every call, for A/B comparisons).
+bool fused_enabled() {
+  const char* e = std::getenv("AOAKV_STEP_IMPL");
+  return !(e && std::strcmp(e, "chain") == 0);
 }
 
 }  // namespace
@@ -66,6 +80,31 @@ extern "C" int aoakv_step_workspace_size(int32_t num_heads, int32_t head_dim,
                       max_pages >= 1 && max_page_budget >= 1,
                   "step_workspace_size: bad arguments");
   *bytes = step_ws_layout(num_heads, head_dim, max_pages, max_page_budget).total;
+  return AOAKV_OK;
+}
+
+extern "C" int aoakv_step_launches(int32_t num_heads, int32_t head_dim, int32_t page_size,
+                                   int32_t num_kv_pages, int32_t page_budget,
+                                   int32_t sink_first_page, int32_t want_selected,
+                                   int32_t* kernels_out) {
+  AOAKV_CHECK_ARG(kernels_out != nullptr, "step_launches: kernels_out is NULL");
+  AOAKV_CHECK_ARG(num_heads >= 1 && (head_dim == 64 || head_dim == 128) && page_size >= 1 &&
+                      num_kv_pages >= 1 && page_budget >= 1,
+                  "step_launches: bad arguments");
+  const int N = num_kv_pages;
+  const int k_pages = sink_first_page ? (page_budget < 3 ? 3 : page_budget) : page_budget;
+  const int k = k_pages < N ? k_pages : N;
+  const bool sparse = N > k && k > 1;
+  int n = sparse ? 4 : 2;
+  if (sparse && fused_enabled()) {
+    int grid = 0, chunk = 0, n_chunks = 0;
+    size_t smem = 0;
+    if (fused_supported(num_heads, head_dim, page_size, N - 1, k - 1, &grid, &smem, &chunk,
+                        &n_chunks))
+      n = 1;
+  }
+  if (want_selected && n > 1) ++n;
+  *kernels_out = n;
   return AOAKV_OK;
 }
 
@@ -102,8 +141,77 @@ extern "C" int aoakv_decode_step(
     return set_error(AOAKV_ERR_WORKSPACE,
                      "step: workspace smaller than aoakv_step_workspace_size(...) = " +
                          std::to_string(lay.total));
+  AOAKV_CHECK_ARG(kv_last_page_len >= 1 && kv_last_page_len <= P,
+                  "step: kv_last_page_len must be in [1, page_size]");
+  AOAKV_CHECK_ARG(metadata_capacity_pages >= n_meta,
+                  "step: metadata capacity below ceil(num_kv_pages / page_size)");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
+
+  if (sparse && fused_enabled()) {
+    int grid = 0, chunk = 0, n_chunks = 0;
+    size_t smem = 0;
+    if (fused_supported(H, D, P, N - 1, k - 1, &grid, &smem, &chunk, &n_chunks)) {
+      FusedArgs f = {};
+      f.k_new = static_cast<const __half*>(k_new);
+      f.v_new = static_cast<const __half*>(v_new);
+      f.kv = static_cast<__half*>(kv_data);
+      f.kv_indices = kv_indices;
+      f.n_pages = N;
+      f.last_len = kv_last_page_len;
+      f.kv_cap = kv_capacity_pages;
+      f.meta = static_cast<__half*>(metadata_data);
+      f.meta_indices = metadata_indices;
+      f.meta_cap = metadata_capacity_pages;
+      f.vlog = static_cast<__half*>(v_log_norm);
+      f.H = H;
+      f.P = P;
+      f.k_sel = k - 1;
+      f.sink = sink_first_page != 0;
+      f.sel = reinterpret_cast<int32_t*>(ws + lay.idx_off);
+      f.sync = reinterpret_cast<uint32_t*>(ws + lay.sync_off);
+      f.selected_out = selected_out;
+      f.sel_cols = k_pages;
+      f.err = dev_error_ptr();
+      EstimateArgs& ea = f.est;
+      ea.q = static_cast<const __half*>(q);
+      ea.meta = f.meta;
+      ea.meta_indices = metadata_indices;
+      ea.kv_indices = kv_indices;
+      ea.vlog = f.vlog;
+      ea.out = ws + lay.scores_off;
+      ea.out_stride = N;
+      ea.out_f32 = 1;
+      ea.n_score = N - 1;
+      ea.H = H;
+      ea.P = P;
+      ea.meta_cap = metadata_capacity_pages;
+      ea.kv_cap = kv_capacity_pages;
+      ea.mode = score_mode;
+      ea.two_rsqrt_d = 2.f / std::sqrt(static_cast<float>(D));
+      ea.err = f.err;
+      DecodeArgs& dd = f.dec;
+      dd.q = ea.q;
+      dd.o = static_cast<__half*>(o);
+      dd.indices = f.sel;
+      dd.idx_stride = k - 1;
+      dd.n_sel = k - 1;
+      dd.last_len = kv_last_page_len;
+      dd.last_page_ptr = kv_indices + (N - 1);
+      dd.H = H;
+      dd.P = P;
+      dd.kv_cap = kv_capacity_pages;
+      dd.chunk_pages = chunk;
+      dd.n_chunks = n_chunks;
+      dd.scale_log2 = (1.f / std::sqrt(static_cast<float>(D))) * 1.4426950408889634f;
+      dd.err = f.err;
+      carve_decode_ws(ws + lay.dec_off, H, D, k, dd);
+      CUtensorMap tmap;
+      rc = make_kv_tmap(&tmap, kv_data, H, D, P, kv_capacity_pages);
+      if (rc) return rc;
+      return launch_fused(tmap, f, D, grid, smem, s);
+    }
+  }
 
   rc = aoakv_append_kv_cache_decode(k_new, v_new, kv_data, kv_indices, N,
                                     kv_last_page_len, kv_capacity_pages, metadata_data,

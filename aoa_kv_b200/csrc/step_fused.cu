@@ -1,0 +1,319 @@
+// Fused per-layer decode step: ONE cooperative launch runs append, page
+// scoring, top-k page selection, split-KV sparse decode and the
+// log-sum-exp merge.
+//
+//   A  CTA c < H appends head c of the new token, fused with the page's key
+//      max/min and, on page fill, its v_log_norm (decode_page.cuh:392-506).
+//   E  every CTA scores a contiguous share of the (page, head) rows
+//      (decode_attn.cuh:143-199, :263-443) into fp32 scores in the workspace
+//      and arrives on `est_done`.
+//   T  every CTA that owns decode units waits for all arrivals (the one
+//      grid-wide wait, bounded), then selects its head's pages itself with
+//      the shared-memory radix select (decode_select_k.cuh:25-61 semantics,
+//      exact, ties to the lower page) and keeps only the page ids of its
+//      own chunks in shared memory; the redundant selections of a head run
+//      in parallel on different SMs instead of hand-offs through flags.
+//   D  each unit (head, chunk of pages) gathers its pages with TMA and
+//      merges its partial state; the last unit of a head (ticket) writes
+//      o[h] (decode_attn.cuh:469-688, :937-1047).
+// The counters are re-armed to zero by their last user, so the workspace
+// stays zeroed between calls. A wait past ~1 s records AOAKV_DEV_ERR_TIMEOUT
+// and the CTA returns; the caller must then zero the workspace again.
+#include <cmath>
+
+#include "decode.cuh"
+#include "estimate.cuh"
+#include "fused.h"
+#include "plan.h"
+#include "topk.cuh"
+
+namespace aoakv {
+namespace {
+
+constexpr int kFThreads = 512;
+constexpr int kFWarps = kFThreads / 32;
+constexpr int kFMaxWin = 64;                 // selected slots one CTA may own
+constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s
+
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Thread 0 spins until *p >= target or the time limit; the result is
+// broadcast through *ok_s. Returns false on timeout (error recorded).
+__device__ __forceinline__ bool cta_wait_geq(const uint32_t* p, uint32_t target, int* ok_s,
+                                             int* err) {
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    if (ld_acquire(p) < target) {
+      const uint64_t t0 = global_ns();
+      uint32_t it = 0;
+      while (ld_acquire(p) < target) {
+        if (++it > 64) __nanosleep(32);
+        if ((it & 255u) == 0 && global_ns() - t0 > kWaitNs) {
+          raise_dev_error(err, AOAKV_DEV_ERR_TIMEOUT);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    __threadfence();
+    *ok_s = ok;
+  }
+  __syncthreads();
+  return *ok_s != 0;
+}
+
+__host__ __device__ inline int fused_smem_bytes(int H, int D, int P, int n_score, int chunk) {
+  const int q_bytes = H * D * 4;  // generic estimate path only
+  const int keys_bytes = n_score * 4;
+  const int dec_bytes = static_cast<int>(dec_smem_bytes(D, P, chunk, kFWarps));
+  int m = q_bytes > keys_bytes ? q_bytes : keys_bytes;
+  if (dec_bytes > m) m = dec_bytes;
+  return m + 128;  // + alignment slack for the TMA tiles
+}
+
+// Units [u, u_end) of one CTA; all units of this CTA for head u / n_chunks
+// end at min(u_end, next head's first unit).
+template <int D>
+__global__ void __launch_bounds__(kFThreads, 2)
+    fused_step_kernel(const __grid_constant__ CUtensorMap tmap, FusedArgs f) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
+  __shared__ TopkSmem tsm;
+  __shared__ int ok_s, flag_s;
+  __shared__ uint64_t bars[kDecMaxChunk];
+  __shared__ int tok_s[kDecMaxChunk];
+  __shared__ int win_s[kFMaxWin];
+
+  const int G = gridDim.x, b = blockIdx.x, H = f.H, P = f.P;
+  uint32_t* est_done = f.sync;
+  uint32_t* passed = f.sync + 1;
+
+  if (threadIdx.x == 0) {
+    for (int j = 0; j < kDecMaxChunk; ++j) mbar_init(&bars[j], 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap);
+  }
+
+  // ---- A: append head b of the new token (warp 0, D/8 lanes)
+  if (b < H && threadIdx.x < 32) {
+    constexpr int L = D / 8;
+    const int lane = threadIdx.x;
+    const int h = b;
+    const int page_iter = f.n_pages - 1;
+    const int entry = f.last_len - 1;
+    const int pid = __ldg(f.kv_indices + page_iter);
+    const int mpid = __ldg(f.meta_indices + page_iter / P);
+    const int mentry = page_iter % P;
+    const bool ok = pid >= 0 && pid < f.kv_cap && mpid >= 0 && mpid < f.meta_cap;
+    if (!ok && lane == 0) raise_dev_error(f.err, AOAKV_DEV_ERR_BAD_PAGE);
+    float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (ok && lane < L) {
+      const size_t HD = static_cast<size_t>(H) * D;
+      const size_t col = static_cast<size_t>(h) * D + lane * 8;
+      const uint4 kk = *reinterpret_cast<const uint4*>(f.k_new + col);
+      const uint4 vv = *reinterpret_cast<const uint4*>(f.v_new + col);
+      __half* mk = f.meta + ((static_cast<size_t>(mpid) * 2 + 0) * P + mentry) * HD + col;
+      __half* mv = f.meta + ((static_cast<size_t>(mpid) * 2 + 1) * P + mentry) * HD + col;
+      uint4 mx, mn;
+      if (entry > 0) {
+        mx = *reinterpret_cast<const uint4*>(mk);
+        mn = *reinterpret_cast<const uint4*>(mv);
+      } else {
+        const __half2 lo = __float2half2_rn(-65504.f), hi = __float2half2_rn(65504.f);
+        mx.x = mx.y = mx.z = mx.w = *reinterpret_cast<const uint32_t*>(&lo);
+        mn.x = mn.y = mn.z = mn.w = *reinterpret_cast<const uint32_t*>(&hi);
+      }
+      __half2* a2 = reinterpret_cast<__half2*>(&mx);
+      __half2* n2 = reinterpret_cast<__half2*>(&mn);
+      const __half2* k2 = reinterpret_cast<const __half2*>(&kk);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a2[i] = __hmax2(a2[i], k2[i]);
+        n2[i] = __hmin2(n2[i], k2[i]);
+      }
+      __half* kvk = f.kv + ((static_cast<size_t>(pid) * 2 + 0) * P + entry) * HD + col;
+      __half* kvv = f.kv + ((static_cast<size_t>(pid) * 2 + 1) * P + entry) * HD + col;
+      *reinterpret_cast<uint4*>(kvk) = kk;
+      *reinterpret_cast<uint4*>(kvv) = vv;
+      *reinterpret_cast<uint4*>(mk) = mx;
+      *reinterpret_cast<uint4*>(mv) = mn;
+      if (entry + 1 == P) {  // earlier V rows of the page: 8 loads in flight
+        for (int e0 = 0; e0 + 1 < P; e0 += 8) {
+          uint4 r[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (e0 + u + 1 < P)
+              r[u] = ld_stream_u4(f.kv + ((static_cast<size_t>(pid) * 2 + 1) * P + e0 + u) * HD +
+                                  col);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            if (e0 + u + 1 < P) {
+              float t[8];
+              u4_to_f8(r[u], t);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) s[i] += t[i];
+            }
+          }
+        }
+        float t[8];
+        u4_to_f8(vv, t);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s[i] += t[i];
+      }
+    }
+    if (entry + 1 == P) {
+      const float inv = 1.f / P;
+      float l2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) l2 += (s[i] * inv) * (s[i] * inv);
+#pragma unroll
+      for (int off = L / 2; off > 0; off >>= 1) l2 += __shfl_xor_sync(0xffffffffu, l2, off);
+      if (ok && lane == 0)
+        f.vlog[static_cast<size_t>(pid) * H + h] = __float2half_rn(logf(sqrtf(l2) + 1e-6f));
+    }
+  }
+
+  // ---- E: score this CTA's share of the (page, head) rows
+  if (H * (D / 8) == kFThreads) {  // head-stationary: one thread per (head, 8 channels)
+    int pb, pe;
+    page_range(f.est.n_score, b, G, &pb, &pe);
+    estimate_pages_hs<D, 4>(f.est, pb, pe);
+  } else {
+    float* q_s = reinterpret_cast<float*>(smem);
+    stage_q<D>(f.est.q, q_s, H);
+    __syncthreads();
+    constexpr int RPS = kFThreads / (D / 8);
+    estimate_rows_t<D, kFThreads>(f.est, q_s, b * RPS * kEstUnroll, G * RPS * kEstUnroll,
+                                  f.est.n_score * H);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(est_done, 1u);
+  }
+
+  // ---- T: wait for every CTA's scores, then re-arm the counters
+  if (!cta_wait_geq(est_done, static_cast<uint32_t>(G), &ok_s, f.err)) return;
+  if (threadIdx.x == 0 && atomicAdd(passed, 1u) == static_cast<uint32_t>(G - 1)) {
+    *est_done = 0u;  // every CTA has passed its wait
+    *passed = 0u;
+  }
+
+  // ---- T + D: this CTA's units [u_lo, u_hi), contiguous, possibly 2 heads
+  const int n_chunks = f.dec.n_chunks, C = f.dec.chunk_pages;
+  const int n_units = H * n_chunks;
+  const int upc = (n_units + G - 1) / G;
+  const int u_lo = min(n_units, b * upc), u_hi = min(n_units, u_lo + upc);
+  float* mrg = reinterpret_cast<float*>(smem + kDecHeader);
+  __half* tiles = reinterpret_cast<__half*>(smem + dec_tile_offset(D, kFWarps));
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem);
+  uint32_t phase_bits = 0;
+  int win_lo = 0;
+  for (int u = u_lo; u < u_hi; ++u) {
+    const int h = u / n_chunks, c = u % n_chunks;
+    if (u == u_lo || c == 0) {  // first unit of a head in this CTA: select
+      const int u_end = min(u_hi, (h + 1) * n_chunks);
+      win_lo = c * C;
+      const int win_hi = min(f.k_sel, u_end * C - h * n_chunks * C);
+      __syncthreads();  // keys overlap the previous unit's tiles
+      TopkArgs ta;
+      ta.scores = f.est.out;
+      ta.s_stride = f.est.out_stride;
+      ta.in_idx = f.kv_indices;
+      ta.in_stride = 0;
+      ta.out_vals = nullptr;
+      ta.ov_stride = 0;
+      const bool full_row = f.selected_out && c == 0;
+      ta.out_idx = full_row ? f.selected_out : nullptr;
+      ta.oi_stride = f.sel_cols;
+      ta.f32 = 1;
+      ta.n = f.est.n_score;
+      ta.k = f.k_sel;
+      ta.sink = f.sink;
+      topk_row_cg(ta, h, keys, tsm, win_s, win_lo, win_hi);
+      if (full_row)  // the last page after the selection, -1 padding
+        for (int i = f.k_sel + threadIdx.x; i < f.sel_cols; i += blockDim.x)
+          f.selected_out[static_cast<size_t>(h) * f.sel_cols + i] =
+              i == f.k_sel ? __ldg(f.kv_indices + f.n_pages - 1) : -1;
+      __syncthreads();
+    }
+    if (threadIdx.x == 0)  // (issues a proxy fence: appended page -> TMA reads)
+      decode_issue(f.dec, &tmap, h, c, bars, tok_s, tiles, D, win_s, win_lo);
+    __syncthreads();
+    decode_compute_multi<D, kFWarps>(f.dec, h, c, bars, tok_s, tiles, mrg, &flag_s,
+                                     phase_bits, nullptr);
+    const int ns = min(f.dec.n_sel + 1, (c + 1) * C) - c * C;
+    for (int j = 0; j < ns; ++j)
+      if (tok_s[j] > 0) phase_bits ^= 1u << j;
+    __syncthreads();
+  }
+}
+
+}  // namespace
+
+int fused_supported(int H, int D, int P, int n_score, int k_sel, int* grid_out,
+                    size_t* smem_out, int* chunk_out, int* n_chunks_out) {
+  const int k_slots = k_sel + 1;
+  const void* fn = D == 128 ? reinterpret_cast<const void*>(fused_step_kernel<128>)
+                            : reinterpret_cast<const void*>(fused_step_kernel<64>);
+  // chunk: the smallest C with H * ceil(k_slots / C) units <= grid (else C max)
+  for (int chunk = 1; chunk <= kDecMaxChunk; ++chunk) {
+    const int smem = fused_smem_bytes(H, D, P, n_score, chunk);
+    if (smem > 200 * 1024) return 0;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return 0;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kFThreads, smem) !=
+            cudaSuccess ||
+        occ < 1)
+      return 0;
+    const int grid = occ * num_sms();
+    const int n_chunks = (k_slots + chunk - 1) / chunk;
+    const int n_units = H * n_chunks;
+    if (grid < H) return 0;
+    if (n_units <= grid || chunk == kDecMaxChunk) {
+      const int upc = (n_units + grid - 1) / grid;
+      if (upc * chunk > kFMaxWin) return 0;  // a CTA's slot window must fit
+      *grid_out = grid;
+      *smem_out = smem;
+      *chunk_out = chunk;
+      *n_chunks_out = n_chunks;
+      return 1;
+    }
+  }
+  return 0;
+}
+
+size_t fused_sync_bytes(int H) { return ((2 + 2 * static_cast<size_t>(H)) * 4 + 255) / 256 * 256; }
+
+int launch_fused(const CUtensorMap& tmap, const FusedArgs& f, int D, int grid, size_t smem,
+                 cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kFThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (D == 128)
+    AOAKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, fused_step_kernel<128>, tmap, f), "fused step launch");
+  else
+    AOAKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, fused_step_kernel<64>, tmap, f), "fused step launch");
+  return AOAKV_OK;
+}
+
+}  // namespace aoakv

@@ -40,7 +40,12 @@ struct TopkSmem {
   uint32_t sel_rank;
 };
 
+// kL2: read through L2 only (scores written by other CTAs of the same launch).
+template <bool kL2 = false>
 __device__ __forceinline__ float load_score(const void* s, int f32, size_t i) {
+  if constexpr (kL2)
+    return f32 ? __ldcg(static_cast<const float*>(s) + i)
+               : __half2float(__ldcg(static_cast<const __half*>(s) + i));
   return f32 ? static_cast<const float*>(s)[i]
              : __half2float(static_cast<const __half*>(s)[i]);
 }
@@ -135,12 +140,17 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, TopkSmem& sm) {
 }
 
 // Selects row `row`'s top-k into out arrays. keys: shared buffer of >= n.
-// Must be called by every thread of the block.
+// Must be called by every thread of the block. Optionally also copies the
+// selected ids whose output position lies in [win_lo, win_hi) to
+// win[pos - win_lo] (a shared-memory window).
+template <bool kL2 = false>
 __device__ __forceinline__ void topk_row(const TopkArgs& a, int row,
-                                         uint32_t* keys, TopkSmem& sm) {
+                                         uint32_t* keys, TopkSmem& sm,
+                                         int* win = nullptr, int win_lo = 0,
+                                         int win_hi = 0) {
   const size_t sbase = static_cast<size_t>(row) * a.s_stride;
   for (int i = threadIdx.x; i < a.n; i += blockDim.x) {
-    uint32_t key = float_to_key(load_score(a.scores, a.f32, sbase + i));
+    uint32_t key = float_to_key(load_score<kL2>(a.scores, a.f32, sbase + i));
     if (a.sink && i == 0) key = 0xffffffffu;  // above every float key
     keys[i] = key;
   }
@@ -178,9 +188,10 @@ __device__ __forceinline__ void topk_row(const TopkArgs& a, int row,
       ++eq_before;
     }
     if (take) {
-      if (a.out_idx)
-        a.out_idx[static_cast<size_t>(row) * a.oi_stride + pos] =
-            a.in_idx ? __ldg(a.in_idx + ibase + i) : i;
+      const int id = a.in_idx ? __ldg(a.in_idx + ibase + i) : i;
+      if (a.out_idx) a.out_idx[static_cast<size_t>(row) * a.oi_stride + pos] = id;
+      if (win && static_cast<int>(pos) >= win_lo && static_cast<int>(pos) < win_hi)
+        win[pos - win_lo] = id;
       if (a.out_vals) {
         const size_t o = static_cast<size_t>(row) * a.ov_stride + pos;
         if (a.f32)
@@ -191,6 +202,13 @@ __device__ __forceinline__ void topk_row(const TopkArgs& a, int row,
     }
   }
   __syncthreads();
+}
+
+// topk_row for scores produced earlier in the same launch by other CTAs.
+__device__ __forceinline__ void topk_row_cg(const TopkArgs& a, int row, uint32_t* keys,
+                                            TopkSmem& sm, int* win = nullptr, int win_lo = 0,
+                                            int win_hi = 0) {
+  topk_row<true>(a, row, keys, sm, win, win_lo, win_hi);
 }
 
 }  // namespace aoakv

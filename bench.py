@@ -277,6 +277,11 @@ def run_ours(a):
 
     ctl, news = setup_layers(a, dev)
     outs = [torch.empty(1, H, D, dtype=torch.float16, device=dev) for _ in range(a.layers)]
+    import ctypes
+    nk = ctypes.c_int32(0)
+    ak._lib.call("aoakv_step_launches", H, D, P, len(ctl.kv_cache.indicies),
+                 ctl.step_page_budget(), int(ctl.sink_first_page), 0, ctypes.byref(nk))
+    kernels_per_layer = int(nk.value)
 
     def one_step():
         for layer, (q, k, v) in enumerate(news):
@@ -434,7 +439,8 @@ def run_ours(a):
             "step_roofline": {"bytes_per_layer_step": sb, "achieved": round(step_ach, 1),
                               "unit": "GB/s", "frac": round(step_ach / peak, 4),
                               "ideal_us": round(sb / (peak * 1e9) * 1e6, 3)},
-            "e2e": e2e, "gpu_launches": 4 * a.layers * a.steps, "clocks": clocks,
+            "e2e": e2e, "gpu_launches": kernels_per_layer * a.layers * a.steps,
+            "step_kernels_per_layer": kernels_per_layer, "clocks": clocks,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)

@@ -195,6 +195,17 @@ AOAKV_API int aoakv_step_workspace_size(int32_t num_heads, int32_t head_dim,
                               int32_t max_pages, int32_t max_page_budget,
                               size_t* bytes);
 
+/* Reports how aoakv_decode_step will run this problem on the current device:
+ * *kernels_out = 1 (one fused cooperative kernel: append, scoring, top-k and
+ * decode), 2 (append + decode, nothing to score), 4 (append, estimate,
+ * top-k, decode launched back to back with programmatic dependent launch;
+ * AOAKV_STEP_IMPL=chain forces it), plus 1 when selected_out is requested on
+ * the multi-kernel paths. */
+AOAKV_API int aoakv_step_launches(int32_t num_heads, int32_t head_dim, int32_t page_size,
+                                  int32_t num_kv_pages, int32_t page_budget,
+                                  int32_t sink_first_page, int32_t want_selected,
+                                  int32_t* kernels_out);
+
 AOAKV_API int aoakv_decode_step(
     const void* q, const void* k_new, const void* v_new, void* o,
     void* kv_data, const int32_t* kv_indices, int32_t num_kv_pages,

@@ -109,6 +109,86 @@ def test_step_sink_matches_reference_simulation(cuda, method, S, B, dist):
         assert np.abs(got_o - out_s).max() < 2e-3
 
 
+@pytest.fixture(params=["fused", "chain"])
+def step_impl(request, monkeypatch):
+    """Runs a test with the fused cooperative kernel and with the four-launch
+    chain (AOAKV_STEP_IMPL is read by the library on every call)."""
+    monkeypatch.setenv("AOAKV_STEP_IMPL", request.param)
+    return request.param
+
+
+@pytest.mark.parametrize("mode,sink,S,budget", [
+    (m, s, S, b) for m in ("aoakv", "quest") for s in (False, True)
+    for S, b in ((32768, 64), (8192 + 9, 64), (3000, 5))] + [("aoakv", False, 131072, 256)])
+def test_step_impls_agree_with_oracle(cuda, step_impl, mode, sink, S, budget):
+    H, D, P = 32, 128, 16
+    q, K, V = gen_qkv(S + 3 * budget, H, S, D, "outlier")
+    n, last = (S + P - 1) // P, (S - 1) % P + 1
+    lay = GpuLayer(n + 1, H, D, P, seed=S + 5)
+    lay.fill(K[:-1], V[:-1])
+    torch.cuda.synchronize()
+    ref = lay.snapshot()
+    got_o, got_sel = run_step(lay, q, K[-1], V[-1], n, last, budget, mode, sink)
+    kp = max(3, budget) if sink else budget
+    k = min(kp, n)
+    want_o, want_sel = kt.step(q, K[-1], V[-1], ref, lay.kv_idx_np, lay.meta_idx_np, n, last,
+                               budget, mode, sink)
+    g_log = np.array(logical(got_sel, lay.kv_idx_np, n))
+    w_log = np.array(logical(want_sel, lay.kv_idx_np, n))
+    scores = kt.estimate(q, ref, lay.meta_idx_np, lay.kv_idx_np, n, mode)
+    scores = np.concatenate([scores, np.full((H, 1), np.inf, np.float32)], axis=1)
+    if sink:
+        scores[:, 0] = np.inf
+    assert not selection_mismatch(g_log, w_log, scores)
+    phys = np.array([[int(p) for p in row[: k - 1]] for row in got_sel], dtype=np.int64)
+    o_ref = kt.sparse_decode(q, ref, phys.reshape(H, k - 1), int(lay.kv_idx_np[n - 1]), last)
+    assert np.abs(got_o - o_ref).max() < 2e-3
+    if np.array_equal(g_log, w_log):
+        assert np.abs(got_o - want_o).max() < 2e-3
+    # the appended token landed exactly as the oracle put it
+    after = lay.snapshot()
+    pid = int(lay.kv_idx_np[n - 1])
+    assert np.array_equal(after.kv[pid], ref.kv[pid])
+    assert np.array_equal(after.meta, ref.meta)
+    assert _lib.device_error() == 0
+
+
+def test_step_captured_in_cuda_graph(cuda, step_impl):
+    """The step (cooperative fused kernel or PDL chain) captures into a CUDA
+    graph and replays with the same result; the workspace stays clean."""
+    H, D, P, B = 32, 128, 16, 64
+    S = 8192
+    q, K, V = gen_qkv(99, H, S, D, "outlier")
+    n, last = (S + P - 1) // P, (S - 1) % P + 1
+    lay = GpuLayer(n + 1, H, D, P, seed=4)
+    lay.fill(K[:-1], V[:-1])
+    ws_n = _lib.size_query("aoakv_step_workspace_size", H, D, lay.cap, B)
+    ws = torch.zeros(ws_n, dtype=torch.uint8, device="cuda")
+    o = torch.empty(H, D, dtype=torch.float16, device="cuda")
+    qd, kd, vd = (torch.from_numpy(x).cuda() for x in (q, K[-1], V[-1]))
+
+    def call():
+        _lib.call("aoakv_decode_step", ptr(qd), ptr(kd), ptr(vd), ptr(o), ptr(lay.kv),
+                  ptr(lay.kv_idx), n, last, lay.cap, ptr(lay.meta), ptr(lay.meta_idx), lay.mcap,
+                  ptr(lay.vlog), H, D, P, B, _lib.SCORE_AOAKV, 0, None, ptr(ws), ws_n,
+                  torch.cuda.current_stream().cuda_stream)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        call()
+    torch.cuda.synchronize()
+    eager = o.clone()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        call()
+    for _ in range(5):
+        o.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(o, eager)
+    assert int(ws[:512].view(torch.int32).abs().sum()) == 0
+    assert _lib.device_error() == 0
+
+
 def test_step_repeated_calls_keep_workspace_clean(cuda):
     """Ten consecutive steps (tokens appended each time, one page boundary
     crossed) against the oracle: the tickets in the workspace re-arm."""
