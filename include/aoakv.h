@@ -175,6 +175,30 @@ AOAKV_API int aoakv_sparse_decode(
     int32_t num_heads, int32_t head_dim, int32_t page_size, int32_t layout,
     float sm_scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Sparse decode for callers that cannot allocate device memory — no
+ * counterpart in the reference. Same inputs, outputs and results as
+ * aoakv_sparse_decode, but the partial softmax states of the page chunks go
+ * to a fixed 1 MiB array inside the library (one per GPU that loads it, kept
+ * until the process exits) instead of a caller workspace. It calls no
+ * cudaMalloc/cudaFree. Use it when the caller's memory is all pre-reserved,
+ * when it is invoked during someone else's stream capture, or when an
+ * allocation's possible device synchronisation is unacceptable.
+ *   - The first call on each device resolves the array's address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - Every call shares the array: calls that overlap on the GPU race, so
+ *     serialise them (one stream per device). Each call zeroes the chunk
+ *     tickets it needs on its own stream first.
+ *   - Problems whose num_heads x page chunks need more than 1 MiB of partial
+ *     states (e.g. 32 heads of head_dim 128 with more than ~60 chunks) return
+ *     AOAKV_ERR_UNSUPPORTED; use aoakv_sparse_decode with a workspace. */
+AOAKV_API int aoakv_sparse_decode_noalloc(
+    const void* q, void* o,
+    const void* kv_data, int32_t kv_capacity_pages,
+    const int32_t* indices, int64_t indices_row_stride, int32_t num_selected,
+    int32_t last_page_idx, int32_t last_page_len,
+    int32_t num_heads, int32_t head_dim, int32_t page_size, int32_t layout,
+    float sm_scale, void* stream);
+
 /* Whole per-layer decode step for one request: a1 append of (k_new, v_new),
  * a3 estimate, a4 top-k and a5 sparse decode, as the reference's
  * QuestAttention.forward decode branch issues them
