@@ -71,6 +71,28 @@ int make_kv_tmap(CUtensorMap* map, const void* kv, int H, int D, int P, int cap)
   return AOAKV_OK;
 }
 
+int make_meta_tmap(CUtensorMap* map, const void* meta, int H, int D, int P, int meta_cap) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(AOAKV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (reinterpret_cast<uintptr_t>(meta) % 16)
+    return set_error(AOAKV_ERR_INVALID_ARG, "metadata_data must be 16-byte aligned");
+  if (H > 256 || D > 256)
+    return set_error(AOAKV_ERR_UNSUPPORTED, "metadata tensor map: heads or head_dim above 256");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(meta_cap) * 2 * P};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2,
+                           static_cast<cuuint64_t>(H) * D * 2};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(D), static_cast<cuuint32_t>(H), 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(meta), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(AOAKV_ERR_CUDA,
+                     "cuTensorMapEncodeTiled (metadata) failed with CUresult " + std::to_string(r));
+  return AOAKV_OK;
+}
+
 DecodePlan plan_decode(int H, int n_slots, int D, int P) {
   DecodePlan pl;
   const int64_t target = static_cast<int64_t>(num_sms()) * 4;

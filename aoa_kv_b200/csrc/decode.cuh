@@ -43,6 +43,8 @@ struct DecodeArgs {
   float2* ws_ml;               // [H, n_chunks] partial (max, denominator)
   int* ws_cnt;                 // [H] arrival tickets, zero between calls
   int* err;
+  float* o_f32;                // if set: fp32 output [H, D] instead of o
+  float* lse;                  // if set: natural-log sum of exp of the scores [H]
 };
 
 __host__ __device__ constexpr int dec_merge_bytes(int D, int nw = kDecWarps) {
@@ -76,9 +78,6 @@ __device__ __forceinline__ void load_row(const __half* p, float f[CPL]) {
   }
 }
 
-__device__ __forceinline__ void fence_proxy_async() {
-  asm volatile("fence.proxy.async;" ::: "memory");
-}
 
 // Issues the TMA loads of unit (h, c). Thread 0 only. Slot token counts land
 // in tok[] (0 = skipped slot: bad page id or none). Selected page ids come
@@ -93,18 +92,28 @@ __device__ __forceinline__ void decode_issue(const DecodeArgs& a,
   const int ns = min(n_slots, s0 + a.chunk_pages) - s0;
   const int tile = a.P * D;
   fence_proxy_async();  // prior generic smem/global accesses before async-proxy ones
-  for (int j = 0; j < ns; ++j) {
+  int pids[kDecMaxChunk];
+#pragma unroll
+  for (int j = 0; j < kDecMaxChunk; ++j) {  // all page ids first: one round trip
     const int slot = s0 + j;
-    int pid, nt;
-    if (slot < a.n_sel) {
-      pid = win ? win[slot - win_lo]
-                : __ldcg(a.indices + static_cast<size_t>(h) * a.idx_stride + slot);
-      nt = a.P;
-    } else {
-      pid = a.last_page_ptr ? __ldcg(a.last_page_ptr) : a.last_page;
-      nt = a.last_len;
+    pids[j] = 0;
+    if (j < ns) {
+      if (slot < a.n_sel)
+        pids[j] = win ? win[slot - win_lo]
+                      : __ldcg(a.indices + static_cast<size_t>(h) * a.idx_stride + slot);
+      else
+        pids[j] = a.last_page_ptr ? __ldcg(a.last_page_ptr) : a.last_page;
     }
-    if (pid < 0 || pid >= a.kv_cap) {
+  }
+#pragma unroll
+  for (int j = 0; j < kDecMaxChunk; ++j) {
+    if (j >= ns) break;
+    const int slot = s0 + j;
+    const int pid = pids[j];
+    int nt = slot < a.n_sel ? a.P : a.last_len;
+    if (pid == -1) {
+      nt = 0;  // "no page here" (a shard that does not own this selected page)
+    } else if (pid < 0 || pid >= a.kv_cap) {
       raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
       nt = 0;
     }
@@ -115,6 +124,21 @@ __device__ __forceinline__ void decode_issue(const DecodeArgs& a,
       tma_load_3d(tiles + (2 * j + 1) * tile, tmap, 0, h, (pid * 2 + 1) * a.P, &bars[j]);
     }
   }
+}
+
+// Final output of head h, channel d from the merged state (numerator O,
+// denominator L, running max M in log2 units): o = O / L (fp16, or fp32 when
+// a.o_f32 is set) and, if requested, lse = ln(sum exp(s)) = (M + log2 L) ln 2.
+// A head with no tokens (L == 0) gets o = 0 and lse = -inf.
+__device__ __forceinline__ void decode_write_out(const DecodeArgs& a, int h, int d, int D,
+                                                 float O, float L, float M) {
+  const float v = L > 0.f ? O / L : 0.f;
+  const size_t i = static_cast<size_t>(h) * D + d;
+  if (a.o_f32)
+    a.o_f32[i] = v;
+  else
+    a.o[i] = __float2half_rn(v);
+  if (a.lse && d == 0) a.lse[h] = L > 0.f ? (M + log2f(L)) * 0.6931471805599453f : -INFINITY;
 }
 
 // Online-softmax update of one warp's (m, l, o) with tokens [t0, t0+8) of
@@ -246,8 +270,7 @@ __device__ __forceinline__ void decode_compute_multi(const DecodeArgs& a, int h,
     }
   }
   if (a.n_chunks == 1) {
-    if (d < D)
-      a.o[static_cast<size_t>(h) * D + d] = __float2half_rn(Ls > 0.f ? O / Ls : 0.f);
+    if (d < D) decode_write_out(a, h, d, D, O, Ls, M);
     if (rearm && threadIdx.x == 0) *rearm = 0u;
     __syncthreads();
     return;
@@ -276,7 +299,7 @@ __device__ __forceinline__ void decode_compute_multi(const DecodeArgs& a, int h,
           OO += sc * __ldcg(po + static_cast<size_t>(k) * D + d);
         }
       }
-      a.o[static_cast<size_t>(h) * D + d] = __float2half_rn(LL > 0.f ? OO / LL : 0.f);
+      decode_write_out(a, h, d, D, OO, LL, MM);
     }
     if (threadIdx.x == 0) {
       a.ws_cnt[h] = 0;

@@ -1,5 +1,7 @@
 // a3 stand-alone entry point: aoakv_estimate_attn_score.
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
 
 #include "estimate.cuh"
 #include "plan.h"
@@ -26,26 +28,75 @@ __global__ void __launch_bounds__(1024) estimate_hs_kernel(EstimateArgs a) {
   estimate_pages_hs<D, kHsUnroll>(a, b, e);
 }
 
+template <int D>
+__global__ void __launch_bounds__(1024) estimate_tma_kernel(EstimateArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* stages = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
+  __shared__ uint64_t bars[kEstStages];
+  __shared__ int ids_s[2 * kEstMaxRange];
+  if (threadIdx.x == 0) {
+    for (int j = 0; j < kEstStages; ++j) mbar_init(&bars[j], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  int b, e;
+  page_range(a.n_score, blockIdx.x, gridDim.x, &b, &e);
+  uint32_t phase = 0;
+  estimate_pages_tma<D>(a, b, e, stages, bars, ids_s, &phase);
+}
+
 }  // namespace
 
 // Head-stationary grid: enough CTAs of H*D/8 threads to cover every SM
-// (up to 2048 threads per SM), each with a contiguous page range.
+// (up to 2048 threads per SM), each with a contiguous page range. With
+// H % 8 == 0, 16-byte aligned buffers and <= kEstMaxRange pages per CTA the
+// pages stream through a shared-memory ring by bulk copies; otherwise the
+// threads load their 16-byte rows into registers.
+int launch_estimate_hs(const EstimateArgs& a, int D, cudaStream_t s, bool tma);
+
 int launch_estimate_hs(const EstimateArgs& a, int D, cudaStream_t s) {
+  const bool aoa = a.mode == AOAKV_SCORE_AOAKV;
+  const char* impl = std::getenv("AOAKV_EST_IMPL");  // "regs": A/B comparisons
+  const bool tma = a.H % 8 == 0 && reinterpret_cast<uintptr_t>(a.meta) % 16 == 0 &&
+                   (!aoa || reinterpret_cast<uintptr_t>(a.vlog) % 16 == 0) &&
+                   !(impl && std::strcmp(impl, "regs") == 0);
+  return launch_estimate_hs(a, D, s, tma);
+}
+
+int launch_estimate_hs(const EstimateArgs& a, int D, cudaStream_t s, bool tma) {
   const int threads = a.H * (D / 8);
+  const size_t smem = tma ? static_cast<size_t>(kEstStages) * est_stage_bytes(a.H, D) + 128 : 0;
+  const void* fn =
+      tma ? (D == 128 ? reinterpret_cast<const void*>(estimate_tma_kernel<128>)
+                      : reinterpret_cast<const void*>(estimate_tma_kernel<64>))
+          : (D == 128 ? reinterpret_cast<const void*>(estimate_hs_kernel<128>)
+                      : reinterpret_cast<const void*>(estimate_hs_kernel<64>));
+  if (smem > 48 * 1024)
+    AOAKV_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem)),
+                   "estimate smem attribute");
   int per_sm = 0;
-  const void* fn = D == 128 ? reinterpret_cast<const void*>(estimate_hs_kernel<128>)
-                            : reinterpret_cast<const void*>(estimate_hs_kernel<64>);
-  AOAKV_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0),
+  AOAKV_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem),
                  "estimate occupancy");
   int grid = num_sms() * (per_sm < 1 ? 1 : per_sm);
   const int min_pages = 2;  // at least a couple of pages per CTA
   if (grid > (a.n_score + min_pages - 1) / min_pages)
     grid = (a.n_score + min_pages - 1) / min_pages;
   if (grid < 1) grid = 1;
-  if (D == 128)
-    estimate_hs_kernel<128><<<grid, threads, 0, s>>>(a);
-  else
-    estimate_hs_kernel<64><<<grid, threads, 0, s>>>(a);
+  if (tma && (a.n_score + grid - 1) / grid > kEstMaxRange)  // too long a range per CTA
+    return launch_estimate_hs(a, D, s, false);
+  if (tma) {
+    if (D == 128)
+      estimate_tma_kernel<128><<<grid, threads, smem, s>>>(a);
+    else
+      estimate_tma_kernel<64><<<grid, threads, smem, s>>>(a);
+  } else {
+    if (D == 128)
+      estimate_hs_kernel<128><<<grid, threads, 0, s>>>(a);
+    else
+      estimate_hs_kernel<64><<<grid, threads, 0, s>>>(a);
+  }
   AOAKV_CUDA_TRY(cudaGetLastError(), "estimate launch");
   return AOAKV_OK;
 }

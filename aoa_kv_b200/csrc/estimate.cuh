@@ -198,6 +198,225 @@ __device__ __forceinline__ void estimate_pages_hs(const EstimateArgs& a, int p_b
   }
 }
 
+// ---------------------------------------------------------------------------
+// Bulk-copy pipelined page scorer (blockDim.x == H * D/8, H % 8 == 0): the
+// metadata of one page for all heads — its max block and min block, H*D fp16
+// each, contiguous — and its v_log_norm row land in a shared-memory stage by
+// three 1-D bulk copies issued by one thread; kEstStages stages keep the
+// CTA's next pages in flight while the current one is scored, so HBM sees
+// large contiguous reads with no register cost. The page-table entries of
+// the CTA's whole range are fetched first in one round trip.
+constexpr int kEstStages = 4;
+constexpr int kEstMaxRange = 64;  // pages per CTA for this path
+
+__host__ __device__ constexpr int est_stage_bytes(int H, int D) {
+  return (2 * H * D * 2 + H * 2 + 127) / 128 * 128;
+}
+
+// ids_s: shared int[2 * kEstMaxRange]; bars: kEstStages mbarriers initialised
+// to count 1 whose phases are tracked in *phase_bits (bit s = next parity).
+template <int D>
+__device__ __forceinline__ void estimate_pages_tma(const EstimateArgs& a, int p_begin, int p_end,
+                                                   uint8_t* stages, uint64_t* bars, int* ids_s,
+                                                   uint32_t* phase_bits) {
+  constexpr int L = D / 8;
+  const int h = threadIdx.x / L, lane = threadIdx.x % L;
+  const int R = p_end - p_begin;
+  const bool aoa = a.mode == AOAKV_SCORE_AOAKV;
+  const int H = a.H;
+  const size_t HD = static_cast<size_t>(H) * D;
+  const int sb = est_stage_bytes(H, D);
+  float qv[8];
+  uint32_t msk[4];
+  u4_to_f8(__ldg(reinterpret_cast<const uint4*>(a.q + static_cast<size_t>(h) * D + lane * 8)),
+           qv);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    msk[i] = (qv[2 * i] > 0.f ? 0x0000ffffu : 0u) | (qv[2 * i + 1] > 0.f ? 0xffff0000u : 0u);
+  for (int t = threadIdx.x; t < R; t += blockDim.x) {
+    const int p = p_begin + t;
+    int mp = __ldg(a.meta_indices + p / a.P);
+    const int pid = aoa ? (a.kv_indices ? __ldg(a.kv_indices + p) : p) : 0;
+    if (mp < 0 || mp >= a.meta_cap || pid < 0 || (aoa && pid >= a.kv_cap)) {
+      raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
+      mp = -1;
+    }
+    ids_s[2 * t] = mp;
+    ids_s[2 * t + 1] = pid;
+  }
+  __syncthreads();
+  auto issue = [&](int j) {  // thread 0 only
+    const int s = j % kEstStages;
+    const int mp = ids_s[2 * j], pid = ids_s[2 * j + 1];
+    if (mp < 0) {
+      mbar_arrive(&bars[s]);  // complete the phase; the page is skipped
+      return;
+    }
+    uint8_t* st = stages + s * sb;
+    const int p = p_begin + j;
+    const uint32_t blk = static_cast<uint32_t>(HD * 2);
+    mbar_arrive_expect_tx(&bars[s], 2 * blk + (aoa ? static_cast<uint32_t>(H * 2) : 0u));
+    const __half* row = a.meta + (static_cast<size_t>(mp) * 2 * a.P + p % a.P) * HD;
+    bulk_g2s(st, row, blk, &bars[s]);
+    bulk_g2s(st + blk, row + static_cast<size_t>(a.P) * HD, blk, &bars[s]);
+    if (aoa) bulk_g2s(st + 2 * blk, a.vlog + static_cast<size_t>(pid) * H, H * 2, &bars[s]);
+  };
+  if (threadIdx.x == 0) {
+    fence_proxy_async_smem();
+    for (int j = 0; j < R && j < kEstStages; ++j) issue(j);
+  }
+  // The issuing thread must rejoin its warp before anyone polls the
+  // barriers: without this block barrier its head's scores came out wrong
+  // inside the fused step kernel.
+  __syncthreads();
+  for (int j = 0; j < R; ++j) {
+    const int s = j % kEstStages;
+    const bool arrived = mbar_wait_bounded(&bars[s], (*phase_bits >> s) & 1u, a.err);
+    *phase_bits ^= 1u << s;
+    const uint8_t* st = stages + s * sb;
+    const bool ok = arrived && ids_s[2 * j] >= 0;
+    const size_t off = (static_cast<size_t>(h) * D + lane * 8) * 2;
+    const uint4 mx = *reinterpret_cast<const uint4*>(st + off);
+    const uint4 mn = *reinterpret_cast<const uint4*>(st + HD * 2 + off);
+    const float vl = aoa ? __half2float(reinterpret_cast<const __half*>(st + HD * 4)[h]) : 0.f;
+    uint4 sel;
+    sel.x = (mx.x & msk[0]) | (mn.x & ~msk[0]);
+    sel.y = (mx.y & msk[1]) | (mn.y & ~msk[1]);
+    sel.z = (mx.z & msk[2]) | (mn.z & ~msk[2]);
+    sel.w = (mx.w & msk[3]) | (mn.w & ~msk[3]);
+    float f[8];
+    u4_to_f8(sel, f);
+    float s0 = qv[0] * f[0], s1 = qv[1] * f[1];
+#pragma unroll
+    for (int i = 2; i < 8; i += 2) {
+      s0 = fmaf(qv[i], f[i], s0);
+      s1 = fmaf(qv[i + 1], f[i + 1], s1);
+    }
+    float sc = s0 + s1;
+#pragma unroll
+    for (int off2 = L / 2; off2 > 0; off2 >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off2);
+    if (ok && lane == 0) {
+      const float score = aoa ? a.two_rsqrt_d * sc + 2.f * vl : sc;
+      const size_t o = static_cast<size_t>(h) * a.out_stride + (p_begin + j);
+      if (a.out_f32)
+        static_cast<float*>(a.out)[o] = score;
+      else
+        static_cast<__half*>(a.out)[o] = __float2half_rn(score);
+    }
+    __syncthreads();  // stage s is free again
+    if (threadIdx.x == 0 && j + kEstStages < R) {
+      fence_proxy_async_smem();
+      issue(j + kEstStages);
+    }
+    __syncwarp();  // the issuing thread rejoins warp 0 before its next wait
+  }
+}
+
+// Tensor-map variant of estimate_pages_tma: the max and min blocks of a
+// page are two 3-D TMA boxes {D, H, 1} of `mmap` (the metadata viewed as
+// [rows = meta_page*2*P + slot*P + entry][H][D]); v_log_norm values are
+// plain loads issued before the wait. Same results, same stage layout.
+template <int D>
+__device__ __forceinline__ void estimate_pages_tmap(const EstimateArgs& a, const CUtensorMap* mmap,
+                                                    int p_begin, int p_end, uint8_t* stages,
+                                                    uint64_t* bars, int* ids_s,
+                                                    uint32_t* phase_bits) {
+  constexpr int L = D / 8;
+  const int h = threadIdx.x / L, lane = threadIdx.x % L;
+  const int R = p_end - p_begin;
+  const bool aoa = a.mode == AOAKV_SCORE_AOAKV;
+  const int H = a.H;
+  const size_t HD = static_cast<size_t>(H) * D;
+  const int sb = est_stage_bytes(H, D);
+  float qv[8];
+  uint32_t msk[4];
+  u4_to_f8(__ldg(reinterpret_cast<const uint4*>(a.q + static_cast<size_t>(h) * D + lane * 8)),
+           qv);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    msk[i] = (qv[2 * i] > 0.f ? 0x0000ffffu : 0u) | (qv[2 * i + 1] > 0.f ? 0xffff0000u : 0u);
+  for (int t = threadIdx.x; t < R; t += blockDim.x) {
+    const int p = p_begin + t;
+    int mp = __ldg(a.meta_indices + p / a.P);
+    const int pid = aoa ? (a.kv_indices ? __ldg(a.kv_indices + p) : p) : 0;
+    if (mp < 0 || mp >= a.meta_cap || pid < 0 || (aoa && pid >= a.kv_cap)) {
+      raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
+      mp = -1;
+    }
+    ids_s[2 * t] = mp;
+    ids_s[2 * t + 1] = pid;
+  }
+  __syncthreads();
+  const uint32_t blk = static_cast<uint32_t>(HD * 2);
+  if (threadIdx.x == 0) {
+    fence_proxy_async();
+    for (int j = 0; j < R && j < kEstStages; ++j) {
+      const int mp = ids_s[2 * j];
+      if (mp < 0) {
+        mbar_arrive(&bars[j]);
+        continue;
+      }
+      const int row = (mp * 2) * a.P + (p_begin + j) % a.P;
+      mbar_arrive_expect_tx(&bars[j], 2 * blk);
+      tma_load_3d(stages + j * sb, mmap, 0, 0, row, &bars[j]);
+      tma_load_3d(stages + j * sb + blk, mmap, 0, 0, row + a.P, &bars[j]);
+    }
+  }
+  __syncthreads();  // the issuing thread rejoins its warp before the waits
+  for (int j = 0; j < R; ++j) {
+    const int s = j % kEstStages;
+    const int pid = ids_s[2 * j + 1];
+    const float vl =
+        (aoa && ids_s[2 * j] >= 0) ? __half2float(a.vlog[static_cast<size_t>(pid) * H + h]) : 0.f;
+    const bool arrived = mbar_wait_bounded(&bars[s], (*phase_bits >> s) & 1u, a.err);
+    *phase_bits ^= 1u << s;
+    const uint8_t* st = stages + s * sb;
+    const bool ok = arrived && ids_s[2 * j] >= 0;
+    const size_t off = (static_cast<size_t>(h) * D + lane * 8) * 2;
+    const uint4 mx = *reinterpret_cast<const uint4*>(st + off);
+    const uint4 mn = *reinterpret_cast<const uint4*>(st + blk + off);
+    uint4 sel;
+    sel.x = (mx.x & msk[0]) | (mn.x & ~msk[0]);
+    sel.y = (mx.y & msk[1]) | (mn.y & ~msk[1]);
+    sel.z = (mx.z & msk[2]) | (mn.z & ~msk[2]);
+    sel.w = (mx.w & msk[3]) | (mn.w & ~msk[3]);
+    float f[8];
+    u4_to_f8(sel, f);
+    float s0 = qv[0] * f[0], s1 = qv[1] * f[1];
+#pragma unroll
+    for (int i = 2; i < 8; i += 2) {
+      s0 = fmaf(qv[i], f[i], s0);
+      s1 = fmaf(qv[i + 1], f[i + 1], s1);
+    }
+    float sc = s0 + s1;
+#pragma unroll
+    for (int off2 = L / 2; off2 > 0; off2 >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off2);
+    if (ok && lane == 0) {
+      const float score = aoa ? a.two_rsqrt_d * sc + 2.f * vl : sc;
+      const size_t o = static_cast<size_t>(h) * a.out_stride + (p_begin + j);
+      if (a.out_f32)
+        static_cast<float*>(a.out)[o] = score;
+      else
+        static_cast<__half*>(a.out)[o] = __float2half_rn(score);
+    }
+    __syncthreads();  // stage s is free again
+    const int jn = j + kEstStages;
+    if (threadIdx.x == 0 && jn < R) {
+      fence_proxy_async();
+      const int mp = ids_s[2 * jn];
+      if (mp < 0) {
+        mbar_arrive(&bars[s]);
+      } else {
+        const int row = (mp * 2) * a.P + (p_begin + jn) % a.P;
+        mbar_arrive_expect_tx(&bars[s], 2 * blk);
+        tma_load_3d(stages + s * sb, mmap, 0, 0, row, &bars[s]);
+        tma_load_3d(stages + s * sb + blk, mmap, 0, 0, row + a.P, &bars[s]);
+      }
+    }
+    __syncwarp();
+  }
+}
+
 // Contiguous page range [*b, *e) of CTA `cta` out of `ctas` over n pages.
 __device__ __forceinline__ void page_range(int n, int cta, int ctas, int* b, int* e) {
   const int per = (n + ctas - 1) / ctas;

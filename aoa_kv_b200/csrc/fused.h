@@ -6,6 +6,8 @@
 
 namespace aoakv {
 
+constexpr int kFusedThreads = 512;  // threads per CTA of the fused step kernel
+
 struct FusedArgs {
   const __half* k_new;          // [H, D] new token
   const __half* v_new;
@@ -23,6 +25,7 @@ struct FusedArgs {
   uint32_t* sync;               // zeroed sync words, see step_fused.cu
   int32_t* selected_out;        // optional [H, sel_cols]
   int sel_cols;
+  int est_tma;                  // 1: TMA-pipelined scorer (estimate_pages_tmap)
   int* err;
   EstimateArgs est;             // out = fp32 scores [H, out_stride]
   DecodeArgs dec;               // indices = sel
@@ -33,7 +36,8 @@ struct FusedArgs {
 int fused_supported(int H, int D, int P, int n_score, int k_sel, int* grid, size_t* smem,
                     int* chunk, int* n_chunks);
 size_t fused_sync_bytes(int H);
-int launch_fused(const CUtensorMap& tmap, const FusedArgs& f, int D, int grid, size_t smem,
+int launch_fused(const CUtensorMap& tmap, const CUtensorMap& mtmap, const FusedArgs& f, int D,
+                 int grid, size_t smem,
                  cudaStream_t s);
 
 }  // namespace aoakv

@@ -173,6 +173,13 @@ extern "C" int aoakv_decode_step(
       f.selected_out = selected_out;
       f.sel_cols = k_pages;
       f.err = dev_error_ptr();
+      const int per_cta = (N - 1 + grid - 1) / grid;
+      const char* est_impl = std::getenv("AOAKV_EST_IMPL");  // "regs": A/B comparisons
+      f.est_tma = H * (D / 8) == kFusedThreads && H % 8 == 0 && per_cta <= kEstMaxRange &&
+                  reinterpret_cast<uintptr_t>(metadata_data) % 16 == 0 &&
+                  (score_mode != AOAKV_SCORE_AOAKV ||
+                   reinterpret_cast<uintptr_t>(v_log_norm) % 16 == 0) &&
+                  !(est_impl && std::strcmp(est_impl, "regs") == 0);
       EstimateArgs& ea = f.est;
       ea.q = static_cast<const __half*>(q);
       ea.meta = f.meta;
@@ -206,10 +213,16 @@ extern "C" int aoakv_decode_step(
       dd.scale_log2 = (1.f / std::sqrt(static_cast<float>(D))) * 1.4426950408889634f;
       dd.err = f.err;
       carve_decode_ws(ws + lay.dec_off, H, D, k, dd);
-      CUtensorMap tmap;
+      CUtensorMap tmap, mtmap;
       rc = make_kv_tmap(&tmap, kv_data, H, D, P, kv_capacity_pages);
       if (rc) return rc;
-      return launch_fused(tmap, f, D, grid, smem, s);
+      if (f.est_tma) {
+        rc = make_meta_tmap(&mtmap, metadata_data, H, D, P, metadata_capacity_pages);
+        if (rc) return rc;
+      } else {
+        mtmap = tmap;  // unused
+      }
+      return launch_fused(tmap, mtmap, f, D, grid, smem, s);
     }
   }
 

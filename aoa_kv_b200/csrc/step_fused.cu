@@ -4,15 +4,18 @@
 //
 //   A  CTA c < H appends head c of the new token, fused with the page's key
 //      max/min and, on page fill, its v_log_norm (decode_page.cuh:392-506).
-//   E  every CTA scores a contiguous share of the (page, head) rows
-//      (decode_attn.cuh:143-199, :263-443) into fp32 scores in the workspace
-//      and arrives on `est_done`.
+//   E  every CTA scores a contiguous page range for all heads
+//      (decode_attn.cuh:143-199, :263-443): the page's key max/min blocks
+//      stream through a TMA ring in shared memory, one thread group per
+//      head; fp32 scores go to the workspace and the CTA arrives on
+//      `est_done`.
 //   T  every CTA that owns decode units waits for all arrivals (the one
-//      grid-wide wait, bounded), then selects its head's pages itself with
-//      the shared-memory radix select (decode_select_k.cuh:25-61 semantics,
-//      exact, ties to the lower page) and keeps only the page ids of its
-//      own chunks in shared memory; the redundant selections of a head run
-//      in parallel on different SMs instead of hand-offs through flags.
+//      grid-wide wait, bounded), then selects its head's pages itself
+//      (decode_select_k.cuh:25-61 semantics, exact, ties to the lower page):
+//      a warp-register bitonic top-K for k <= 128, the shared-memory radix
+//      select above; it keeps only the page ids of its own chunks in shared
+//      memory. The redundant selections of a head run in parallel on
+//      different SMs instead of hand-offs through flags.
 //   D  each unit (head, chunk of pages) gathers its pages with TMA and
 //      merges its partial state; the last unit of a head (ticket) writes
 //      o[h] (decode_attn.cuh:469-688, :937-1047).
@@ -26,11 +29,12 @@
 #include "fused.h"
 #include "plan.h"
 #include "topk.cuh"
+#include "topk_bitonic.cuh"
 
 namespace aoakv {
 namespace {
 
-constexpr int kFThreads = 512;
+constexpr int kFThreads = kFusedThreads;
 constexpr int kFWarps = kFThreads / 32;
 constexpr int kFMaxWin = 64;                 // selected slots one CTA may own
 constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s
@@ -45,6 +49,21 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+
+#ifdef AOAKV_PHASE_PROBE
+// Development builds with -DAOAKV_PHASE_PROBE record, per CTA, %globaltimer
+// at each phase boundary (8 slots per CTA); the library build compiles the
+// stamps out.
+__device__ uint64_t g_phase_ns[2048 * 8];
+#define AOAKV_STAMP(i)                                                    \
+  do {                                                                    \
+    if (threadIdx.x == 0) g_phase_ns[blockIdx.x * 8 + (i)] = global_ns(); \
+  } while (0)
+#else
+#define AOAKV_STAMP(i) \
+  do {                 \
+  } while (0)
+#endif
 
 // Thread 0 spins until *p >= target or the time limit; the result is
 // broadcast through *ok_s. Returns false on timeout (error recorded).
@@ -71,12 +90,17 @@ __device__ __forceinline__ bool cta_wait_geq(const uint32_t* p, uint32_t target,
   return *ok_s != 0;
 }
 
+__host__ __device__ inline int fused_xbuf_offset(int n_score) { return (n_score + 3) / 4 * 16; }
+
 __host__ __device__ inline int fused_smem_bytes(int H, int D, int P, int n_score, int chunk) {
   const int q_bytes = H * D * 4;  // generic estimate path only
-  const int keys_bytes = n_score * 4;
+  const int keys_bytes =
+      fused_xbuf_offset(n_score) + static_cast<int>(bitonic_xbuf_bytes(kFWarps, kBitonicMaxK));
   const int dec_bytes = static_cast<int>(dec_smem_bytes(D, P, chunk, kFWarps));
+  const int est_bytes = kEstStages * est_stage_bytes(H, D);
   int m = q_bytes > keys_bytes ? q_bytes : keys_bytes;
   if (dec_bytes > m) m = dec_bytes;
+  if (est_bytes > m) m = est_bytes;
   return m + 128;  // + alignment slack for the TMA tiles
 }
 
@@ -84,7 +108,8 @@ __host__ __device__ inline int fused_smem_bytes(int H, int D, int P, int n_score
 // end at min(u_end, next head's first unit).
 template <int D>
 __global__ void __launch_bounds__(kFThreads, 2)
-    fused_step_kernel(const __grid_constant__ CUtensorMap tmap, FusedArgs f) {
+    fused_step_kernel(const __grid_constant__ CUtensorMap tmap,
+                      const __grid_constant__ CUtensorMap mtmap, FusedArgs f) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
@@ -93,15 +118,20 @@ __global__ void __launch_bounds__(kFThreads, 2)
   __shared__ uint64_t bars[kDecMaxChunk];
   __shared__ int tok_s[kDecMaxChunk];
   __shared__ int win_s[kFMaxWin];
+  __shared__ uint64_t ebars[kEstStages];
+  __shared__ int ids_s[2 * kEstMaxRange];
 
   const int G = gridDim.x, b = blockIdx.x, H = f.H, P = f.P;
   uint32_t* est_done = f.sync;
   uint32_t* passed = f.sync + 1;
 
+  AOAKV_STAMP(0);
   if (threadIdx.x == 0) {
     for (int j = 0; j < kDecMaxChunk; ++j) mbar_init(&bars[j], 1);
+    for (int j = 0; j < kEstStages; ++j) mbar_init(&ebars[j], 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmap);
+    if (f.est_tma) tma_prefetch_desc(&mtmap);
   }
 
   // ---- A: append head b of the new token (warp 0, D/8 lanes)
@@ -184,7 +214,13 @@ __global__ void __launch_bounds__(kFThreads, 2)
   }
 
   // ---- E: score this CTA's share of the (page, head) rows
-  if (H * (D / 8) == kFThreads) {  // head-stationary: one thread per (head, 8 channels)
+  if (f.est_tma) {  // TMA boxes of whole page blocks through a 4-stage ring
+    int pb, pe;
+    page_range(f.est.n_score, b, G, &pb, &pe);
+    __syncthreads();  // mbarrier initialisation visible to every thread
+    uint32_t ephase = 0;
+    estimate_pages_tmap<D>(f.est, &mtmap, pb, pe, smem, ebars, ids_s, &ephase);
+  } else if (H * (D / 8) == kFThreads) {  // head-stationary, loads into registers
     int pb, pe;
     page_range(f.est.n_score, b, G, &pb, &pe);
     estimate_pages_hs<D, 4>(f.est, pb, pe);
@@ -197,6 +233,7 @@ __global__ void __launch_bounds__(kFThreads, 2)
                                   f.est.n_score * H);
   }
   __syncthreads();
+  AOAKV_STAMP(1);
   if (threadIdx.x == 0) {
     __threadfence();
     atomicAdd(est_done, 1u);
@@ -204,6 +241,7 @@ __global__ void __launch_bounds__(kFThreads, 2)
 
   // ---- T: wait for every CTA's scores, then re-arm the counters
   if (!cta_wait_geq(est_done, static_cast<uint32_t>(G), &ok_s, f.err)) return;
+  AOAKV_STAMP(2);
   if (threadIdx.x == 0 && atomicAdd(passed, 1u) == static_cast<uint32_t>(G - 1)) {
     *est_done = 0u;  // every CTA has passed its wait
     *passed = 0u;
@@ -240,18 +278,25 @@ __global__ void __launch_bounds__(kFThreads, 2)
       ta.n = f.est.n_score;
       ta.k = f.k_sel;
       ta.sink = f.sink;
-      topk_row_cg(ta, h, keys, tsm, win_s, win_lo, win_hi);
+      if (f.k_sel <= 128)  // register budget of the 2-CTA/SM kernel: K <= 128 here
+        topk_row_small<true, 4>(ta, h, keys,
+                             reinterpret_cast<uint64_t*>(smem + fused_xbuf_offset(ta.n)), win_s,
+                             win_lo, win_hi);
+      else
+        topk_row_cg(ta, h, keys, tsm, win_s, win_lo, win_hi);
       if (full_row)  // the last page after the selection, -1 padding
         for (int i = f.k_sel + threadIdx.x; i < f.sel_cols; i += blockDim.x)
           f.selected_out[static_cast<size_t>(h) * f.sel_cols + i] =
               i == f.k_sel ? __ldg(f.kv_indices + f.n_pages - 1) : -1;
       __syncthreads();
+      AOAKV_STAMP(3);
     }
     if (threadIdx.x == 0)  // (issues a proxy fence: appended page -> TMA reads)
       decode_issue(f.dec, &tmap, h, c, bars, tok_s, tiles, D, win_s, win_lo);
     __syncthreads();
     decode_compute_multi<D, kFWarps>(f.dec, h, c, bars, tok_s, tiles, mrg, &flag_s,
                                      phase_bits, nullptr);
+    AOAKV_STAMP(4);
     const int ns = min(f.dec.n_sel + 1, (c + 1) * C) - c * C;
     for (int j = 0; j < ns; ++j)
       if (tok_s[j] > 0) phase_bits ^= 1u << j;
@@ -297,7 +342,8 @@ int fused_supported(int H, int D, int P, int n_score, int k_sel, int* grid_out,
 
 size_t fused_sync_bytes(int H) { return ((2 + 2 * static_cast<size_t>(H)) * 4 + 255) / 256 * 256; }
 
-int launch_fused(const CUtensorMap& tmap, const FusedArgs& f, int D, int grid, size_t smem,
+int launch_fused(const CUtensorMap& tmap, const CUtensorMap& mtmap, const FusedArgs& f, int D,
+                 int grid, size_t smem,
                  cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -310,10 +356,20 @@ int launch_fused(const CUtensorMap& tmap, const FusedArgs& f, int D, int grid, s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (D == 128)
-    AOAKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, fused_step_kernel<128>, tmap, f), "fused step launch");
+    AOAKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, fused_step_kernel<128>, tmap, mtmap, f), "fused step launch");
   else
-    AOAKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, fused_step_kernel<64>, tmap, f), "fused step launch");
+    AOAKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, fused_step_kernel<64>, tmap, mtmap, f), "fused step launch");
   return AOAKV_OK;
 }
 
 }  // namespace aoakv
+
+#ifdef AOAKV_PHASE_PROBE
+extern "C" __attribute__((visibility("default"))) int aoakv_probe_phase_ns(uint64_t* host,
+                                                                           int n) {
+  return cudaMemcpyFromSymbol(host, aoakv::g_phase_ns, static_cast<size_t>(n) * 8) ==
+                 cudaSuccess
+             ? 0
+             : 3;
+}
+#endif

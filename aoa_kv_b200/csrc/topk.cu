@@ -1,9 +1,17 @@
 // a4 stand-alone entry point: aoakv_topk_filtering.
+//
+// k <= 256: warp-register bitonic top-K (topk_bitonic.cuh), 512 threads per
+// row, results in descending score order. k > 256: shared-memory radix
+// select (topk.cuh), 1024 threads per row, results in ascending position
+// order.
 #include "plan.h"
 #include "topk.cuh"
+#include "topk_bitonic.cuh"
 
 namespace aoakv {
 namespace {
+
+constexpr int kSmallThreads = 512;
 
 __global__ void __launch_bounds__(kTopkThreads) topk_kernel(TopkArgs a) {
   extern __shared__ uint32_t keys[];
@@ -12,18 +20,30 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(TopkArgs a) {
   topk_row(a, blockIdx.x, keys, sm);
 }
 
+__global__ void __launch_bounds__(kSmallThreads, 1) topk_small_kernel(TopkArgs a) {
+  extern __shared__ uint32_t keys[];
+  uint64_t* xbuf = reinterpret_cast<uint64_t*>(keys + (a.n + 3) / 4 * 4);
+  pdl_wait();
+  topk_row_small(a, blockIdx.x, keys, xbuf);
+}
+
 }  // namespace
 
 int launch_topk(const TopkArgs& a, int rows, cudaStream_t s, bool pdl) {
-  const size_t smem = static_cast<size_t>(a.n) * sizeof(uint32_t);
+  const bool small = a.k <= kBitonicMaxK;
+  const void* fn = small ? reinterpret_cast<const void*>(topk_small_kernel)
+                         : reinterpret_cast<const void*>(topk_kernel);
+  size_t smem = static_cast<size_t>(a.n) * sizeof(uint32_t);
+  if (small)
+    smem = static_cast<size_t>((a.n + 3) / 4 * 4) * 4 +
+           bitonic_xbuf_bytes(kSmallThreads / 32, kBitonicMaxK);
   if (smem > 48 * 1024)
-    AOAKV_CUDA_TRY(cudaFuncSetAttribute(topk_kernel,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+    AOAKV_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(smem)),
                    "topk smem attribute");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(rows);
-  cfg.blockDim = dim3(kTopkThreads);
+  cfg.blockDim = dim3(small ? kSmallThreads : kTopkThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -31,7 +51,10 @@ int launch_topk(const TopkArgs& a, int rows, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  AOAKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, topk_kernel, a), "topk launch");
+  if (small)
+    AOAKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, topk_small_kernel, a), "topk launch");
+  else
+    AOAKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, topk_kernel, a), "topk launch");
   return AOAKV_OK;
 }
 

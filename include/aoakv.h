@@ -136,9 +136,11 @@ AOAKV_API int aoakv_estimate_attn_score(
  *    RAFT radix_topk_one_block_kernel).
  * For each of num_rows rows selects the k largest of num_pages scores
  * (scores_dtype f16 or f32). Ties break toward the lower position; NaN
- * ranks below every number. With sink_first_page != 0 position 0 is always
- * selected (the simulation's fixed sink page) and the other k-1 come from
- * positions 1..num_pages-1. Results are written in ascending position order:
+ * ranks below every number; -0 equals +0. With sink_first_page != 0
+ * position 0 is always selected (the simulation's fixed sink page) and the
+ * other k-1 come from positions 1..num_pages-1. Output order: descending
+ * score (ties: lower position first) for k <= 256, ascending position for
+ * larger k (the reference's order is unspecified):
  *   out_indices[r*out_indices_row_stride + i] = in_indices[r*in_row_stride + pos]
  *   (pos itself when in_indices is NULL; in_row_stride may be 0 to share
  *    one index row), out_values likewise (may be NULL; same dtype as

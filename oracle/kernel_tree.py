@@ -120,17 +120,29 @@ def estimate(q: np.ndarray, c: LayerCache, meta_indices: np.ndarray, kv_indices:
     return (F32(2.0 / math.sqrt(D)) * s + F32(2) * vl).astype(F32)
 
 
+BITONIC_MAX_K = 256
+
+
 def topk_positions(scores: np.ndarray, k: int, sink: bool = False) -> np.ndarray:
     """The library's exact selection rule (the reference's RAFT radix select,
     decode_select_k.cuh:25-61, leaves ties and order unspecified): the k
-    largest per row, ties toward the lower position, NaN lowest; with sink,
-    position 0 always plus the k-1 largest of the rest. Ascending, [H, k]."""
-    s = np.where(np.isnan(scores), -np.inf, scores).astype(np.float64)
+    largest per row, ties toward the lower position, NaN lowest, -0 == +0;
+    with sink, position 0 always plus the k-1 largest of the rest. Output
+    order as the library writes it: descending score (ties: lower position
+    first) for k <= 256, ascending position above. [H, k]."""
+    f = np.ascontiguousarray(scores, dtype=np.float32)
+    u = f.view(np.uint32).astype(np.uint64)
+    u = np.where(u == 0x80000000, 0, u)  # -0 == +0
+    key = np.where(u & 0x80000000, ~u & 0xFFFFFFFF, u | 0x80000000)  # order-preserving
+    key = np.where(np.isnan(f), 0, key)  # NaN below -inf
     if sink:
-        s = s.copy()
-        s[:, 0] = np.inf
-    order = np.argsort(-s, axis=-1, kind="stable")[:, :k]
-    return np.sort(order, axis=-1)
+        key[:, 0] = 0xFFFFFFFF
+    n = f.shape[-1]
+    comp = (key << np.uint64(32)) | (~np.arange(n, dtype=np.uint64) & np.uint64(0xFFFFFFFF))
+    order = np.argsort(comp, axis=-1)[:, ::-1][:, :k]  # composite keys are distinct
+    if k > BITONIC_MAX_K:
+        order = np.sort(order, axis=-1)
+    return np.ascontiguousarray(order)
 
 
 def sparse_decode(q: np.ndarray, c: LayerCache, indices: np.ndarray, last_page: int,

@@ -124,10 +124,15 @@ def test_sink_mode_kernel_tree_agrees_with_simulation():
 
 def test_topk_positions_rules():
     s = np.array([[1.0, 5.0, 5.0, 3.0, np.nan, 5.0]], np.float32)
-    assert kt.topk_positions(s, 2).tolist() == [[1, 2]]          # ties -> lower position
-    assert kt.topk_positions(s, 5).tolist() == [[0, 1, 2, 3, 5]]  # NaN ranks last
+    # descending score, ties -> lower position first, NaN last
+    assert kt.topk_positions(s, 2).tolist() == [[1, 2]]
+    assert kt.topk_positions(s, 5).tolist() == [[1, 2, 5, 3, 0]]
     assert kt.topk_positions(s, 2, sink=True).tolist() == [[0, 1]]
-    assert kt.topk_positions(s, 6).tolist() == [[0, 1, 2, 3, 4, 5]]
+    assert kt.topk_positions(s, 6).tolist() == [[1, 2, 5, 3, 0, 4]]
+    z = np.array([[-0.0, 0.0, 1.0]], np.float32)  # -0 == +0: the lower position wins
+    assert kt.topk_positions(z, 2).tolist() == [[2, 0]]
+    big = np.arange(300, dtype=np.float32)[None]  # k > 256: ascending positions
+    assert kt.topk_positions(big, 257).tolist() == [list(range(43, 300))]
 
 
 def test_sim_budget_rule():
