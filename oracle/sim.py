@@ -10,7 +10,7 @@ logsumexp at filter_util.py:352-361 is the identity):
 All arithmetic is float32, as the simulation runs on the CPU (fp16 inputs are
 upcast). Page ids are logical (0 .. N-1).
 
-Each function cites the file:line of /root/reference it restates
+Each function cites the file:line of the reference checkout it restates
 (filtering/filter_util.py = "fu", evaluation/quest_attention.py = "qa").
 """
 from __future__ import annotations

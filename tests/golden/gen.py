@@ -4,7 +4,7 @@ Inputs are regenerated from (seed, shape, distribution) with numpy's PCG64
 generator and rounded to fp16, so fixtures store only outputs plus a SHA-256
 of the inputs (a test fails loudly if regeneration ever diverges).
 
-Distributions:
+Distributions (the benchmark configurations):
   "normal"  : q, K, V ~ N(0, 1)                                  (config 1)
   "outlier" : K = N(0, 1) * s[h, d], s ~ LogNormal(0, 1) per channel; q, V
               ~ N(0, 1)                                          (config 2)

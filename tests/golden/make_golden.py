@@ -1,7 +1,7 @@
 """Writes the golden vectors in tests/golden/*.npz from the reference's OWN code.
 
-Run where the reference checkout exists (default /root/reference, override
-with AOAKV_REFERENCE):  python tests/golden/make_golden.py
+Run where the reference checkout exists (its path in AOAKV_REFERENCE, or the
+built-in default):  python tests/golden/make_golden.py
 
 Semantics A (``sim_*.npz``): the reference simulation — the real
 filtering/filter_util.py functions (imported, not copied) driven by the decode
