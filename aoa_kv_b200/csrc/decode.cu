@@ -176,14 +176,16 @@ extern "C" int aoakv_decode_workspace_size(int32_t num_heads, int32_t head_dim,
   return AOAKV_OK;
 }
 
-extern "C" int aoakv_sparse_decode(const void* q, void* o, const void* kv_data,
-                                   int32_t kv_capacity_pages, const int32_t* indices,
-                                   int64_t indices_row_stride, int32_t num_selected,
-                                   int32_t last_page_idx, int32_t last_page_len,
-                                   int32_t num_heads, int32_t head_dim, int32_t page_size,
-                                   int32_t layout, float sm_scale, void* workspace,
-                                   size_t workspace_bytes, void* stream) {
-  AOAKV_CHECK_ARG(q && o && kv_data, "decode: NULL pointer argument");
+namespace {
+
+// Shared body of aoakv_sparse_decode (fp16 o) and aoakv_sparse_decode_partial
+// (fp32 o plus lse; last_page_idx -1 = no last page on this shard).
+int sparse_decode_impl(const void* q, void* o, float* o_f32, float* lse, const void* kv_data,
+                       int32_t kv_capacity_pages, const int32_t* indices,
+                       int64_t indices_row_stride, int32_t num_selected, int32_t last_page_idx,
+                       int32_t last_page_len, int32_t num_heads, int32_t head_dim,
+                       int32_t page_size, int32_t layout, float sm_scale, void* workspace,
+                       size_t workspace_bytes, void* stream, bool allow_no_last) {
   int rc = check_decode_shape(num_heads, head_dim, page_size, kv_capacity_pages, layout);
   if (rc) return rc;
   AOAKV_CHECK_ARG(num_selected >= 0, "decode: num_selected must be >= 0");
@@ -192,13 +194,16 @@ extern "C" int aoakv_sparse_decode(const void* q, void* o, const void* kv_data,
                   "decode: indices_row_stride must be 0 or >= num_selected");
   AOAKV_CHECK_ARG(last_page_len >= 1 && last_page_len <= page_size,
                   "decode: last_page_len must be in [1, page_size]");
-  AOAKV_CHECK_ARG(last_page_idx >= 0 && last_page_idx < kv_capacity_pages,
+  AOAKV_CHECK_ARG((last_page_idx >= 0 && last_page_idx < kv_capacity_pages) ||
+                      (allow_no_last && last_page_idx == -1),
                   "decode: last_page_idx out of range");
   const int n_slots = num_selected + 1;
   DecodePlan pl = plan_decode(num_heads, n_slots, head_dim, page_size);
   DecodeArgs a = {};
   a.q = static_cast<const __half*>(q);
   a.o = static_cast<__half*>(o);
+  a.o_f32 = o_f32;
+  a.lse = lse;
   a.indices = indices;
   a.idx_stride = indices_row_stride;
   a.n_sel = num_selected;
@@ -226,4 +231,33 @@ extern "C" int aoakv_sparse_decode(const void* q, void* o, const void* kv_data,
   rc = make_kv_tmap(&tmap, kv_data, num_heads, head_dim, page_size, kv_capacity_pages);
   if (rc) return rc;
   return launch_decode(a, tmap, head_dim, pl, static_cast<cudaStream_t>(stream), false);
+}
+
+}  // namespace
+
+extern "C" int aoakv_sparse_decode(const void* q, void* o, const void* kv_data,
+                                   int32_t kv_capacity_pages, const int32_t* indices,
+                                   int64_t indices_row_stride, int32_t num_selected,
+                                   int32_t last_page_idx, int32_t last_page_len,
+                                   int32_t num_heads, int32_t head_dim, int32_t page_size,
+                                   int32_t layout, float sm_scale, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  AOAKV_CHECK_ARG(q && o && kv_data, "decode: NULL pointer argument");
+  return sparse_decode_impl(q, o, nullptr, nullptr, kv_data, kv_capacity_pages, indices,
+                            indices_row_stride, num_selected, last_page_idx, last_page_len,
+                            num_heads, head_dim, page_size, layout, sm_scale, workspace,
+                            workspace_bytes, stream, false);
+}
+
+extern "C" int aoakv_sparse_decode_partial(
+    const void* q, float* o_partial, float* lse, const void* kv_data, int32_t kv_capacity_pages,
+    const int32_t* indices, int64_t indices_row_stride, int32_t num_selected,
+    int32_t last_page_idx, int32_t last_page_len, int32_t num_heads, int32_t head_dim,
+    int32_t page_size, int32_t layout, float sm_scale, void* workspace, size_t workspace_bytes,
+    void* stream) {
+  AOAKV_CHECK_ARG(q && o_partial && lse && kv_data, "decode_partial: NULL pointer argument");
+  return sparse_decode_impl(q, nullptr, o_partial, lse, kv_data, kv_capacity_pages, indices,
+                            indices_row_stride, num_selected, last_page_idx, last_page_len,
+                            num_heads, head_dim, page_size, layout, sm_scale, workspace,
+                            workspace_bytes, stream, true);
 }

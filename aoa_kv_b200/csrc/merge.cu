@@ -1,0 +1,57 @@
+// Log-sum-exp merge of partial decode states: aoakv_merge_states.
+//
+// Reference: the split-KV merge FlashInfer's VariableLengthMergeStates runs
+// after BatchDecodeWithPagedKVCacheKernel (call site decode_attn.cuh:1035-1043),
+// restated from its definition. For head h over parts g with partial output
+// o_g (already normalised by its own softmax denominator) and
+// lse_g = ln(sum of exp(scores)) of that part:
+//   m = max_g lse_g,  w_g = exp(lse_g - m),
+//   o = sum_g w_g o_g / sum_g w_g,  lse = m + ln(sum_g w_g).
+// A part with lse = -inf (no tokens) contributes nothing; a head with no
+// tokens in any part gets o = 0 and lse = -inf. Used by the page-range
+// sharded step, where each GPU decodes the selected pages it owns.
+#include <cmath>
+
+#include "common.cuh"
+
+namespace aoakv {
+namespace {
+
+__global__ void merge_states_kernel(const float* o_parts, const float* lse_parts, int G, int H,
+                                    int D, __half* o, float* lse_out) {
+  const int h = blockIdx.x;
+  float m = -INFINITY;
+  for (int g = 0; g < G; ++g) m = fmaxf(m, lse_parts[static_cast<size_t>(g) * H + h]);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f, sum = 0.f;
+    if (m != -INFINITY) {
+      for (int g = 0; g < G; ++g) {
+        const float l = lse_parts[static_cast<size_t>(g) * H + h];
+        if (l == -INFINITY) continue;
+        const float w = expf(l - m);
+        sum += w;
+        acc += w * o_parts[(static_cast<size_t>(g) * H + h) * D + d];
+      }
+    }
+    o[static_cast<size_t>(h) * D + d] = __float2half_rn(sum > 0.f ? acc / sum : 0.f);
+    if (lse_out && d == 0) lse_out[h] = sum > 0.f ? m + logf(sum) : -INFINITY;
+  }
+}
+
+}  // namespace
+}  // namespace aoakv
+
+using namespace aoakv;
+
+extern "C" int aoakv_merge_states(const float* o_parts, const float* lse_parts,
+                                  int32_t num_parts, int32_t num_heads, int32_t head_dim,
+                                  void* o, float* lse_out, void* stream) {
+  AOAKV_CHECK_ARG(o_parts && lse_parts && o, "merge_states: NULL pointer argument");
+  AOAKV_CHECK_ARG(num_parts >= 1 && num_heads >= 1 && head_dim >= 1 && head_dim <= 1024,
+                  "merge_states: bad sizes");
+  const int threads = head_dim < 128 ? ((head_dim + 31) / 32) * 32 : 128;
+  merge_states_kernel<<<num_heads, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      o_parts, lse_parts, num_parts, num_heads, head_dim, static_cast<__half*>(o), lse_out);
+  AOAKV_CUDA_TRY(cudaGetLastError(), "merge_states launch");
+  return AOAKV_OK;
+}

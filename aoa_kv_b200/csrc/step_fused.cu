@@ -12,10 +12,11 @@
 //   T  every CTA that owns decode units waits for all arrivals (the one
 //      grid-wide wait, bounded), then selects its head's pages itself
 //      (decode_select_k.cuh:25-61 semantics, exact, ties to the lower page):
-//      a warp-register bitonic top-K for k <= 128, the shared-memory radix
-//      select above; it keeps only the page ids of its own chunks in shared
-//      memory. The redundant selections of a head run in parallel on
-//      different SMs instead of hand-offs through flags.
+//      one histogram pass plus exact ranking of the candidates; when many
+//      scores are equal, a warp-register bitonic top-K for k <= 128 or the
+//      shared-memory radix select above. It keeps only the page ids of its
+//      own chunks in shared memory. The redundant selections of a head run
+//      in parallel on different SMs instead of hand-offs through flags.
 //   D  each unit (head, chunk of pages) gathers its pages with TMA and
 //      merges its partial state; the last unit of a head (ticket) writes
 //      o[h] (decode_attn.cuh:469-688, :937-1047).
@@ -30,6 +31,30 @@
 #include "plan.h"
 #include "topk.cuh"
 #include "topk_bitonic.cuh"
+
+#ifdef AOAKV_PHASE_PROBE
+// Development builds with -DAOAKV_PHASE_PROBE record, per CTA, %globaltimer
+// at each phase boundary (8 slots per CTA); the library build compiles the
+// stamps out.
+namespace aoakv {
+__device__ uint64_t g_phase_ns[2048 * 8];
+__device__ __forceinline__ uint64_t probe_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+}  // namespace aoakv
+#define AOAKV_STAMP(i)                                                   \
+  do {                                                                   \
+    if (threadIdx.x == 0) g_phase_ns[blockIdx.x * 8 + (i)] = probe_ns(); \
+  } while (0)
+#else
+#define AOAKV_STAMP(i) \
+  do {                 \
+  } while (0)
+#endif
+#define AOAKV_TOPK_STAMP(i) AOAKV_STAMP(i)
+#include "topk_hist.cuh"
 
 namespace aoakv {
 namespace {
@@ -49,21 +74,6 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-
-#ifdef AOAKV_PHASE_PROBE
-// Development builds with -DAOAKV_PHASE_PROBE record, per CTA, %globaltimer
-// at each phase boundary (8 slots per CTA); the library build compiles the
-// stamps out.
-__device__ uint64_t g_phase_ns[2048 * 8];
-#define AOAKV_STAMP(i)                                                    \
-  do {                                                                    \
-    if (threadIdx.x == 0) g_phase_ns[blockIdx.x * 8 + (i)] = global_ns(); \
-  } while (0)
-#else
-#define AOAKV_STAMP(i) \
-  do {                 \
-  } while (0)
-#endif
 
 // Thread 0 spins until *p >= target or the time limit; the result is
 // broadcast through *ok_s. Returns false on timeout (error recorded).
@@ -94,8 +104,9 @@ __host__ __device__ inline int fused_xbuf_offset(int n_score) { return (n_score 
 
 __host__ __device__ inline int fused_smem_bytes(int H, int D, int P, int n_score, int chunk) {
   const int q_bytes = H * D * 4;  // generic estimate path only
-  const int keys_bytes =
-      fused_xbuf_offset(n_score) + static_cast<int>(bitonic_xbuf_bytes(kFWarps, kBitonicMaxK));
+  const int xb = static_cast<int>(bitonic_xbuf_bytes(kFWarps, kBitonicMaxK));
+  const int hb = static_cast<int>(sizeof(HistSmem));
+  const int keys_bytes = fused_xbuf_offset(n_score) + (xb > hb ? xb : hb);
   const int dec_bytes = static_cast<int>(dec_smem_bytes(D, P, chunk, kFWarps));
   const int est_bytes = kEstStages * est_stage_bytes(H, D);
   int m = q_bytes > keys_bytes ? q_bytes : keys_bytes;
@@ -278,12 +289,15 @@ __global__ void __launch_bounds__(kFThreads, 2)
       ta.n = f.est.n_score;
       ta.k = f.k_sel;
       ta.sink = f.sink;
-      if (f.k_sel <= 128)  // register budget of the 2-CTA/SM kernel: K <= 128 here
-        topk_row_small<true, 4>(ta, h, keys,
-                             reinterpret_cast<uint64_t*>(smem + fused_xbuf_offset(ta.n)), win_s,
-                             win_lo, win_hi);
-      else
-        topk_row_cg(ta, h, keys, tsm, win_s, win_lo, win_hi);
+      uint8_t* un = smem + fused_xbuf_offset(ta.n);
+      if (!topk_row_hist<true>(ta, h, keys, *reinterpret_cast<HistSmem*>(un), win_s, win_lo,
+                               win_hi)) {  // many equal scores: exact fallbacks
+        if (f.k_sel <= 128)  // register budget of the 2-CTA/SM kernel: K <= 128 here
+          topk_row_small<true, 4>(ta, h, keys, reinterpret_cast<uint64_t*>(un), win_s, win_lo,
+                                  win_hi);
+        else
+          topk_row_cg(ta, h, keys, tsm, win_s, win_lo, win_hi);
+      }
       if (full_row)  // the last page after the selection, -1 padding
         for (int i = f.k_sel + threadIdx.x; i < f.sel_cols; i += blockDim.x)
           f.selected_out[static_cast<size_t>(h) * f.sel_cols + i] =

@@ -1,12 +1,14 @@
 // a4 stand-alone entry point: aoakv_topk_filtering.
 //
-// k <= 256: warp-register bitonic top-K (topk_bitonic.cuh), 512 threads per
-// row, results in descending score order. k > 256: shared-memory radix
-// select (topk.cuh), 1024 threads per row, results in ascending position
-// order.
+// k <= 256: one histogram pass and exact candidate ranking (topk_hist.cuh),
+// or, when too many keys share the top bins, the warp-register bitonic
+// top-K (topk_bitonic.cuh); 512 threads per row, results in descending score
+// order either way. k > 256: shared-memory radix select (topk.cuh), 1024
+// threads per row, results in ascending position order.
 #include "plan.h"
 #include "topk.cuh"
 #include "topk_bitonic.cuh"
+#include "topk_hist.cuh"
 
 namespace aoakv {
 namespace {
@@ -20,11 +22,18 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(TopkArgs a) {
   topk_row(a, blockIdx.x, keys, sm);
 }
 
+// Dynamic shared memory: keys, then one region used either as the
+// histogram state or, on the fallback, as the bitonic exchange buffer.
+constexpr size_t kSmallUnion = sizeof(HistSmem) > bitonic_xbuf_bytes(kSmallThreads / 32, kBitonicMaxK)
+                                   ? sizeof(HistSmem)
+                                   : bitonic_xbuf_bytes(kSmallThreads / 32, kBitonicMaxK);
+
 __global__ void __launch_bounds__(kSmallThreads, 1) topk_small_kernel(TopkArgs a) {
   extern __shared__ uint32_t keys[];
-  uint64_t* xbuf = reinterpret_cast<uint64_t*>(keys + (a.n + 3) / 4 * 4);
+  uint8_t* un = reinterpret_cast<uint8_t*>(keys + (a.n + 3) / 4 * 4);
   pdl_wait();
-  topk_row_small(a, blockIdx.x, keys, xbuf);
+  if (!topk_row_hist(a, blockIdx.x, keys, *reinterpret_cast<HistSmem*>(un)))
+    topk_row_small(a, blockIdx.x, keys, reinterpret_cast<uint64_t*>(un));
 }
 
 }  // namespace
@@ -35,8 +44,7 @@ int launch_topk(const TopkArgs& a, int rows, cudaStream_t s, bool pdl) {
                          : reinterpret_cast<const void*>(topk_kernel);
   size_t smem = static_cast<size_t>(a.n) * sizeof(uint32_t);
   if (small)
-    smem = static_cast<size_t>((a.n + 3) / 4 * 4) * 4 +
-           bitonic_xbuf_bytes(kSmallThreads / 32, kBitonicMaxK);
+    smem = static_cast<size_t>((a.n + 3) / 4 * 4) * 4 + kSmallUnion;
   if (smem > 48 * 1024)
     AOAKV_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(smem)),

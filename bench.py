@@ -16,11 +16,14 @@ and runs estimate -> top-k -> sparse decode. The 32 layers touch
             CUDA-graph replays of the 32-layer step / (K * 32 * n_gpus)
   e2e       the same through InferenceController.decode_step with q, k, v
             copied from pinned host memory and o copied back every layer
-  roofline  the dominant kernel (page-score estimate) timed alone with CUDA
-            events: algorithmic bytes per launch / average launch time
+  roofline  the step kernel (one fused launch per layer): algorithmic bytes
+            of a layer-step / its average duration inside the timed graph;
+            estimate_roofline: the stand-alone page scorer timed the same way
 
 With --gpus N (torchrun, one process per GPU) every rank serves its own
 request (request sharding, no collective): scaling "weak".
+--mode longctx instead splits ONE 128K-context request (budget 4096) by page
+range over the GPUs, with two NCCL all_gathers per layer: scaling "strong".
 --impl reference times the reference's CPU simulation path (the numpy port
 in oracle/sim.py of filter_util.py + quest_attention.py) on the host cores.
 """
@@ -50,9 +53,13 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--layers", type=int, default=32)
-    ap.add_argument("--ctx", type=int, default=32768)
-    ap.add_argument("--budget", type=int, default=1024, help="token budget")
+    ap.add_argument("--mode", choices=["headline", "longctx"], default="headline",
+                    help="headline: 32K ctx, 1K budget, one request per GPU; longctx: one "
+                         "128K-context request split by page range over the GPUs")
+    ap.add_argument("--layers", type=int, default=None, help="default 32 (headline), 4 (longctx)")
+    ap.add_argument("--ctx", type=int, default=None, help="default 32768 (headline), 131072 (longctx)")
+    ap.add_argument("--budget", type=int, default=None,
+                    help="token budget; default 1024 (headline), 4096 (longctx)")
     ap.add_argument("--method", choices=["aoakv", "quest"], default="aoakv")
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -61,7 +68,13 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--soak-seconds", type=float, default=1.0,
                     help="graph replays before the timed region so the clock sampler sees load")
-    return ap.parse_args()
+    ap.add_argument("--no-graph", action="store_true", help="longctx: launch without a CUDA graph")
+    a = ap.parse_args()
+    long = a.mode == "longctx"
+    a.layers = a.layers or (4 if long else 32)
+    a.ctx = a.ctx or (131072 if long else 32768)
+    a.budget = a.budget or (4096 if long else 1024)
+    return a
 
 
 def workload_config(a, n_gpus):
@@ -458,10 +471,158 @@ def run_ours(a):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------ long context, sharded
+LONG_METRIC = "sparse-decode µs/layer @128K ctx, 4K budget, page-range sharded"
+
+
+class _SoloGroup:
+    """The all_gather of a one-rank job."""
+
+    @staticmethod
+    def all_gather_stack(t):
+        return t.unsqueeze(0)
+
+
+def run_longctx(a):
+    """One request of a.ctx tokens split by page range over the job's GPUs
+    (aoa_kv_b200.sharded): per layer, the last rank appends, every rank
+    scores and proposes its top-(k-1), all_gather, global top-(k-1), partial
+    decode of the owned pages, all_gather, LSE merge. Strong scaling: the
+    total work is one request whatever the GPU count."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from aoa_kv_b200 import _lib, sharded
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        group = dist.group.WORLD
+    else:
+        group = _SoloGroup()
+    _lib.load()
+    S = a.ctx
+    n_total, last_len = S // P + 1, S % P + 1
+    lo, hi = sharded.partition_pages(n_total, world, P)[rank]
+    n_local = hi - lo
+    owns = rank == world - 1
+    cap = n_local + 1
+    mcap = -(-cap // P)
+    layers, news = [], []
+    for layer in range(a.layers):
+        g_layer = torch.Generator(device=dev).manual_seed(a.seed * 1000 + layer)
+        scale = torch.exp(torch.randn(H, D, device=dev, generator=g_layer))
+        q = torch.randn(H, D, device=dev, generator=g_layer).half()
+        k_new = (torch.randn(H, D, device=dev, generator=g_layer) * scale).half()
+        v_new = torch.randn(H, D, device=dev, generator=g_layer).half()
+        g_rank = torch.Generator(device=dev).manual_seed(a.seed * 100000 + layer * 100 + rank)
+        kv = torch.empty(cap, 2, P, H, D, dtype=torch.float16, device=dev)
+        meta = torch.empty(mcap, 2, P, H, D, dtype=torch.float16, device=dev)
+        vlog = torch.zeros(cap, H, dtype=torch.float16, device=dev)
+        kv_idx = torch.arange(n_local, dtype=torch.int32, device=dev)
+        meta_idx = torch.arange(mcap, dtype=torch.int32, device=dev)
+        t0, t1 = lo * P, min(hi * P, S)
+        if t1 > t0:
+            Kc = (torch.randn(t1 - t0, H, D, device=dev, generator=g_rank) * scale).half()
+            Vc = torch.randn(t1 - t0, H, D, device=dev, generator=g_rank).half()
+            n_pref = -(-(t1 - t0) // P)
+            _lib.call("aoakv_append_kv_cache_prefill", Kc.data_ptr(), Vc.data_ptr(), t1 - t0,
+                      kv.data_ptr(), kv_idx.data_ptr(), n_pref, (t1 - t0 - 1) % P + 1, cap,
+                      meta.data_ptr(), meta_idx.data_ptr(), -(-n_pref // P),
+                      (n_pref - 1) % P + 1, mcap, vlog.data_ptr(), H, D, P, _lib.LAYOUT_NHD,
+                      torch.cuda.current_stream().cuda_stream)
+            del Kc, Vc
+        layers.append(sharded.ShardLayer(kv=kv, meta=meta, vlog=vlog, kv_idx=kv_idx,
+                                         meta_idx=meta_idx, page_lo=lo, n_local=n_local,
+                                         n_total=n_total, last_len=last_len, owns_last=owns,
+                                         last_phys=n_local - 1 if owns else -1))
+        news.append((q, k_new, v_new))
+    torch.cuda.synchronize()
+    dec = sharded.ShardedDecoder(group, H, D, P, a.budget // P, a.method)
+
+    def one_step():
+        for lay, (q, k, v) in zip(layers, news):
+            dec.step(lay, q, k, v)
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        one_step()  # workspaces and kernel attributes outside capture
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = None
+    if not a.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            one_step()
+    run = graph.replay if graph is not None else one_step
+    for _ in range(a.warmup):
+        run()
+    torch.cuda.synchronize()
+    _lib.check_device()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(a.steps):
+        run()
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    _lib.check_device()
+    us = ms * 1e3 / (a.steps * a.layers)
+    sb = step_bytes(a)
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    peak = float(peaks.get("hbm_gbs") or 6650.0)
+    ach = sb / (us * 1e-6) / 1e9
+    ks = min(a.budget // P, n_total) - 1
+    if rank == 0:
+        print(json.dumps({
+            "metric": LONG_METRIC, "value": round(us, 3), "unit": "us", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic",
+            "config": {"workload": f"1 request, {a.layers}-layer decode step, ctx {S}, budget "
+                                   f"{a.budget}, pages split by range over {world} GPU(s)",
+                       "context_tokens": S, "token_budget": a.budget, "page_size": P,
+                       "num_heads": H, "head_dim": D, "layers_per_step": a.layers,
+                       "score_mode": a.method, "pages_per_gpu": n_local,
+                       "exchange_bytes_per_layer_per_gpu": world * H * ks * 8 +
+                       world * H * (D + 1) * 4,
+                       "graph": graph is not None,
+                       "parallelism": f"page-range x{world}, all_gather of candidates and "
+                                      f"partial states (NCCL)" if world > 1 else "1 GPU"},
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak * world,
+                         "unit": "GB/s", "frac": round(ach / (peak * world), 4),
+                         "algorithmic_bytes": sb, "avg_layer_us": round(us, 3),
+                         "note": "peak = measured HBM GB/s x GPUs"},
+        }), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         run_reference(a)
+    elif a.mode == "longctx":
+        run_longctx(a)
     else:
         run_ours(a)
 

@@ -201,6 +201,35 @@ AOAKV_API int aoakv_sparse_decode_noalloc(
     int32_t num_heads, int32_t head_dim, int32_t page_size, int32_t layout,
     float sm_scale, void* stream);
 
+/* a5 split across GPUs — the per-GPU half of the reference's split-KV decode
+ * (decode_attn.cuh:469-688 writes per-chunk (o, lse) before
+ * VariableLengthMergeStates, :1035-1043), for a sequence whose pages are
+ * spread over several GPUs by page range. Same inputs as
+ * aoakv_sparse_decode, but:
+ *   - an index of -1 means "not on this GPU" and is skipped;
+ *   - last_page_idx may be -1 when another GPU owns the last page;
+ *   - outputs are this GPU's partial state: o_partial [num_heads, head_dim]
+ *     fp32 (normalised over this GPU's tokens) and lse [num_heads] fp32
+ *     (natural log of the sum of exp(scaled scores)); a head with no tokens
+ *     here gets o_partial = 0 and lse = -inf.
+ * Combine the parts with aoakv_merge_states. */
+AOAKV_API int aoakv_sparse_decode_partial(
+    const void* q, float* o_partial, float* lse,
+    const void* kv_data, int32_t kv_capacity_pages,
+    const int32_t* indices, int64_t indices_row_stride, int32_t num_selected,
+    int32_t last_page_idx, int32_t last_page_len,
+    int32_t num_heads, int32_t head_dim, int32_t page_size, int32_t layout,
+    float sm_scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Log-sum-exp merge of num_parts partial states (the math of FlashInfer's
+ * VariableLengthMergeStates, call site decode_attn.cuh:1035-1043):
+ * o_parts [num_parts, num_heads, head_dim] fp32 and lse_parts
+ * [num_parts, num_heads] fp32 -> o [num_heads, head_dim] fp16 and, if
+ * lse_out is not NULL, the merged lse [num_heads] fp32. */
+AOAKV_API int aoakv_merge_states(const float* o_parts, const float* lse_parts,
+                                 int32_t num_parts, int32_t num_heads, int32_t head_dim,
+                                 void* o, float* lse_out, void* stream);
+
 /* Whole per-layer decode step for one request: a1 append of (k_new, v_new),
  * a3 estimate, a4 top-k and a5 sparse decode, as the reference's
  * QuestAttention.forward decode branch issues them

@@ -102,6 +102,10 @@ def test_topk_exact(cuda, n, k, f32, sink):
     if n > 10:
         s[3, 4] = np.nan
         s[5, :] = 1.0                          # an all-tie row
+    if n > 20:
+        s[7, :] = 1.0 + g.random(n, dtype=np.float32) * 1e-3   # one histogram bin, distinct
+        s[9, :] = np.round(g.standard_normal(n) * 3)          # integer ties across bins
+        s[11, :] = 100 + g.standard_normal(n) * 0.5           # a few crowded bins
     if not f32:
         s = s.astype(np.float16).astype(np.float32)
     idx = np.stack([g.permutation(10 * n)[:n] for _ in range(rows)]).astype(np.int32)
@@ -157,6 +161,49 @@ def test_sparse_decode_matches_oracle(cuda, D, n_sel, last_len):
         want = kt.sparse_decode(q, ref, sel, last, last_len)
         got = o.float().cpu().numpy()
         assert np.abs(got - want).max() < 2e-3
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("n_parts", [1, 2, 3])
+@pytest.mark.parametrize("n_sel", [0, 5, 63])
+def test_partial_decode_and_merge_equal_full_decode(cuda, n_parts, n_sel):
+    """aoakv_sparse_decode_partial over disjoint page subsets (-1 = page not
+    here; the last page on one part only) merged by aoakv_merge_states gives
+    the full decode; a part with no pages has lse = -inf."""
+    H, D, P, cap = 32, 128, 16, 200
+    lay = GpuLayer(cap, H, D, P, seed=7 + n_sel)
+    ref = lay.snapshot()
+    g = np.random.default_rng(n_sel + 10 * n_parts)
+    sel = np.stack([g.permutation(cap - 1)[:n_sel] for _ in range(H)]).astype(np.int32)
+    last, last_len = cap - 1, 11
+    q = g.standard_normal((H, D), dtype=np.float32).astype(np.float16)
+    qd = _dev(q)
+    owner = g.integers(0, n_parts, size=sel.shape)  # which part holds each selected page
+    o_parts = torch.empty(n_parts, H, D, dtype=torch.float32, device="cuda")
+    lse_parts = torch.empty(n_parts, H, dtype=torch.float32, device="cuda")
+    ws_n = _lib.size_query("aoakv_decode_workspace_size", H, D, max(n_sel, 1))
+    ws = torch.zeros(ws_n, dtype=torch.uint8, device="cuda")
+    for p in range(n_parts):
+        mine = np.where(owner == p, sel, -1).astype(np.int32)
+        md = _dev(mine) if n_sel else None
+        _lib.call("aoakv_sparse_decode_partial", ptr(qd), ptr(o_parts[p]), ptr(lse_parts[p]),
+                  ptr(lay.kv), cap, ptr(md), n_sel, n_sel, last if p == n_parts - 1 else -1,
+                  last_len, H, D, P, 0, 0.0, ptr(ws), ws_n, stream())
+    o = torch.empty(H, D, dtype=torch.float16, device="cuda")
+    lse = torch.empty(H, dtype=torch.float32, device="cuda")
+    _lib.call("aoakv_merge_states", ptr(o_parts), ptr(lse_parts), n_parts, H, D, ptr(o), ptr(lse),
+              stream())
+    want = kt.sparse_decode(q, ref, sel, last, last_len)
+    assert np.abs(o.float().cpu().numpy() - want).max() < 2e-3
+    # lse of the whole set, from the oracle's pages
+    Kf = [np.concatenate([ref.kv[pg, 0, :, h] for pg in sel[h]] + [ref.kv[last, 0, :last_len, h]])
+          .astype(np.float32) for h in range(H)]
+    want_lse = np.array([np.log(np.exp(k @ q[h].astype(np.float32) / np.sqrt(D)).sum())
+                         for h, k in enumerate(Kf)])
+    np.testing.assert_allclose(lse.cpu().numpy(), want_lse, rtol=1e-3, atol=1e-3)
+    if n_sel == 0 and n_parts > 1:
+        assert np.all(np.isneginf(lse_parts[0].cpu().numpy()))
+        assert np.all(o_parts[0].cpu().numpy() == 0)
     assert _lib.device_error() == 0
 
 
