@@ -71,7 +71,8 @@ int make_kv_tmap(CUtensorMap* map, const void* kv, int H, int D, int P, int cap)
   return AOAKV_OK;
 }
 
-int make_meta_tmap(CUtensorMap* map, const void* meta, int H, int D, int P, int meta_cap) {
+int make_meta_tmap(CUtensorMap* map, const void* meta, int H, int D, int P, int meta_cap,
+                   int box_heads) {
   auto fn = encode_fn();
   if (!fn) return set_error(AOAKV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   if (reinterpret_cast<uintptr_t>(meta) % 16)
@@ -82,7 +83,7 @@ int make_meta_tmap(CUtensorMap* map, const void* meta, int H, int D, int P, int 
                         static_cast<cuuint64_t>(meta_cap) * 2 * P};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2,
                            static_cast<cuuint64_t>(H) * D * 2};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(D), static_cast<cuuint32_t>(H), 1u};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(D), static_cast<cuuint32_t>(box_heads), 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(meta), dims,
                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,

@@ -316,11 +316,18 @@ __device__ __forceinline__ void estimate_pages_tma(const EstimateArgs& a, int p_
 // page are two 3-D TMA boxes {D, H, 1} of `mmap` (the metadata viewed as
 // [rows = meta_page*2*P + slot*P + entry][H][D]); v_log_norm values are
 // plain loads issued before the wait. Same results, same stage layout.
-template <int D>
+// `overlap()` runs on every thread after the first boxes are issued and
+// before the first wait (the fused step appends the new token there).
+struct NoOverlap {
+  __device__ void operator()() const {}
+};
+
+template <int D, typename Overlap = NoOverlap>
 __device__ __forceinline__ void estimate_pages_tmap(const EstimateArgs& a, const CUtensorMap* mmap,
                                                     int p_begin, int p_end, uint8_t* stages,
                                                     uint64_t* bars, int* ids_s,
-                                                    uint32_t* phase_bits) {
+                                                    uint32_t* phase_bits,
+                                                    Overlap overlap = Overlap()) {
   constexpr int L = D / 8;
   const int h = threadIdx.x / L, lane = threadIdx.x % L;
   const int R = p_end - p_begin;
@@ -328,13 +335,6 @@ __device__ __forceinline__ void estimate_pages_tmap(const EstimateArgs& a, const
   const int H = a.H;
   const size_t HD = static_cast<size_t>(H) * D;
   const int sb = est_stage_bytes(H, D);
-  float qv[8];
-  uint32_t msk[4];
-  u4_to_f8(__ldg(reinterpret_cast<const uint4*>(a.q + static_cast<size_t>(h) * D + lane * 8)),
-           qv);
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    msk[i] = (qv[2 * i] > 0.f ? 0x0000ffffu : 0u) | (qv[2 * i + 1] > 0.f ? 0xffff0000u : 0u);
   for (int t = threadIdx.x; t < R; t += blockDim.x) {
     const int p = p_begin + t;
     int mp = __ldg(a.meta_indices + p / a.P);
@@ -362,7 +362,15 @@ __device__ __forceinline__ void estimate_pages_tmap(const EstimateArgs& a, const
       tma_load_3d(stages + j * sb + blk, mmap, 0, 0, row + a.P, &bars[j]);
     }
   }
+  overlap();
   __syncthreads();  // the issuing thread rejoins its warp before the waits
+  float qv[8];
+  uint32_t msk[4];
+  u4_to_f8(__ldg(reinterpret_cast<const uint4*>(a.q + static_cast<size_t>(h) * D + lane * 8)),
+           qv);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    msk[i] = (qv[2 * i] > 0.f ? 0x0000ffffu : 0u) | (qv[2 * i + 1] > 0.f ? 0xffff0000u : 0u);
   for (int j = 0; j < R; ++j) {
     const int s = j % kEstStages;
     const int pid = ids_s[2 * j + 1];

@@ -36,8 +36,14 @@ struct FusedArgs {
 int fused_supported(int H, int D, int P, int n_score, int k_sel, int* grid, size_t* smem,
                     int* chunk, int* n_chunks);
 size_t fused_sync_bytes(int H);
+// The pipelined step kernel (step_pipe.cu): same arguments; its sync words
+// (1 + 2 * H / 8) fit in fused_sync_bytes(H).
+int pipe_supported(int H, int D, int P, int n_score, int k_sel, int* grid, size_t* smem,
+                   int* chunk, int* n_chunks);
+int pipe_group_heads();
+int launch_pipe(const CUtensorMap& tmap, const CUtensorMap& gmap, const FusedArgs& f, int D,
+                int grid, size_t smem, cudaStream_t s);
 int launch_fused(const CUtensorMap& tmap, const CUtensorMap& mtmap, const FusedArgs& f, int D,
-                 int grid, size_t smem,
-                 cudaStream_t s);
+                 int grid, size_t smem, cudaStream_t s);
 
 }  // namespace aoakv

@@ -28,8 +28,9 @@ int check_decode_shape(int H, int D, int P, int kv_cap, int layout);
 // 3-D tensor map over one layer's KV pages: dims {D, H, cap*2*P}, box {D,1,P}.
 int make_kv_tmap(CUtensorMap* map, const void* kv, int H, int D, int P, int cap);
 // 3-D tensor map over one layer's metadata pages: dims {D, H, meta_cap*2*P},
-// box {D, H, 1} (one page's max or min block for all heads).
-int make_meta_tmap(CUtensorMap* map, const void* meta, int H, int D, int P, int meta_cap);
+// box {D, box_heads, 1} (one page's max or min block for box_heads heads).
+int make_meta_tmap(CUtensorMap* map, const void* meta, int H, int D, int P, int meta_cap,
+                   int box_heads);
 
 int launch_decode(const DecodeArgs& a, const CUtensorMap& tmap, int D,
                   const DecodePlan& pl, cudaStream_t s, bool pdl);

@@ -60,11 +60,34 @@ StepWs step_ws_layout(int H, int D, int max_pages, int max_budget) {
   return w;
 }
 
-// AOAKV_STEP_IMPL=chain selects the four-launch path instead of the fused
-// cooperative kernel (read on every call, for A/B comparisons).
-bool fused_enabled() {
+// Which kernel(s) run a sparse step: the phase-by-phase fused kernel
+// (step_fused.cu) when the shape allows, else the four-launch chain.
+// AOAKV_STEP_IMPL=pipe selects the pipelined two-role kernel (step_pipe.cu;
+// measured slower at the headline shape: its scorers get half the SMs'
+// loads in flight) and =chain the chain (read on every call, for A/B
+// comparisons).
+enum class StepImpl { kPipe, kFused, kChain };
+
+struct StepChoice {
+  StepImpl impl;
+  int grid, chunk, n_chunks;
+  size_t smem;
+};
+
+StepChoice choose_step(int H, int D, int P, int N, int k) {
   const char* e = std::getenv("AOAKV_STEP_IMPL");
-  return !(e && std::strcmp(e, "chain") == 0);
+  const bool want_chain = e && std::strcmp(e, "chain") == 0;
+  const bool want_pipe = e && std::strcmp(e, "pipe") == 0;
+  StepChoice c = {StepImpl::kChain, 0, 0, 0, 0};
+  if (want_chain) return c;
+  if (want_pipe && pipe_supported(H, D, P, N - 1, k - 1, &c.grid, &c.smem, &c.chunk,
+                                  &c.n_chunks)) {
+    c.impl = StepImpl::kPipe;
+    return c;
+  }
+  if (fused_supported(H, D, P, N - 1, k - 1, &c.grid, &c.smem, &c.chunk, &c.n_chunks))
+    c.impl = StepImpl::kFused;
+  return c;
 }
 
 }  // namespace
@@ -96,13 +119,8 @@ extern "C" int aoakv_step_launches(int32_t num_heads, int32_t head_dim, int32_t 
   const int k = k_pages < N ? k_pages : N;
   const bool sparse = N > k && k > 1;
   int n = sparse ? 4 : 2;
-  if (sparse && fused_enabled()) {
-    int grid = 0, chunk = 0, n_chunks = 0;
-    size_t smem = 0;
-    if (fused_supported(num_heads, head_dim, page_size, N - 1, k - 1, &grid, &smem, &chunk,
-                        &n_chunks))
-      n = 1;
-  }
+  if (sparse && choose_step(num_heads, head_dim, page_size, N, k).impl != StepImpl::kChain)
+    n = 1;
   if (want_selected && n > 1) ++n;
   *kernels_out = n;
   return AOAKV_OK;
@@ -148,10 +166,11 @@ extern "C" int aoakv_decode_step(
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
 
-  if (sparse && fused_enabled()) {
-    int grid = 0, chunk = 0, n_chunks = 0;
-    size_t smem = 0;
-    if (fused_supported(H, D, P, N - 1, k - 1, &grid, &smem, &chunk, &n_chunks)) {
+  if (sparse) {
+    const StepChoice sc = choose_step(H, D, P, N, k);
+    const int grid = sc.grid, chunk = sc.chunk, n_chunks = sc.n_chunks;
+    const size_t smem = sc.smem;
+    if (sc.impl != StepImpl::kChain) {
       FusedArgs f = {};
       f.k_new = static_cast<const __half*>(k_new);
       f.v_new = static_cast<const __half*>(v_new);
@@ -216,8 +235,14 @@ extern "C" int aoakv_decode_step(
       CUtensorMap tmap, mtmap;
       rc = make_kv_tmap(&tmap, kv_data, H, D, P, kv_capacity_pages);
       if (rc) return rc;
+      if (sc.impl == StepImpl::kPipe) {
+        rc = make_meta_tmap(&mtmap, metadata_data, H, D, P, metadata_capacity_pages,
+                            pipe_group_heads());
+        if (rc) return rc;
+        return launch_pipe(tmap, mtmap, f, D, grid, smem, s);
+      }
       if (f.est_tma) {
-        rc = make_meta_tmap(&mtmap, metadata_data, H, D, P, metadata_capacity_pages);
+        rc = make_meta_tmap(&mtmap, metadata_data, H, D, P, metadata_capacity_pages, H);
         if (rc) return rc;
       } else {
         mtmap = tmap;  // unused

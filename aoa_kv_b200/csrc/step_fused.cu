@@ -2,8 +2,13 @@
 // scoring, top-k page selection, split-KV sparse decode and the
 // log-sum-exp merge.
 //
-//   A  CTA c < H appends head c of the new token, fused with the page's key
-//      max/min and, on page fill, its v_log_norm (decode_page.cuh:392-506).
+//   A  after its scoring, a CTA without decode units (or, when there are
+//      too few of those, the CTA owning head h's last decode unit) appends
+//      head h of the new token, fused with the page's key max/min and, on
+//      page fill, its v_log_norm (decode_page.cuh:392-506); its inputs were
+//      copied to shared memory at kernel start. The last page is never
+//      scored, so only the unit attending it reads what the append writes;
+//      that unit waits for the head's `appended` flag.
 //   E  every CTA scores a contiguous page range for all heads
 //      (decode_attn.cuh:143-199, :263-443): the page's key max/min blocks
 //      stream through a TMA ring in shared memory, one thread group per
@@ -23,11 +28,16 @@
 // The counters are re-armed to zero by their last user, so the workspace
 // stays zeroed between calls. A wait past ~1 s records AOAKV_DEV_ERR_TIMEOUT
 // and the CTA returns; the caller must then zero the workspace again.
+#include <atomic>
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
 
 #include "decode.cuh"
 #include "estimate.cuh"
 #include "fused.h"
+#include "grid_sync.cuh"
+#include "step_append.cuh"
 #include "plan.h"
 #include "topk.cuh"
 #include "topk_bitonic.cuh"
@@ -38,15 +48,19 @@
 // stamps out.
 namespace aoakv {
 __device__ uint64_t g_phase_ns[2048 * 8];
+__device__ long long g_phase_clk[2048 * 8];
 __device__ __forceinline__ uint64_t probe_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
 }  // namespace aoakv
-#define AOAKV_STAMP(i)                                                   \
-  do {                                                                   \
-    if (threadIdx.x == 0) g_phase_ns[blockIdx.x * 8 + (i)] = probe_ns(); \
+#define AOAKV_STAMP(i)                                   \
+  do {                                                   \
+    if (threadIdx.x == 0) {                              \
+      g_phase_ns[blockIdx.x * 8 + (i)] = probe_ns();     \
+      g_phase_clk[blockIdx.x * 8 + (i)] = clock64();     \
+    }                                                    \
   } while (0)
 #else
 #define AOAKV_STAMP(i) \
@@ -62,45 +76,10 @@ namespace {
 constexpr int kFThreads = kFusedThreads;
 constexpr int kFWarps = kFThreads / 32;
 constexpr int kFMaxWin = 64;                 // selected slots one CTA may own
-constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s
 
-__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__host__ __device__ inline int fused_xbuf_offset(int n_score) {
+  return hist_stage_bytes(n_score, true);
 }
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Thread 0 spins until *p >= target or the time limit; the result is
-// broadcast through *ok_s. Returns false on timeout (error recorded).
-__device__ __forceinline__ bool cta_wait_geq(const uint32_t* p, uint32_t target, int* ok_s,
-                                             int* err) {
-  if (threadIdx.x == 0) {
-    int ok = 1;
-    if (ld_acquire(p) < target) {
-      const uint64_t t0 = global_ns();
-      uint32_t it = 0;
-      while (ld_acquire(p) < target) {
-        if (++it > 64) __nanosleep(32);
-        if ((it & 255u) == 0 && global_ns() - t0 > kWaitNs) {
-          raise_dev_error(err, AOAKV_DEV_ERR_TIMEOUT);
-          ok = 0;
-          break;
-        }
-      }
-    }
-    __threadfence();
-    *ok_s = ok;
-  }
-  __syncthreads();
-  return *ok_s != 0;
-}
-
-__host__ __device__ inline int fused_xbuf_offset(int n_score) { return (n_score + 3) / 4 * 16; }
 
 __host__ __device__ inline int fused_smem_bytes(int H, int D, int P, int n_score, int chunk) {
   const int q_bytes = H * D * 4;  // generic estimate path only
@@ -132,7 +111,7 @@ __global__ void __launch_bounds__(kFThreads, 2)
   __shared__ uint64_t ebars[kEstStages];
   __shared__ int ids_s[2 * kEstMaxRange];
 
-  const int G = gridDim.x, b = blockIdx.x, H = f.H, P = f.P;
+  const int G = gridDim.x, b = blockIdx.x, H = f.H;
   uint32_t* est_done = f.sync;
   uint32_t* passed = f.sync + 1;
 
@@ -144,83 +123,22 @@ __global__ void __launch_bounds__(kFThreads, 2)
     tma_prefetch_desc(&tmap);
     if (f.est_tma) tma_prefetch_desc(&mtmap);
   }
+  pdl_wait();  // launched with programmatic serialization: inputs of the previous kernel
 
-  // ---- A: append head b of the new token (warp 0, D/8 lanes)
-  if (b < H && threadIdx.x < 32) {
-    constexpr int L = D / 8;
-    const int lane = threadIdx.x;
-    const int h = b;
-    const int page_iter = f.n_pages - 1;
-    const int entry = f.last_len - 1;
-    const int pid = __ldg(f.kv_indices + page_iter);
-    const int mpid = __ldg(f.meta_indices + page_iter / P);
-    const int mentry = page_iter % P;
-    const bool ok = pid >= 0 && pid < f.kv_cap && mpid >= 0 && mpid < f.meta_cap;
-    if (!ok && lane == 0) raise_dev_error(f.err, AOAKV_DEV_ERR_BAD_PAGE);
-    float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (ok && lane < L) {
-      const size_t HD = static_cast<size_t>(H) * D;
-      const size_t col = static_cast<size_t>(h) * D + lane * 8;
-      const uint4 kk = *reinterpret_cast<const uint4*>(f.k_new + col);
-      const uint4 vv = *reinterpret_cast<const uint4*>(f.v_new + col);
-      __half* mk = f.meta + ((static_cast<size_t>(mpid) * 2 + 0) * P + mentry) * HD + col;
-      __half* mv = f.meta + ((static_cast<size_t>(mpid) * 2 + 1) * P + mentry) * HD + col;
-      uint4 mx, mn;
-      if (entry > 0) {
-        mx = *reinterpret_cast<const uint4*>(mk);
-        mn = *reinterpret_cast<const uint4*>(mv);
-      } else {
-        const __half2 lo = __float2half2_rn(-65504.f), hi = __float2half2_rn(65504.f);
-        mx.x = mx.y = mx.z = mx.w = *reinterpret_cast<const uint32_t*>(&lo);
-        mn.x = mn.y = mn.z = mn.w = *reinterpret_cast<const uint32_t*>(&hi);
-      }
-      __half2* a2 = reinterpret_cast<__half2*>(&mx);
-      __half2* n2 = reinterpret_cast<__half2*>(&mn);
-      const __half2* k2 = reinterpret_cast<const __half2*>(&kk);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        a2[i] = __hmax2(a2[i], k2[i]);
-        n2[i] = __hmin2(n2[i], k2[i]);
-      }
-      __half* kvk = f.kv + ((static_cast<size_t>(pid) * 2 + 0) * P + entry) * HD + col;
-      __half* kvv = f.kv + ((static_cast<size_t>(pid) * 2 + 1) * P + entry) * HD + col;
-      *reinterpret_cast<uint4*>(kvk) = kk;
-      *reinterpret_cast<uint4*>(kvv) = vv;
-      *reinterpret_cast<uint4*>(mk) = mx;
-      *reinterpret_cast<uint4*>(mv) = mn;
-      if (entry + 1 == P) {  // earlier V rows of the page: 8 loads in flight
-        for (int e0 = 0; e0 + 1 < P; e0 += 8) {
-          uint4 r[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-            if (e0 + u + 1 < P)
-              r[u] = ld_stream_u4(f.kv + ((static_cast<size_t>(pid) * 2 + 1) * P + e0 + u) * HD +
-                                  col);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            if (e0 + u + 1 < P) {
-              float t[8];
-              u4_to_f8(r[u], t);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) s[i] += t[i];
-            }
-          }
-        }
-        float t[8];
-        u4_to_f8(vv, t);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) s[i] += t[i];
-      }
-    }
-    if (entry + 1 == P) {
-      const float inv = 1.f / P;
-      float l2 = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) l2 += (s[i] * inv) * (s[i] * inv);
-#pragma unroll
-      for (int off = L / 2; off > 0; off >>= 1) l2 += __shfl_xor_sync(0xffffffffu, l2, off);
-      if (ok && lane == 0)
-        f.vlog[static_cast<size_t>(pid) * H + h] = __float2half_rn(logf(sqrtf(l2) + 1e-6f));
+  // start copying the append inputs of the heads this CTA appends (see A
+  // below; the unit range is derived again there, so nothing stays live
+  // across the scoring loop)
+  __shared__ AppendStage app_s;
+  if (threadIdx.x < 32) {
+    const int nc = f.dec.n_chunks, nu = H * nc;
+    if (G - nu >= H) {  // a CTA without decode units appends one head
+      if (b >= nu && b < nu + H) append_prefetch<D>(f, b - nu, 0, app_s);
+    } else {
+      const int up = (nu + G - 1) / G;
+      const int lo = min(nu, b * up), hi = min(nu, lo + up);
+      int slot = 0;
+      for (int u = lo; u < hi && slot < kAppendStaged; ++u)
+        if (u % nc == nc - 1) append_prefetch<D>(f, u / nc, slot++, app_s);
     }
   }
 
@@ -250,19 +168,46 @@ __global__ void __launch_bounds__(kFThreads, 2)
     atomicAdd(est_done, 1u);
   }
 
+  // ---- A: append the new token of every head whose last decode unit (the
+  // one holding the last page) is this CTA's, while the other CTAs finish
+  // scoring; no other CTA reads these rows in this launch (the last page is
+  // never scored, and its K/V are read only by that unit, below)
+  const int n_chunks = f.dec.n_chunks, C = f.dec.chunk_pages;
+  const int n_units = H * n_chunks;
+  const int upc = (n_units + G - 1) / G;
+  const int u_lo = min(n_units, b * upc), u_hi = min(n_units, u_lo + upc);
+  uint32_t* appended = f.sync + 2;  // [H] flags: head h's new token is in place
+  const bool spare_append = G - n_units >= H;
+  if (spare_append) {
+    // CTA n_units + h has no decode unit: it appends head h and raises
+    // appended[h]; the unit that decodes head h's last page waits for it
+    if (b >= n_units && b < n_units + H) {
+      if (threadIdx.x < 32) append_head<D>(f, b - n_units, &app_s, 0);
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        __threadfence();
+        atomicExch(appended + (b - n_units), 1u);
+      }
+    }
+  } else if (threadIdx.x < 32) {  // the owner of head h's last unit appends it
+    int slot = 0;
+    for (int u = u_lo; u < u_hi; ++u) {
+      if (u % n_chunks != n_chunks - 1) continue;
+      append_head<D>(f, u / n_chunks, slot < kAppendStaged ? &app_s : nullptr, slot);
+      ++slot;
+    }
+  }
+
   // ---- T: wait for every CTA's scores, then re-arm the counters
   if (!cta_wait_geq(est_done, static_cast<uint32_t>(G), &ok_s, f.err)) return;
   AOAKV_STAMP(2);
+  pdl_launch_dependents();  // the next kernel may launch (it waits for our completion)
   if (threadIdx.x == 0 && atomicAdd(passed, 1u) == static_cast<uint32_t>(G - 1)) {
     *est_done = 0u;  // every CTA has passed its wait
     *passed = 0u;
   }
 
   // ---- T + D: this CTA's units [u_lo, u_hi), contiguous, possibly 2 heads
-  const int n_chunks = f.dec.n_chunks, C = f.dec.chunk_pages;
-  const int n_units = H * n_chunks;
-  const int upc = (n_units + G - 1) / G;
-  const int u_lo = min(n_units, b * upc), u_hi = min(n_units, u_lo + upc);
   float* mrg = reinterpret_cast<float*>(smem + kDecHeader);
   __half* tiles = reinterpret_cast<__half*>(smem + dec_tile_offset(D, kFWarps));
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem);
@@ -290,8 +235,9 @@ __global__ void __launch_bounds__(kFThreads, 2)
       ta.k = f.k_sel;
       ta.sink = f.sink;
       uint8_t* un = smem + fused_xbuf_offset(ta.n);
-      if (!topk_row_hist<true>(ta, h, keys, *reinterpret_cast<HistSmem*>(un), win_s, win_lo,
-                               win_hi)) {  // many equal scores: exact fallbacks
+      if (!topk_row_hist<true>(ta, h, reinterpret_cast<uint8_t*>(keys), true,
+                             *reinterpret_cast<HistSmem*>(un), win_s, win_lo, win_hi)) {
+        // many equal scores: exact fallbacks
         if (f.k_sel <= 128)  // register budget of the 2-CTA/SM kernel: K <= 128 here
           topk_row_small<true, 4>(ta, h, keys, reinterpret_cast<uint64_t*>(un), win_s, win_lo,
                                   win_hi);
@@ -304,6 +250,10 @@ __global__ void __launch_bounds__(kFThreads, 2)
               i == f.k_sel ? __ldg(f.kv_indices + f.n_pages - 1) : -1;
       __syncthreads();
       AOAKV_STAMP(3);
+    }
+    if (spare_append && c == n_chunks - 1) {  // this unit attends the last page
+      if (!cta_wait_geq(appended + h, 1u, &ok_s, f.err)) return;
+      if (threadIdx.x == 0) appended[h] = 0u;  // the only reader: re-arm
     }
     if (threadIdx.x == 0)  // (issues a proxy fence: appended page -> TMA reads)
       decode_issue(f.dec, &tmap, h, c, bars, tok_s, tiles, D, win_s, win_lo);
@@ -356,29 +306,62 @@ int fused_supported(int H, int D, int P, int n_score, int k_sel, int* grid_out,
 
 size_t fused_sync_bytes(int H) { return ((2 + 2 * static_cast<size_t>(H)) * 4 + 255) / 256 * 256; }
 
+// Programmatic dependent launch on top of the cooperative attribute lets the
+// next kernel's launch overlap this one's tail. Whether the driver accepts
+// the pair is learnt on the first launch outside stream capture (-1 unknown,
+// 0 rejected, 1 accepted); AOAKV_NO_PDL=1 disables it.
+std::atomic<int> g_fused_pdl{-1};
+
 int launch_fused(const CUtensorMap& tmap, const CUtensorMap& mtmap, const FusedArgs& f, int D,
-                 int grid, size_t smem,
-                 cudaStream_t s) {
+                 int grid, size_t smem, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kFThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
+  auto launch = [&]() {
+    return D == 128 ? cudaLaunchKernelEx(&cfg, fused_step_kernel<128>, tmap, mtmap, f)
+                    : cudaLaunchKernelEx(&cfg, fused_step_kernel<64>, tmap, mtmap, f);
+  };
+  const char* no_pdl = std::getenv("AOAKV_NO_PDL");
+  int pdl = (no_pdl && std::strcmp(no_pdl, "1") == 0) ? 0 : g_fused_pdl.load();
+  if (pdl == -1) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+      pdl = 0;  // learn outside capture only: a failed launch would end the capture
+  }
+  if (pdl != 0) {
+    cfg.numAttrs = 2;
+    const cudaError_t e = launch();
+    if (e == cudaSuccess) {
+      g_fused_pdl.store(1);
+      return AOAKV_OK;
+    }
+    if (pdl == 1) AOAKV_CUDA_TRY(e, "fused step launch");
+    (void)cudaGetLastError();  // rejected pairing: plain cooperative launches from now on
+    g_fused_pdl.store(0);
+  }
   cfg.numAttrs = 1;
-  if (D == 128)
-    AOAKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, fused_step_kernel<128>, tmap, mtmap, f), "fused step launch");
-  else
-    AOAKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, fused_step_kernel<64>, tmap, mtmap, f), "fused step launch");
+  AOAKV_CUDA_TRY(launch(), "fused step launch");
   return AOAKV_OK;
 }
 
 }  // namespace aoakv
 
 #ifdef AOAKV_PHASE_PROBE
+extern "C" __attribute__((visibility("default"))) int aoakv_probe_phase_clk(long long* host,
+                                                                            int n) {
+  return cudaMemcpyFromSymbol(host, aoakv::g_phase_clk, static_cast<size_t>(n) * 8) ==
+                 cudaSuccess
+             ? 0
+             : 3;
+}
 extern "C" __attribute__((visibility("default"))) int aoakv_probe_phase_ns(uint64_t* host,
                                                                            int n) {
   return cudaMemcpyFromSymbol(host, aoakv::g_phase_ns, static_cast<size_t>(n) * 8) ==

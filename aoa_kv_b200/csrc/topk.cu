@@ -14,6 +14,7 @@ namespace aoakv {
 namespace {
 
 constexpr int kSmallThreads = 512;
+constexpr int kSmallIdsMaxN = 16384;  // ids and bins staged in shared memory up to here
 
 __global__ void __launch_bounds__(kTopkThreads) topk_kernel(TopkArgs a) {
   extern __shared__ uint32_t keys[];
@@ -30,9 +31,11 @@ constexpr size_t kSmallUnion = sizeof(HistSmem) > bitonic_xbuf_bytes(kSmallThrea
 
 __global__ void __launch_bounds__(kSmallThreads, 1) topk_small_kernel(TopkArgs a) {
   extern __shared__ uint32_t keys[];
-  uint8_t* un = reinterpret_cast<uint8_t*>(keys + (a.n + 3) / 4 * 4);
+  const bool staged = a.n <= kSmallIdsMaxN;
+  uint8_t* un = reinterpret_cast<uint8_t*>(keys) + hist_stage_bytes(a.n, staged);
   pdl_wait();
-  if (!topk_row_hist(a, blockIdx.x, keys, *reinterpret_cast<HistSmem*>(un)))
+  if (!topk_row_hist(a, blockIdx.x, reinterpret_cast<uint8_t*>(keys), staged,
+                     *reinterpret_cast<HistSmem*>(un)))
     topk_row_small(a, blockIdx.x, keys, reinterpret_cast<uint64_t*>(un));
 }
 
@@ -44,7 +47,7 @@ int launch_topk(const TopkArgs& a, int rows, cudaStream_t s, bool pdl) {
                          : reinterpret_cast<const void*>(topk_kernel);
   size_t smem = static_cast<size_t>(a.n) * sizeof(uint32_t);
   if (small)
-    smem = static_cast<size_t>((a.n + 3) / 4 * 4) * 4 + kSmallUnion;
+    smem = static_cast<size_t>(hist_stage_bytes(a.n, a.n <= kSmallIdsMaxN)) + kSmallUnion;
   if (smem > 48 * 1024)
     AOAKV_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(smem)),

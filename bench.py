@@ -560,7 +560,12 @@ def run_longctx(a):
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             one_step()
-    run = graph.replay if graph is not None else one_step
+    def run():
+        if graph is not None:
+            graph.replay()
+        else:
+            one_step()
+
     for _ in range(a.warmup):
         run()
     torch.cuda.synchronize()
@@ -611,7 +616,12 @@ def run_longctx(a):
                          "algorithmic_bytes": sb, "avg_layer_us": round(us, 3),
                          "note": "peak = measured HBM GB/s x GPUs"},
         }), flush=True)
-    del graph
+    # a graph that holds NCCL calls must be released before the process
+    # group, or the exit waits for ever
+    graph = None
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -109,10 +109,11 @@ def test_step_sink_matches_reference_simulation(cuda, method, S, B, dist):
         assert np.abs(got_o - out_s).max() < 2e-3
 
 
-@pytest.fixture(params=["fused", "chain"])
+@pytest.fixture(params=["pipe", "fused", "chain"])
 def step_impl(request, monkeypatch):
-    """Runs a test with the fused cooperative kernel and with the four-launch
-    chain (AOAKV_STEP_IMPL is read by the library on every call)."""
+    """Runs a test with the phase-by-phase fused kernel (the default), the
+    pipelined two-role kernel and the four-launch chain (AOAKV_STEP_IMPL is
+    read by the library on every call)."""
     monkeypatch.setenv("AOAKV_STEP_IMPL", request.param)
     return request.param
 
