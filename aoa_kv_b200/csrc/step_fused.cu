@@ -123,24 +123,30 @@ __global__ void __launch_bounds__(kFThreads, 2)
     tma_prefetch_desc(&tmap);
     if (f.est_tma) tma_prefetch_desc(&mtmap);
   }
-  pdl_wait();  // launched with programmatic serialization: inputs of the previous kernel
-
-  // start copying the append inputs of the heads this CTA appends (see A
-  // below; the unit range is derived again there, so nothing stays live
-  // across the scoring loop)
+  // Launched with programmatic serialization, the kernel may start before
+  // the previous kernel on the stream has finished. Until pdl_wait() it
+  // reads only what no kernel of this step writes: this layer's page tables
+  // and metadata (the scorer's first boxes are issued before the wait);
+  // q, k_new, v_new, the workspace and every write come after it.
   __shared__ AppendStage app_s;
-  if (threadIdx.x < 32) {
-    const int nc = f.dec.n_chunks, nu = H * nc;
-    if (G - nu >= H) {  // a CTA without decode units appends one head
-      if (b >= nu && b < nu + H) append_prefetch<D>(f, b - nu, 0, app_s);
-    } else {
-      const int up = (nu + G - 1) / G;
-      const int lo = min(nu, b * up), hi = min(nu, lo + up);
-      int slot = 0;
-      for (int u = lo; u < hi && slot < kAppendStaged; ++u)
-        if (u % nc == nc - 1) append_prefetch<D>(f, u / nc, slot++, app_s);
+  auto after_wait = [&]() {
+    pdl_wait();
+    // start copying the append inputs of the heads this CTA appends (see A
+    // below; the unit range is derived again there, so nothing stays live
+    // across the scoring loop)
+    if (threadIdx.x < 32) {
+      const int nc = f.dec.n_chunks, nu = H * nc;
+      if (G - nu >= H) {  // a CTA without decode units appends one head
+        if (b >= nu && b < nu + H) append_prefetch<D>(f, b - nu, 0, app_s);
+      } else {
+        const int up = (nu + G - 1) / G;
+        const int lo = min(nu, b * up), hi = min(nu, lo + up);
+        int slot = 0;
+        for (int u = lo; u < hi && slot < kAppendStaged; ++u)
+          if (u % nc == nc - 1) append_prefetch<D>(f, u / nc, slot++, app_s);
+      }
     }
-  }
+  };
 
   // ---- E: score this CTA's share of the (page, head) rows
   if (f.est_tma) {  // TMA boxes of whole page blocks through a 4-stage ring
@@ -148,12 +154,14 @@ __global__ void __launch_bounds__(kFThreads, 2)
     page_range(f.est.n_score, b, G, &pb, &pe);
     __syncthreads();  // mbarrier initialisation visible to every thread
     uint32_t ephase = 0;
-    estimate_pages_tmap<D>(f.est, &mtmap, pb, pe, smem, ebars, ids_s, &ephase);
+    estimate_pages_tmap<D>(f.est, &mtmap, pb, pe, smem, ebars, ids_s, &ephase, after_wait);
   } else if (H * (D / 8) == kFThreads) {  // head-stationary, loads into registers
+    after_wait();
     int pb, pe;
     page_range(f.est.n_score, b, G, &pb, &pe);
     estimate_pages_hs<D, 4>(f.est, pb, pe);
   } else {
+    after_wait();
     float* q_s = reinterpret_cast<float*>(smem);
     stage_q<D>(f.est.q, q_s, H);
     __syncthreads();
