@@ -11,17 +11,18 @@ softmax states:
 2. every GPU scores its own pages (a3) and keeps its local top-(k-1) per
    head (a4) as (score, global page id) — k-1 from each GPU is enough for
    the global top-(k-1) to be among them;
-3. all_gather of the candidates, G * H * (k-1) * 8 bytes; every GPU selects
+3. one all_gather of the candidates, G * H * (k-1) * 8 bytes (score and
+   page id packed in one fp32 tensor); every GPU selects
    the same global top-(k-1) from them (a4 again). Candidates are laid out
    GPU by GPU, each list in the library's selection order, so equal scores
    still resolve to the lower page id, as on one GPU;
 4. every GPU decodes the selected pages it holds, plus the last page on its
    owner, into a partial (o, lse) per head (a5 without its merge);
-5. all_gather of the partial states, G * H * (D + 1) * 4 bytes, and the
+5. one all_gather of the partial states, G * H * (D + 1) * 4 bytes, and the
    log-sum-exp merge (FlashInfer VariableLengthMergeStates' math,
    decode_attn.cuh:1035-1043) gives every GPU the same output.
 
-The data path crosses no GPU boundary except through the two all_gathers
+The data path crosses no GPU boundary except through these two all_gathers
 (NCCL over NVLink on GPUs, gloo in the CPU tests). The kernels are reached
 through an operations object: ``CudaShardOps`` calls libaoakv.so; tests
 pass another implementation of the same operations to exercise this host
@@ -133,11 +134,13 @@ class ShardedDecoder:
                                  f"fewer than the {ks} each rank must propose")
             sink_here = self.sink and layer.page_lo == 0
             vals, ids = ops.local_topk(q, layer, n_score, ks, self.score_mode, sink_here)
-            all_v = _gather(vals, self.group)  # [G, H, ks]
-            all_i = _gather(ids, self.group)
-            G = all_v.shape[0]
-            cand_v = all_v.permute(1, 0, 2).reshape(self.H, G * ks).contiguous()
-            cand_i = all_i.permute(1, 0, 2).reshape(self.H, G * ks).contiguous()
+            # one collective for both: the ids travel as the bits of fp32 words
+            packed = torch.stack([vals, ids.view(torch.float32)])  # [2, H, ks]
+            allp = _gather(packed, self.group)  # [G, 2, H, ks]
+            G = allp.shape[0]
+            cand = allp.permute(1, 2, 0, 3).reshape(2, self.H, G * ks)
+            cand_v = cand[0].contiguous()
+            cand_i = cand[1].contiguous().view(torch.int32)
             # page 0, when forced, is GPU 0's first candidate: position 0
             sel = ops.select(cand_v, cand_i, ks, self.sink)
             local = ops.to_local(sel, layer)
@@ -146,7 +149,9 @@ class ShardedDecoder:
         else:  # every page is attended
             local = ops.all_local_pages(layer, n_score)
         o_part, lse = ops.decode_partial(q, layer, local)
-        o = ops.merge(_gather(o_part, self.group), _gather(lse, self.group))
+        state = torch.cat([o_part, lse.unsqueeze(1)], dim=1)  # [H, D + 1], one collective
+        alls = _gather(state, self.group)  # [G, H, D + 1]
+        o = ops.merge(alls[:, :, :self.D].contiguous(), alls[:, :, self.D].contiguous())
         return o, sel
 
 
