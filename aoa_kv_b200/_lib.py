@@ -48,6 +48,7 @@ SIGNATURES = {
                                     _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_f, _c_p, _c_size,
                                     _c_p],
     "aoakv_merge_states": [_c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_p],
+    "aoakv_map_pages": [_c_p, _c_i64, _c_i32, _c_i32, _c_p, _c_p, _c_p],
     "aoakv_step_workspace_size": [_c_i32, _c_i32, _c_i32, _c_i32, _c_sizep],
     "aoakv_step_launches": [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_ip],
     "aoakv_decode_step": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p,

@@ -9,7 +9,8 @@
 //   o = sum_g w_g o_g / sum_g w_g,  lse = m + ln(sum_g w_g).
 // A part with lse = -inf (no tokens) contributes nothing; a head with no
 // tokens in any part gets o = 0 and lse = -inf. Used by the page-range
-// sharded step, where each GPU decodes the selected pages it owns.
+// sharded step, where each GPU decodes the selected pages it owns; that
+// step's global -> local page-id map (aoakv_map_pages) lives here too.
 #include <cmath>
 
 #include "common.cuh"
@@ -38,10 +39,34 @@ __global__ void merge_states_kernel(const float* o_parts, const float* lse_parts
   }
 }
 
+__global__ void map_pages_kernel(const int32_t* ids, int64_t count, int32_t lo, int32_t n_local,
+                                 const int32_t* local, int32_t* out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t r = ids[i] - lo;
+    out[i] = (r >= 0 && r < n_local) ? __ldg(local + r) : -1;
+  }
+}
+
 }  // namespace
 }  // namespace aoakv
 
 using namespace aoakv;
+
+extern "C" int aoakv_map_pages(const int32_t* global_ids, int64_t count, int32_t page_lo,
+                               int32_t n_local, const int32_t* local_kv_indices, int32_t* out,
+                               void* stream) {
+  AOAKV_CHECK_ARG(global_ids && local_kv_indices && out, "map_pages: NULL pointer argument");
+  AOAKV_CHECK_ARG(count >= 0 && n_local >= 0, "map_pages: bad sizes");
+  if (count == 0) return AOAKV_OK;
+  const int threads = 256;
+  const int64_t blocks = (count + threads - 1) / threads;
+  map_pages_kernel<<<static_cast<int>(blocks < 1024 ? blocks : 1024), threads, 0,
+                     static_cast<cudaStream_t>(stream)>>>(global_ids, count, page_lo, n_local,
+                                                          local_kv_indices, out);
+  AOAKV_CUDA_TRY(cudaGetLastError(), "map_pages launch");
+  return AOAKV_OK;
+}
 
 extern "C" int aoakv_merge_states(const float* o_parts, const float* lse_parts,
                                   int32_t num_parts, int32_t num_heads, int32_t head_dim,

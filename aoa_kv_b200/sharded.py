@@ -161,6 +161,7 @@ class CudaShardOps:
     def __init__(self, num_heads: int, head_dim: int, page_size: int):
         self.H, self.D, self.P = num_heads, head_dim, page_size
         self._ws: Optional[torch.Tensor] = None
+        self._rows: dict = {}
 
     @staticmethod
     def _stream(t: torch.Tensor):
@@ -193,8 +194,12 @@ class CudaShardOps:
                   layer.kv_idx.data_ptr(), layer.kv.size(0), layer.vlog.data_ptr(), self.H,
                   self.D, self.P, _lib.LAYOUT_NHD,
                   _lib.SCORE_AOAKV if mode == "aoakv" else _lib.SCORE_QUEST, self._stream(q))
-        ids_row = torch.arange(layer.page_lo, layer.page_lo + n_score, dtype=torch.int32,
-                               device=dev)
+        key = (layer.page_lo, n_score, dev)
+        ids_row = self._rows.get(key)
+        if ids_row is None:  # global page ids of the scored pages, made once
+            ids_row = torch.arange(layer.page_lo, layer.page_lo + n_score, dtype=torch.int32,
+                                   device=dev)
+            self._rows[key] = ids_row
         vals = torch.empty(self.H, ks, dtype=torch.float32, device=dev)
         ids = torch.empty(self.H, ks, dtype=torch.int32, device=dev)
         _lib.call("aoakv_topk_filtering", scores.data_ptr(), _lib.DTYPE_F32, n_score,
@@ -210,12 +215,11 @@ class CudaShardOps:
                   self._stream(cand_v))
         return out
 
-    @staticmethod
-    def to_local(sel, layer: ShardLayer):
-        rel = sel.long() - layer.page_lo
-        mine = (rel >= 0) & (rel < layer.n_local)
-        phys = layer.kv_idx[rel.clamp(0, layer.n_local - 1)]
-        return torch.where(mine, phys, torch.full_like(phys, -1)).to(torch.int32).contiguous()
+    def to_local(self, sel, layer: ShardLayer):
+        out = torch.empty_like(sel)
+        _lib.call("aoakv_map_pages", sel.data_ptr(), sel.numel(), layer.page_lo, layer.n_local,
+                  layer.kv_idx.data_ptr(), out.data_ptr(), self._stream(sel))
+        return out
 
     def all_local_pages(self, layer: ShardLayer, n_score: int):
         return layer.kv_idx[:n_score].to(torch.int32).unsqueeze(0).expand(self.H, n_score) \

@@ -230,6 +230,14 @@ AOAKV_API int aoakv_merge_states(const float* o_parts, const float* lse_parts,
                                  int32_t num_parts, int32_t num_heads, int32_t head_dim,
                                  void* o, float* lse_out, void* stream);
 
+/* Page-range sharding helper (no reference counterpart: the reference runs
+ * on one GPU): out[i] = local_kv_indices[global_ids[i] - page_lo] when the
+ * global page id lies in [page_lo, page_lo + n_local), else -1 (the page is
+ * on another GPU), for count ids. */
+AOAKV_API int aoakv_map_pages(const int32_t* global_ids, int64_t count, int32_t page_lo,
+                              int32_t n_local, const int32_t* local_kv_indices, int32_t* out,
+                              void* stream);
+
 /* Whole per-layer decode step for one request: a1 append of (k_new, v_new),
  * a3 estimate, a4 top-k and a5 sparse decode, as the reference's
  * QuestAttention.forward decode branch issues them

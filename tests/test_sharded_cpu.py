@@ -48,7 +48,12 @@ class NumpyShardOps:
         pos = kt.topk_positions(cand_v.numpy(), ks, sink)
         return torch.from_numpy(np.take_along_axis(cand_i.numpy(), pos, axis=1).astype(np.int32))
 
-    to_local = staticmethod(sharded.CudaShardOps.to_local)
+    @staticmethod
+    def to_local(sel, layer):
+        rel = sel.long() - layer.page_lo
+        mine = (rel >= 0) & (rel < layer.n_local)
+        phys = layer.kv_idx[rel.clamp(0, layer.n_local - 1)]
+        return torch.where(mine, phys, torch.full_like(phys, -1)).to(torch.int32)
 
     def all_local_pages(self, layer, n_score):
         return layer.kv_idx[:n_score].to(torch.int32).unsqueeze(0).expand(self.H, n_score)
