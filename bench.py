@@ -44,6 +44,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "sparse-decode µs/layer @32K ctx, 1K budget; % of B200 HBM roofline"
+# DRAM bytes (read + write) of one fused step launch at the headline shape,
+# from the ncu capture summarised under profiles/ (dram__bytes_read.sum +
+# dram__bytes_write.sum, one layer, caches flushed)
+STEP_TRAFFIC_BYTES = 52_328_448
 H, D, P = 32, 128, 16
 
 
@@ -452,7 +456,10 @@ def run_ours(a):
                          if kernels_per_layer == 1 else
                          f"step chain of {kernels_per_layer} kernels",
                          "achieved": round(step_ach, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(step_ach / peak, 4), "traffic": None,
+                         "frac": round(step_ach / peak, 4),
+                         "traffic": STEP_TRAFFIC_BYTES if (kernels_per_layer == 1 and
+                                                           a.ctx == 32768 and a.budget == 1024 and
+                                                           a.method == "aoakv") else None,
                          "algorithmic_bytes": sb, "avg_launch_us": round(us_layer_gpu, 3),
                          "ideal_us": round(sb / (peak * 1e9) * 1e6, 3),
                          "peak_source": peak_src},
