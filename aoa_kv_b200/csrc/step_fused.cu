@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(kFThreads, 2)
   };
 
   // ---- E: score this CTA's share of the (page, head) rows
-  if (f.est_tma) {  // TMA boxes of whole page blocks through a 4-stage ring
+  if (f.est_tma) {  // TMA boxes of whole page blocks through a kEstStages ring
     int pb, pe;
     page_range(f.est.n_score, b, G, &pb, &pe);
     __syncthreads();  // mbarrier initialisation visible to every thread
