@@ -3,6 +3,7 @@
 #include <string>
 
 #include "common.cuh"
+#include "grid_sync.cuh"
 
 namespace aoakv {
 
@@ -82,6 +83,29 @@ int aoakv_get_device_error(int32_t* code_out, int32_t clear) {
     AOAKV_CUDA_TRY(cudaMemset(p, 0, sizeof(int)), "aoakv_get_device_error clear");
     AOAKV_CUDA_TRY(cudaDeviceSynchronize(), "aoakv_get_device_error sync");
   }
+  return AOAKV_OK;
+}
+
+// One CTA waits, bounded by limit_us, until *flag >= target: the wait the
+// fused step kernels use between their phases, with a caller-chosen limit.
+namespace {
+__global__ void debug_wait_kernel(const uint32_t* flag, uint32_t target, uint64_t limit_ns,
+                                  int* err) {
+  __shared__ int ok_s;
+  aoakv::cta_wait_geq(flag, target, &ok_s, err, limit_ns);
+}
+}  // namespace
+
+int aoakv_debug_wait_flag(const uint32_t* flag, uint32_t target, int32_t limit_us,
+                          void* stream) {
+  AOAKV_CHECK_ARG(flag != nullptr, "debug_wait_flag: flag is NULL");
+  AOAKV_CHECK_ARG(limit_us >= 1 && limit_us <= 1000000,
+                  "debug_wait_flag: limit_us must be in [1, 1000000]");
+  int* err = aoakv::dev_error_ptr();
+  if (!err) return aoakv::set_error(AOAKV_ERR_CUDA, "cannot resolve the device error word");
+  debug_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      flag, target, static_cast<uint64_t>(limit_us) * 1000ull, err);
+  AOAKV_CUDA_TRY(cudaGetLastError(), "debug_wait_flag launch");
   return AOAKV_OK;
 }
 

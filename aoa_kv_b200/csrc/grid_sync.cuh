@@ -20,11 +20,11 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Thread 0 spins until *p >= target or ~1 s has passed; the result is
-// broadcast through *ok_s. Returns false on timeout (AOAKV_DEV_ERR_TIMEOUT
-// recorded). Every thread of the CTA calls it.
+// Thread 0 spins until *p >= target or limit_ns (~1 s by default) has
+// passed; the result is broadcast through *ok_s. Returns false on timeout
+// (AOAKV_DEV_ERR_TIMEOUT recorded). Every thread of the CTA calls it.
 __device__ __forceinline__ bool cta_wait_geq(const uint32_t* p, uint32_t target, int* ok_s,
-                                             int* err) {
+                                             int* err, uint64_t limit_ns = kGridWaitNs) {
   if (threadIdx.x == 0) {
     int ok = 1;
     if (ld_acquire(p) < target) {
@@ -32,7 +32,7 @@ __device__ __forceinline__ bool cta_wait_geq(const uint32_t* p, uint32_t target,
       uint32_t it = 0;
       while (ld_acquire(p) < target) {
         if (++it > 64) __nanosleep(it < 1024 ? 64 : 256);
-        if ((it & 255u) == 0 && global_ns() - t0 > kGridWaitNs) {
+        if ((it & 255u) == 0 && global_ns() - t0 > limit_ns) {
           raise_dev_error(err, AOAKV_DEV_ERR_TIMEOUT);
           ok = 0;
           break;

@@ -72,6 +72,15 @@ AOAKV_API int aoakv_version(void);
  * current device. Synchronises the current device. */
 AOAKV_API int aoakv_get_device_error(int32_t* code_out, int32_t clear);
 
+/* Failure-path check (no reference counterpart): launches one CTA that
+ * waits until *flag >= target, bounded by limit_us microseconds, with the
+ * same bounded wait the fused step kernels use between phases. If the flag
+ * is never raised the wait expires, the kernel records
+ * AOAKV_DEV_ERR_TIMEOUT in the device error word and returns; the context
+ * stays usable. flag is device memory. */
+AOAKV_API int aoakv_debug_wait_flag(const uint32_t* flag, uint32_t target, int32_t limit_us,
+                                    void* stream);
+
 /* a1 — replaces append_kv_cache_decode
  *   (kernels/aoa_kv/quest/ops/csrc/bsk_ops.h:71-86, page.cu:6-105,
  *    kernel decode_page.cuh:392-506).

@@ -83,3 +83,21 @@ def test_step_workspace_size():
 def test_call_raises_with_message():
     with pytest.raises(aoa_kv_b200.AoaKvError, match="INVALID_ARG"):
         _lib.call("aoakv_topk_filtering", 1, 0, 10, None, 0, 1, 10, 0, None, 0, 1, 0, 0, None)
+
+
+def test_partial_decode_argument_checks():
+    f0 = ctypes.c_float(0.0)
+    _expect("aoakv_sparse_decode_partial", 1, 1, None, 1, 8, 1, 4, 4, 0, 1, 32, 128, 16, 0, f0,
+            None, 0, None, match="NULL")
+    _expect("aoakv_sparse_decode_partial", 1, 1, 1, 1, 8, 1, 4, 4, -2, 1, 32, 128, 16, 0, f0,
+            None, 0, None, match="last_page_idx")
+    # -1 ("the last page is on another GPU") is only for the partial decode
+    _expect("aoakv_sparse_decode", 1, 1, 1, 8, 1, 4, 4, -1, 1, 32, 128, 16, 0, f0, None, 0, None,
+            match="last_page_idx")
+
+
+def test_merge_and_map_argument_checks():
+    _expect("aoakv_merge_states", 1, 1, 0, 32, 128, 1, None, None, match="bad sizes")
+    _expect("aoakv_merge_states", None, 1, 2, 32, 128, 1, None, None, match="NULL")
+    _expect("aoakv_map_pages", 1, -1, 0, 4, 1, 1, None, match="bad sizes")
+    _expect("aoakv_map_pages", 1, 0, 0, 4, 1, 1, None, code=0)  # nothing to map: no launch
