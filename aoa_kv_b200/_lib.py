@@ -55,6 +55,9 @@ SIGNATURES = {
     "aoakv_decode_step": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p,
                           _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p,
                           _c_size, _c_p],
+    "aoakv_decode_step_grid": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p,
+                               _c_p, _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+                               _c_i32, _c_p, _c_p, _c_size, _c_i32, _c_p],
 }
 _RESTYPE = {"aoakv_last_error": ctypes.c_char_p}
 

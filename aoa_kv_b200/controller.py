@@ -245,10 +245,13 @@ class InferenceController:
         return self._step_ws
 
     def decode_step(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, layer_idx: int,
-                    out: torch.Tensor | None = None, selected: torch.Tensor | None = None):
+                    out: torch.Tensor | None = None, selected: torch.Tensor | None = None,
+                    max_ctas: int = 0):
         """Append k, v and attend q in one library call (append, estimate,
         top-k, sparse decode). Call after prepare_metadata(1) and
-        begin_forward(1). q, k, v: [1, H, D] or [H, D] fp16. Returns o like q."""
+        begin_forward(1). q, k, v: [1, H, D] or [H, D] fp16. Returns o like q.
+        max_ctas > 0 caps the fused kernel's grid (several requests' steps on
+        separate streams then run side by side)."""
         from .ops import _check_half_cuda, _ptr, _stream
         for name, t in (("q", q), ("k", k), ("v", v)):
             _check_half_cuda(t, name)
@@ -256,12 +259,16 @@ class InferenceController:
         ws = self._ensure_step_workspace()
         kv = self.kv_cache.buf_layer(layer_idx)
         meta = self.metadata_cache.buf_layer(layer_idx)
-        _lib.call("aoakv_decode_step", _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(kv),
-                  _ptr(self.kv_indices_with_last), len(self.kv_cache.indicies),
-                  self.kv_cache.last_page_len, kv.shape[0], _ptr(meta),
-                  _ptr(self.metadata_indices), meta.shape[0],
-                  _ptr(self.v_log_norm_layer(layer_idx)), self.num_heads, self.head_dim,
-                  self.page_size, self.step_page_budget(), self.score_mode,
-                  int(self.sink_first_page), _ptr(selected) if selected is not None else None,
-                  _ptr(ws), ws.numel(), _stream(q))
+        args = (_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(kv),
+                _ptr(self.kv_indices_with_last), len(self.kv_cache.indicies),
+                self.kv_cache.last_page_len, kv.shape[0], _ptr(meta),
+                _ptr(self.metadata_indices), meta.shape[0],
+                _ptr(self.v_log_norm_layer(layer_idx)), self.num_heads, self.head_dim,
+                self.page_size, self.step_page_budget(), self.score_mode,
+                int(self.sink_first_page), _ptr(selected) if selected is not None else None,
+                _ptr(ws), ws.numel())
+        if max_ctas:
+            _lib.call("aoakv_decode_step_grid", *args, int(max_ctas), _stream(q))
+        else:
+            _lib.call("aoakv_decode_step", *args, _stream(q))
         return o

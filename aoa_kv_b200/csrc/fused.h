@@ -32,9 +32,9 @@ struct FusedArgs {
 };
 
 // Returns 1 and the launch shape if the fused kernel can run this problem
-// with every CTA co-resident.
+// with every CTA co-resident; max_grid > 0 caps the grid.
 int fused_supported(int H, int D, int P, int n_score, int k_sel, int* grid, size_t* smem,
-                    int* chunk, int* n_chunks);
+                    int* chunk, int* n_chunks, int max_grid = 0);
 size_t fused_sync_bytes(int H);
 // The pipelined step kernel (step_pipe.cu): same arguments; its sync words
 // (1 + 2 * H / 8) fit in fused_sync_bytes(H).

@@ -74,7 +74,7 @@ struct StepChoice {
   size_t smem;
 };
 
-StepChoice choose_step(int H, int D, int P, int N, int k) {
+StepChoice choose_step(int H, int D, int P, int N, int k, int max_grid = 0) {
   const char* e = std::getenv("AOAKV_STEP_IMPL");
   const bool want_chain = e && std::strcmp(e, "chain") == 0;
   const bool want_pipe = e && std::strcmp(e, "pipe") == 0;
@@ -85,7 +85,8 @@ StepChoice choose_step(int H, int D, int P, int N, int k) {
     c.impl = StepImpl::kPipe;
     return c;
   }
-  if (fused_supported(H, D, P, N - 1, k - 1, &c.grid, &c.smem, &c.chunk, &c.n_chunks))
+  if (fused_supported(H, D, P, N - 1, k - 1, &c.grid, &c.smem, &c.chunk, &c.n_chunks,
+                      max_grid))
     c.impl = StepImpl::kFused;
   return c;
 }
@@ -126,14 +127,16 @@ extern "C" int aoakv_step_launches(int32_t num_heads, int32_t head_dim, int32_t 
   return AOAKV_OK;
 }
 
-extern "C" int aoakv_decode_step(
+namespace {
+
+int decode_step_impl(
     const void* q, const void* k_new, const void* v_new, void* o, void* kv_data,
     const int32_t* kv_indices, int32_t num_kv_pages, int32_t kv_last_page_len,
     int32_t kv_capacity_pages, void* metadata_data, const int32_t* metadata_indices,
     int32_t metadata_capacity_pages, void* v_log_norm, int32_t num_heads,
     int32_t head_dim, int32_t page_size, int32_t page_budget, int32_t score_mode,
     int32_t sink_first_page, int32_t* selected_out, void* workspace,
-    size_t workspace_bytes, void* stream) {
+    size_t workspace_bytes, void* stream, int max_ctas) {
   AOAKV_CHECK_ARG(q && k_new && v_new && o && kv_data && kv_indices && metadata_data &&
                       metadata_indices && v_log_norm,
                   "step: NULL pointer argument");
@@ -167,7 +170,7 @@ extern "C" int aoakv_decode_step(
   uint8_t* ws = static_cast<uint8_t*>(workspace);
 
   if (sparse) {
-    const StepChoice sc = choose_step(H, D, P, N, k);
+    const StepChoice sc = choose_step(H, D, P, N, k, max_ctas);
     const int grid = sc.grid, chunk = sc.chunk, n_chunks = sc.n_chunks;
     const size_t smem = sc.smem;
     if (sc.impl != StepImpl::kChain) {
@@ -327,4 +330,37 @@ extern "C" int aoakv_decode_step(
     AOAKV_CUDA_TRY(cudaGetLastError(), "fill_selected launch");
   }
   return AOAKV_OK;
+}
+
+}  // namespace
+
+extern "C" int aoakv_decode_step(
+    const void* q, const void* k_new, const void* v_new, void* o, void* kv_data,
+    const int32_t* kv_indices, int32_t num_kv_pages, int32_t kv_last_page_len,
+    int32_t kv_capacity_pages, void* metadata_data, const int32_t* metadata_indices,
+    int32_t metadata_capacity_pages, void* v_log_norm, int32_t num_heads,
+    int32_t head_dim, int32_t page_size, int32_t page_budget, int32_t score_mode,
+    int32_t sink_first_page, int32_t* selected_out, void* workspace,
+    size_t workspace_bytes, void* stream) {
+  return decode_step_impl(q, k_new, v_new, o, kv_data, kv_indices, num_kv_pages,
+                          kv_last_page_len, kv_capacity_pages, metadata_data, metadata_indices,
+                          metadata_capacity_pages, v_log_norm, num_heads, head_dim, page_size,
+                          page_budget, score_mode, sink_first_page, selected_out, workspace,
+                          workspace_bytes, stream, 0);
+}
+
+extern "C" int aoakv_decode_step_grid(
+    const void* q, const void* k_new, const void* v_new, void* o, void* kv_data,
+    const int32_t* kv_indices, int32_t num_kv_pages, int32_t kv_last_page_len,
+    int32_t kv_capacity_pages, void* metadata_data, const int32_t* metadata_indices,
+    int32_t metadata_capacity_pages, void* v_log_norm, int32_t num_heads,
+    int32_t head_dim, int32_t page_size, int32_t page_budget, int32_t score_mode,
+    int32_t sink_first_page, int32_t* selected_out, void* workspace,
+    size_t workspace_bytes, int32_t max_ctas, void* stream) {
+  AOAKV_CHECK_ARG(max_ctas >= 0, "step: max_ctas must be >= 0");
+  return decode_step_impl(q, k_new, v_new, o, kv_data, kv_indices, num_kv_pages,
+                          kv_last_page_len, kv_capacity_pages, metadata_data, metadata_indices,
+                          metadata_capacity_pages, v_log_norm, num_heads, head_dim, page_size,
+                          page_budget, score_mode, sink_first_page, selected_out, workspace,
+                          workspace_bytes, stream, max_ctas);
 }

@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(kFThreads, 2)
 }  // namespace
 
 int fused_supported(int H, int D, int P, int n_score, int k_sel, int* grid_out,
-                    size_t* smem_out, int* chunk_out, int* n_chunks_out) {
+                    size_t* smem_out, int* chunk_out, int* n_chunks_out, int max_grid) {
   const int k_slots = k_sel + 1;
   const void* fn = D == 128 ? reinterpret_cast<const void*>(fused_step_kernel<128>)
                             : reinterpret_cast<const void*>(fused_step_kernel<64>);
@@ -295,7 +295,8 @@ int fused_supported(int H, int D, int P, int n_score, int k_sel, int* grid_out,
             cudaSuccess ||
         occ < 1)
       return 0;
-    const int grid = occ * num_sms();
+    int grid = occ * num_sms();
+    if (max_grid > 0 && max_grid < grid) grid = max_grid;
     const int n_chunks = (k_slots + chunk - 1) / chunk;
     const int n_units = H * n_chunks;
     if (grid < H) return 0;

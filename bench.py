@@ -24,6 +24,8 @@ With --gpus N (torchrun, one process per GPU) every rank serves its own
 request (request sharding, no collective): scaling "weak".
 --mode longctx instead splits ONE 128K-context request (budget 4096) by page
 range over the GPUs, with two NCCL all_gathers per layer: scaling "strong".
+--mode batched runs 32 requests of 4K-16K tokens (config 4), balanced over
+the GPUs by bytes, no collective: scaling "strong".
 --impl reference times the reference's CPU simulation path (the numpy port
 in oracle/sim.py of filter_util.py + quest_attention.py) on the host cores.
 """
@@ -57,9 +59,15 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--mode", choices=["headline", "longctx"], default="headline",
+    ap.add_argument("--mode", choices=["headline", "longctx", "batched"], default="headline",
                     help="headline: 32K ctx, 1K budget, one request per GPU; longctx: one "
-                         "128K-context request split by page range over the GPUs")
+                         "128K-context request split by page range over the GPUs; batched: "
+                         "--requests requests of 4K-16K tokens balanced over the GPUs")
+    ap.add_argument("--requests", type=int, default=32, help="batched: requests in the batch")
+    ap.add_argument("--streams", type=int, default=8,
+                    help="batched: requests' steps run side by side on this many streams, each "
+                         "step's fused kernel capped to its share of the GPU (1 = one after "
+                         "another on the whole GPU)")
     ap.add_argument("--layers", type=int, default=None, help="default 32 (headline), 4 (longctx)")
     ap.add_argument("--ctx", type=int, default=None, help="default 32768 (headline), 131072 (longctx)")
     ap.add_argument("--budget", type=int, default=None,
@@ -75,7 +83,7 @@ def parse():
     ap.add_argument("--no-graph", action="store_true", help="longctx: launch without a CUDA graph")
     a = ap.parse_args()
     long = a.mode == "longctx"
-    a.layers = a.layers or (4 if long else 32)
+    a.layers = a.layers or (4 if a.mode != "headline" else 32)
     a.ctx = a.ctx or (131072 if long else 32768)
     a.budget = a.budget or (4096 if long else 1024)
     return a
@@ -634,12 +642,147 @@ def run_longctx(a):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------ batched decode
+BATCH_METRIC = "sparse-decode µs/layer for a batch of 32 requests (4K-16K ctx, 1K budget)"
+
+
+def run_batched(a):
+    """Config 4: a.requests independent requests, context U[4096, 16384]
+    tokens in whole pages (seed 3), budget a.budget, balanced over the job's
+    GPUs by bytes (aoa_kv_b200.batching); each GPU runs its requests' steps
+    (one fused launch per request and layer) in a CUDA graph. No collective
+    on the data path; the total work is fixed: scaling "strong"."""
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import aoa_kv_b200 as ak
+    from aoa_kv_b200 import batching
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    ak._lib.load()
+    g = np.random.default_rng(3)
+    ctxs = [int(c) * P for c in g.integers(4096 // P, 16384 // P + 1, size=a.requests)]
+    weights = [batching.step_bytes(c, a.budget, H, D, P, a.method) for c in ctxs]
+    mine = batching.balance_requests(weights, world)[rank]
+    reqs = []
+    for r in mine:
+        gen = torch.Generator(device=dev).manual_seed(3000 + r)
+        S = ctxs[r]
+        ctl = ak.InferenceController(a.layers, H, D, P, a.budget // P, S + P, torch.float16, dev,
+                                     method=a.method)
+        ctl.prepare_metadata(S - 1)
+        ctl.begin_forward(S - 1)
+        news = []
+        for layer in range(a.layers):
+            scale = torch.exp(torch.randn(H, D, device=dev, generator=gen))
+            K = (torch.randn(S, H, D, device=dev, generator=gen) * scale).half()
+            V = torch.randn(S, H, D, device=dev, generator=gen).half()
+            q = torch.randn(1, H, D, device=dev, generator=gen).half()
+            ak.append_kv(K[:-1].contiguous(), V[:-1].contiguous(), ctl, layer)
+            news.append((q, K[-1:].contiguous(), V[-1:].contiguous(),
+                         torch.empty(1, H, D, dtype=torch.float16, device=dev)))
+            del K, V
+        ctl.end_forward()
+        ctl.prepare_metadata(1)
+        ctl.begin_forward(1)
+        reqs.append((ctl, news))
+    torch.cuda.synchronize()
+
+    n_streams = max(1, min(a.streams, len(reqs)))
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    cap = 0 if n_streams == 1 else max(64, (2 * sms // n_streams) // 2 * 2)
+    lanes = [torch.cuda.Stream(device=dev) for _ in range(n_streams)]
+    order = sorted(range(len(reqs)), key=lambda i: -weights[mine[i]])
+    lane_of = {i: j % n_streams for j, i in enumerate(order)}
+
+    def one_step():
+        # fork: every lane waits for the issuing stream; join at the end
+        main = torch.cuda.current_stream()
+        for ln in lanes:
+            ln.wait_stream(main)
+        for layer in range(a.layers):
+            for i, (ctl, news) in enumerate(reqs):
+                q, k, v, o = news[layer]
+                with torch.cuda.stream(lanes[lane_of[i]]):
+                    ctl.decode_step(q, k, v, layer, out=o, max_ctas=cap)
+        for ln in lanes:
+            main.wait_stream(ln)
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        one_step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        one_step()
+    for _ in range(a.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    ak.check_device()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(a.steps):
+        graph.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ak.check_device()
+    us = ms * 1e3 / (a.steps * a.layers)
+    total_bytes = sum(weights)
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    peak = float(peaks.get("hbm_gbs") or 6650.0)
+    ach = total_bytes / (us * 1e-6) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": BATCH_METRIC.replace("32 requests", f"{a.requests} requests"),
+            "value": round(us, 3), "unit": "us", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4), "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": f"{a.requests} requests, ctx U[4096,16384] tokens (seed 3), "
+                                   f"budget {a.budget}, {a.layers}-layer step",
+                       "requests_on_rank0": len(mine), "bytes_per_layer_step": total_bytes,
+                       "streams": n_streams, "ctas_per_step": cap or "whole GPU",
+                       "parallelism": f"request-sharded x{world} (greedy byte balance), "
+                                      f"no collective"},
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak * world,
+                         "unit": "GB/s", "frac": round(ach / (peak * world), 4),
+                         "note": "peak = measured HBM GB/s x GPUs"},
+        }), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         run_reference(a)
     elif a.mode == "longctx":
         run_longctx(a)
+    elif a.mode == "batched":
+        run_batched(a)
     else:
         run_ours(a)
 

@@ -290,6 +290,20 @@ AOAKV_API int aoakv_decode_step(
     int32_t* selected_out, void* workspace, size_t workspace_bytes,
     void* stream);
 
+/* aoakv_decode_step with the fused kernel's grid capped at max_ctas CTAs
+ * (0 = the whole GPU; no reference counterpart). A capped step leaves the
+ * rest of the GPU free, so the steps of several independent requests can
+ * run concurrently on separate streams (batched decode); results are the
+ * same as with the whole GPU. */
+AOAKV_API int aoakv_decode_step_grid(
+    const void* q, const void* k_new, const void* v_new, void* o, void* kv_data,
+    const int32_t* kv_indices, int32_t num_kv_pages, int32_t kv_last_page_len,
+    int32_t kv_capacity_pages, void* metadata_data, const int32_t* metadata_indices,
+    int32_t metadata_capacity_pages, void* v_log_norm, int32_t num_heads,
+    int32_t head_dim, int32_t page_size, int32_t page_budget, int32_t score_mode,
+    int32_t sink_first_page, int32_t* selected_out, void* workspace,
+    size_t workspace_bytes, int32_t max_ctas, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

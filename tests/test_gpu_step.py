@@ -218,3 +218,37 @@ def test_step_repeated_calls_keep_workspace_clean(cuda):
         assert np.abs(o.float().cpu().numpy() - want_o).max() < 2e-3, t
     cnt = ws[: H * 4].view(torch.int32)
     assert int(cnt.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("max_ctas", [64, 74, 148])
+def test_step_grid_capped_matches_oracle(cuda, max_ctas):
+    """aoakv_decode_step_grid: the fused kernel on a fraction of the GPU (the
+    batched-decode configuration) gives the oracle's selection and output."""
+    H, D, P, budget, S, mode = 32, 128, 16, 64, 8192 + 5, "aoakv"
+    q, K, V = gen_qkv(S + max_ctas, H, S, D, "outlier")
+    n, last = (S + P - 1) // P, (S - 1) % P + 1
+    lay = GpuLayer(n + 1, H, D, P, seed=S + max_ctas)
+    lay.fill(K[:-1], V[:-1])
+    torch.cuda.synchronize()
+    ref = lay.snapshot()
+    ws_n = _lib.size_query("aoakv_step_workspace_size", H, D, lay.cap, budget)
+    ws = torch.zeros(ws_n, dtype=torch.uint8, device="cuda")
+    sel = torch.full((H, budget), -9, dtype=torch.int32, device="cuda")
+    o = torch.empty(H, D, dtype=torch.float16, device="cuda")
+    qd, kd, vd = (torch.from_numpy(x).cuda() for x in (q, K[-1], V[-1]))
+    _lib.call("aoakv_decode_step_grid", ptr(qd), ptr(kd), ptr(vd), ptr(o), ptr(lay.kv),
+              ptr(lay.kv_idx), n, last, lay.cap, ptr(lay.meta), ptr(lay.meta_idx), lay.mcap,
+              ptr(lay.vlog), H, D, P, budget, _lib.SCORE_AOAKV, 0, ptr(sel), ptr(ws), ws_n,
+              max_ctas, stream())
+    torch.cuda.synchronize()
+    want_o, want_sel = kt.step(q, K[-1], V[-1], ref, lay.kv_idx_np, lay.meta_idx_np, n, last,
+                               budget, mode, False)
+    got_sel = sel.cpu().numpy()
+    g_log = np.array(logical(got_sel, lay.kv_idx_np, n))
+    w_log = np.array(logical(want_sel, lay.kv_idx_np, n))
+    scores = kt.estimate(q, ref, lay.meta_idx_np, lay.kv_idx_np, n, mode)
+    scores = np.concatenate([scores, np.full((H, 1), np.inf, np.float32)], axis=1)
+    assert not selection_mismatch(g_log, w_log, scores)
+    if np.array_equal(g_log, w_log):
+        assert np.abs(o.float().cpu().numpy() - want_o).max() < 2e-3
+    assert _lib.device_error() == 0

@@ -57,3 +57,25 @@ def test_begin_forward_decode_needs_two_pages():
     ic.prepare_metadata(1)
     with pytest.raises(AssertionError):
         ic.begin_forward(1)
+
+
+def test_balance_requests_is_a_partition_and_balanced():
+    from aoa_kv_b200 import batching
+    import numpy as np
+    g = np.random.default_rng(3)
+    ctxs = [int(c) * 16 for c in g.integers(256, 1025, size=32)]
+    w = [batching.step_bytes(c, 1024, 32, 128, 16) for c in ctxs]
+    for n in (1, 2, 3, 4, 8):
+        parts = batching.balance_requests(w, n)
+        assert sorted(r for p in parts for r in p) == list(range(32))
+        loads = [sum(w[r] for r in p) for p in parts]
+        # LPT bound: no GPU above the mean by more than the largest request
+        assert max(loads) <= sum(w) / n + max(w)
+    assert batching.balance_requests([5, 5], 2) == [[0], [1]]
+
+
+def test_step_bytes_matches_headline_figure():
+    from aoa_kv_b200 import batching
+    assert batching.step_bytes(32768, 1024, 32, 128, 16, "aoakv") == 50_462_656
+    # dense when the context fits the budget: every page, no metadata
+    assert batching.step_bytes(1024, 1024, 32, 128, 16) == 64 * 16 * 8192 * 2 + 16384
