@@ -158,6 +158,8 @@ class InferenceController:
         self.topk_dindices_buffer = None
         self.topk_buf = None
         self._step_ws = None
+        self._step_ws_key = None
+        self._layer_ptrs: dict = {}
 
     @property
     def score_mode(self) -> int:
@@ -238,11 +240,26 @@ class InferenceController:
         return self._page_budget
 
     def _ensure_step_workspace(self) -> torch.Tensor:
-        need = _lib.size_query("aoakv_step_workspace_size", self.num_heads, self.head_dim,
-                               self.kv_cache.pool.capacity, max(3, self._page_budget))
-        if self._step_ws is None or self._step_ws.numel() < need:
-            self._step_ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        key = (self.kv_cache.pool.capacity, max(3, self._page_budget))
+        if self._step_ws is None or self._step_ws_key != key:
+            need = _lib.size_query("aoakv_step_workspace_size", self.num_heads, self.head_dim,
+                                   *key)
+            if self._step_ws is None or self._step_ws.numel() < need:
+                self._step_ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+            self._step_ws_key = key
         return self._step_ws
+
+    def _layer_buffers(self, layer_idx: int):
+        """(kv ptr, kv pages, metadata ptr, metadata pages, v_log_norm ptr) of
+        a layer; the pools never move, so this is computed once per layer."""
+        t = self._layer_ptrs.get(layer_idx)
+        if t is None:
+            kv = self.kv_cache.buf_layer(layer_idx)
+            meta = self.metadata_cache.buf_layer(layer_idx)
+            t = (kv.data_ptr(), kv.shape[0], meta.data_ptr(), meta.shape[0],
+                 self.v_log_norm_layer(layer_idx).data_ptr())
+            self._layer_ptrs[layer_idx] = t
+        return t
 
     def decode_step(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, layer_idx: int,
                     out: torch.Tensor | None = None, selected: torch.Tensor | None = None,
@@ -257,13 +274,11 @@ class InferenceController:
             _check_half_cuda(t, name)
         o = torch.empty_like(q) if out is None else out
         ws = self._ensure_step_workspace()
-        kv = self.kv_cache.buf_layer(layer_idx)
-        meta = self.metadata_cache.buf_layer(layer_idx)
-        args = (_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(kv),
+        kv_p, kv_cap, meta_p, meta_cap, vlog_p = self._layer_buffers(layer_idx)
+        args = (_ptr(q), _ptr(k), _ptr(v), _ptr(o), kv_p,
                 _ptr(self.kv_indices_with_last), len(self.kv_cache.indicies),
-                self.kv_cache.last_page_len, kv.shape[0], _ptr(meta),
-                _ptr(self.metadata_indices), meta.shape[0],
-                _ptr(self.v_log_norm_layer(layer_idx)), self.num_heads, self.head_dim,
+                self.kv_cache.last_page_len, kv_cap, meta_p,
+                _ptr(self.metadata_indices), meta_cap, vlog_p, self.num_heads, self.head_dim,
                 self.page_size, self.step_page_budget(), self.score_mode,
                 int(self.sink_first_page), _ptr(selected) if selected is not None else None,
                 _ptr(ws), ws.numel())
