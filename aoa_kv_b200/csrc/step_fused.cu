@@ -210,10 +210,18 @@ __global__ void __launch_bounds__(kFThreads, 2)
   if (!cta_wait_geq(est_done, static_cast<uint32_t>(G), &ok_s, f.err)) return;
   AOAKV_STAMP(2);
   pdl_launch_dependents();  // the next kernel may launch (it waits for our completion)
-  if (threadIdx.x == 0 && atomicAdd(passed, 1u) == static_cast<uint32_t>(G - 1)) {
-    *est_done = 0u;  // every CTA has passed its wait
-    *passed = 0u;
-  }
+  // re-arm: the CTA whose ticket is G - 1 knows every CTA has passed the
+  // wait; the ticket is read only after this CTA's top-k, so the atomic's
+  // round trip is not on its critical path
+  uint32_t pass_ticket = 0u;
+  if (threadIdx.x == 0) pass_ticket = atomicAdd(passed, 1u);
+  auto rearm = [&]() {
+    if (threadIdx.x == 0 && pass_ticket == static_cast<uint32_t>(G - 1)) {
+      *est_done = 0u;
+      *passed = 0u;
+    }
+    pass_ticket = 0u;
+  };
 
   // ---- T + D: this CTA's units [u_lo, u_hi), contiguous, possibly 2 heads
   float* mrg = reinterpret_cast<float*>(smem + kDecHeader);
@@ -258,6 +266,7 @@ __global__ void __launch_bounds__(kFThreads, 2)
               i == f.k_sel ? __ldg(f.kv_indices + f.n_pages - 1) : -1;
       __syncthreads();
       AOAKV_STAMP(3);
+      rearm();
     }
     if (spare_append && c == n_chunks - 1) {  // this unit attends the last page
       if (!cta_wait_geq(appended + h, 1u, &ok_s, f.err)) return;
@@ -274,6 +283,7 @@ __global__ void __launch_bounds__(kFThreads, 2)
       if (tok_s[j] > 0) phase_bits ^= 1u << j;
     __syncthreads();
   }
+  rearm();  // a CTA without decode units re-arms here
 }
 
 }  // namespace
