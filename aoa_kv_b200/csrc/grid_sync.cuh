@@ -31,7 +31,7 @@ __device__ __forceinline__ bool cta_wait_geq(const uint32_t* p, uint32_t target,
       const uint64_t t0 = global_ns();
       uint32_t it = 0;
       while (ld_acquire(p) < target) {
-        if (++it > 64) __nanosleep(it < 1024 ? 64 : 256);
+        if (++it > 2048) __nanosleep(it < 8192 ? 64 : 256);  // each poll is a round trip
         if ((it & 255u) == 0 && global_ns() - t0 > limit_ns) {
           raise_dev_error(err, AOAKV_DEV_ERR_TIMEOUT);
           ok = 0;
