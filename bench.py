@@ -26,7 +26,8 @@ request (request sharding, no collective): scaling "weak".
 --mode longctx instead splits ONE 128K-context request (budget 4096) by page
 range over the GPUs, with two NCCL all_gathers per layer: scaling "strong".
 --mode batched runs 32 requests of 4K-16K tokens (config 4), balanced over
-the GPUs by bytes, no collective: scaling "strong".
+the GPUs by bytes, no collective: scaling "strong". --mode model times a
+32-layer Llama-2-7B-shaped decode step with this attention (config 3).
 --impl reference times the reference's CPU simulation path (the numpy port
 in oracle/sim.py of filter_util.py + quest_attention.py) on the host cores.
 """
@@ -60,10 +61,12 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--mode", choices=["headline", "longctx", "batched"], default="headline",
+    ap.add_argument("--mode", choices=["headline", "longctx", "batched", "model"],
+                    default="headline",
                     help="headline: 32K ctx, 1K budget, one request per GPU; longctx: one "
                          "128K-context request split by page range over the GPUs; batched: "
-                         "--requests requests of 4K-16K tokens balanced over the GPUs")
+                         "--requests requests of 4K-16K tokens balanced over the GPUs; "
+                         "model: a 32-layer Llama-2-7B-shaped decode step (random weights)")
     ap.add_argument("--requests", type=int, default=32, help="batched: requests in the batch")
     ap.add_argument("--streams", type=int, default=8,
                     help="batched: requests' steps run side by side on this many streams, each "
@@ -776,6 +779,148 @@ def run_batched(a):
         dist.destroy_process_group()
 
 
+# ------------------------------------------- Llama-2-7B-shaped decode step
+MODEL_METRIC = "ms/token, 32-layer Llama-2-7B-shaped decode, sparse attention (layers 2-31)"
+
+
+def run_model(a):
+    """Config 3: one decode token through a 32-layer Llama-2-7B-shaped model
+    with random fp16 weights (hidden 4096, 32 heads, head_dim 128, MLP 11008,
+    vocab 32000): RMSNorm, q/k/v GEMVs, RoPE, attention through
+    InferenceController.decode_step (layers 0-1 dense, as in the reference's
+    skip layers, llama.py:428-439; the rest with the token budget), o_proj,
+    SwiGLU MLP, final norm, LM head and a device-side argmax, captured in one
+    CUDA graph. The KV caches hold a.ctx synthetic tokens per layer. The
+    GEMVs are torch (cuBLAS); the attention share is timed separately by
+    replaying a graph of only the attention calls."""
+    import torch
+
+    import aoa_kv_b200 as ak
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    ak._lib.load()
+    L, HID, FF, VOCAB = 32, 4096, 11008, 32000
+    gen = torch.Generator(device=dev).manual_seed(a.seed)
+
+    def w(*shape):
+        return (torch.randn(*shape, device=dev, generator=gen) * 0.02).half()
+
+    layers = [dict(ln1=torch.ones(HID, device=dev, dtype=torch.float16), wq=w(HID, HID),
+                   wk=w(HID, HID), wv=w(HID, HID), wo=w(HID, HID),
+                   ln2=torch.ones(HID, device=dev, dtype=torch.float16), wg=w(HID, FF),
+                   wu=w(HID, FF), wd=w(FF, HID)) for _ in range(L)]
+    emb, lm_head = w(VOCAB, HID), w(HID, VOCAB)
+    norm_f = torch.ones(HID, device=dev, dtype=torch.float16)
+    weight_bytes = sum(t.numel() * 2 for lw in layers for t in lw.values()) + \
+        (emb.numel() + lm_head.numel() + norm_f.numel()) * 2
+
+    S = a.ctx
+    ctl = ak.InferenceController(L, H, D, P, a.budget // P, S + P, torch.float16, dev,
+                                 method=a.method)
+    ctl.prepare_metadata(S - 1)
+    ctl.begin_forward(S - 1)
+    for layer in range(L):
+        scale = torch.exp(torch.randn(H, D, device=dev, generator=gen))
+        K = (torch.randn(S - 1, H, D, device=dev, generator=gen) * scale).half()
+        V = torch.randn(S - 1, H, D, device=dev, generator=gen).half()
+        ak.append_kv(K, V, ctl, layer)
+        del K, V
+    ctl.end_forward()
+    ctl.prepare_metadata(1)
+    ctl.begin_forward(1)
+    dense_budget = ctl.kv_cache.pool.capacity  # layers 0-1: every page
+    sparse_budget = a.budget // P
+
+    # RoPE at the new token's position (theta 10000, rotate-half convention)
+    pos = S - 1
+    inv = 1.0 / (10000.0 ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D))
+    ang = pos * inv
+    cos = torch.cat([ang.cos(), ang.cos()]).half()
+    sin = torch.cat([ang.sin(), ang.sin()]).half()
+
+    def rope(x):  # x [1, H, D]
+        x1, x2 = x[..., : D // 2], x[..., D // 2:]
+        return x * cos + torch.cat([-x2, x1], dim=-1) * sin
+
+    def rmsnorm(x, g):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5)).half() * g
+
+    token = torch.zeros(1, dtype=torch.long, device=dev)
+    q_buf = torch.empty(L, 1, H, D, dtype=torch.float16, device=dev)
+    k_buf = torch.empty_like(q_buf)
+    v_buf = torch.empty_like(q_buf)
+    o_buf = torch.empty_like(q_buf)
+    for layer in (0, 1):  # size the step workspace for the dense layers outside capture
+        ctl.set_page_budget(dense_budget)
+        ctl._ensure_step_workspace()
+    ctl.set_page_budget(sparse_budget)
+
+    def attention(layer):
+        ctl.set_page_budget(dense_budget if layer < 2 else sparse_budget)
+        ctl.decode_step(q_buf[layer], k_buf[layer], v_buf[layer], layer, out=o_buf[layer])
+
+    def token_step():
+        x = emb[token]  # [1, HID]
+        for layer, lw in enumerate(layers):
+            h = rmsnorm(x, lw["ln1"])
+            q_buf[layer].copy_(rope((h @ lw["wq"]).view(1, H, D)))
+            k_buf[layer].copy_(rope((h @ lw["wk"]).view(1, H, D)))
+            v_buf[layer].copy_((h @ lw["wv"]).view(1, H, D))
+            attention(layer)
+            x = x + o_buf[layer].view(1, HID) @ lw["wo"]
+            h = rmsnorm(x, lw["ln2"])
+            x = x + (torch.nn.functional.silu(h @ lw["wg"]) * (h @ lw["wu"])) @ lw["wd"]
+        logits = rmsnorm(x, norm_f) @ lm_head
+        token.copy_(logits.argmax(dim=-1))
+
+    def attention_only():
+        for layer in range(L):
+            attention(layer)
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        token_step()
+        attention_only()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g_tok, g_att = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_tok):
+        token_step()
+    with torch.cuda.graph(g_att):
+        attention_only()
+
+    def timed(graph):
+        for _ in range(a.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / a.steps
+
+    ms_tok = timed(g_tok)
+    ms_att = timed(g_att)
+    ak.check_device()
+    print(json.dumps({
+        "metric": MODEL_METRIC, "value": round(ms_tok, 4), "unit": "ms", "n_gpus": 1,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_tok, 4),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic",
+        "config": {"workload": f"Llama-2-7B-shaped decode, random weights, ctx {S}, "
+                               f"budget {a.budget}, layers 0-1 dense",
+                   "weight_bytes": weight_bytes, "context_tokens": S, "token_budget": a.budget},
+        "attention_ms_per_token": round(ms_att, 4),
+        "attention_share": round(ms_att / ms_tok, 4),
+        "weights_ideal_ms": round(weight_bytes / (6452.2e9) * 1e3, 4),
+    }), flush=True)
+    del g_tok, g_att
+
+
 def main():
     a = parse()
     if a.impl == "reference":
@@ -784,6 +929,8 @@ def main():
         run_longctx(a)
     elif a.mode == "batched":
         run_batched(a)
+    elif a.mode == "model":
+        run_model(a)
     else:
         run_ours(a)
 
