@@ -154,8 +154,17 @@ def prefill_forward(q, iController, layer_idx, rope_scale=None, rope_theta=None)
     _not_built("prefill_forward", "utils/__init__.py:133-175")
 
 
-def apply_rope_in_place(q, k, past_kv_len, rope_scale=None, rope_theta=None):
-    _not_built("apply_rope_in_place", "utils/__init__.py:25-52")
+def apply_rope_in_place(q: torch.Tensor, k: torch.Tensor, past_kv_len: int,
+                        rope_scale: Optional[float] = None, rope_theta: Optional[float] = None):
+    """utils/__init__.py:25-52: RoPE in place on q, k [N, H, D] fp16 (NHD),
+    token t at position past_kv_len + t; scale 1 and theta 1e4 by default."""
+    _check_half_cuda(q, "q")
+    _check_half_cuda(k, "k")
+    if q.dim() != 3 or q.shape != k.shape:
+        raise RuntimeError("q and k must be [seq_len, num_heads, head_dim] of equal shape")
+    _lib.call("aoakv_apply_rope_in_place", _ptr(q), _ptr(k), q.size(0), int(past_kv_len),
+              q.size(1), q.size(2), 1.0 if rope_scale is None else float(rope_scale),
+              1e4 if rope_theta is None else float(rope_theta), _stream(q))
 
 
 def rms_norm_forward(input, weight, epsilon):

@@ -110,8 +110,9 @@ def prefill_with_paged_kv_cache(*args, **kwargs):
     _ops._not_built("prefill_with_paged_kv_cache", "ops/csrc/batch_prefill.cu")
 
 
-def apply_rope_in_place(*args, **kwargs):
-    _ops._not_built("apply_rope_in_place", "ops/csrc/page.cu:224-264")
+def apply_rope_in_place(q, k, past_kv_len, rope_scale, rope_theta):
+    """page.cu:224-264 (pybind apply_rope_in_place)."""
+    _ops.apply_rope_in_place(q, k, past_kv_len, rope_scale, rope_theta)
 
 
 def rms_norm_forward(*args, **kwargs):

@@ -786,7 +786,8 @@ MODEL_METRIC = "ms/token, 32-layer Llama-2-7B-shaped decode, sparse attention (l
 def run_model(a):
     """Config 3: one decode token through a 32-layer Llama-2-7B-shaped model
     with random fp16 weights (hidden 4096, 32 heads, head_dim 128, MLP 11008,
-    vocab 32000): RMSNorm, q/k/v GEMVs, RoPE, attention through
+    vocab 32000): RMSNorm, q/k/v GEMVs, RoPE (aoakv_apply_rope_in_place),
+    attention through
     InferenceController.decode_step (layers 0-1 dense, as in the reference's
     skip layers, llama.py:428-439; the rest with the token budget), o_proj,
     SwiGLU MLP, final norm, LM head and a device-side argmax, captured in one
@@ -831,16 +832,6 @@ def run_model(a):
     dense_budget = ctl.kv_cache.pool.capacity  # layers 0-1: every page
     sparse_budget = a.budget // P
 
-    # RoPE at the new token's position (theta 10000, rotate-half convention)
-    pos = S - 1
-    inv = 1.0 / (10000.0 ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D))
-    ang = pos * inv
-    cos = torch.cat([ang.cos(), ang.cos()]).half()
-    sin = torch.cat([ang.sin(), ang.sin()]).half()
-
-    def rope(x):  # x [1, H, D]
-        x1, x2 = x[..., : D // 2], x[..., D // 2:]
-        return x * cos + torch.cat([-x2, x1], dim=-1) * sin
 
     def rmsnorm(x, g):
         xf = x.float()
@@ -864,9 +855,11 @@ def run_model(a):
         x = emb[token]  # [1, HID]
         for layer, lw in enumerate(layers):
             h = rmsnorm(x, lw["ln1"])
-            q_buf[layer].copy_(rope((h @ lw["wq"]).view(1, H, D)))
-            k_buf[layer].copy_(rope((h @ lw["wk"]).view(1, H, D)))
+            q_buf[layer].copy_((h @ lw["wq"]).view(1, H, D))
+            k_buf[layer].copy_((h @ lw["wk"]).view(1, H, D))
             v_buf[layer].copy_((h @ lw["wv"]).view(1, H, D))
+            # RoPE at the new token's position (this library's kernel)
+            ak.apply_rope_in_place(q_buf[layer], k_buf[layer], S - 1)
             attention(layer)
             x = x + o_buf[layer].view(1, HID) @ lw["wo"]
             h = rmsnorm(x, lw["ln2"])

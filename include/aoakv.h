@@ -81,6 +81,17 @@ AOAKV_API int aoakv_get_device_error(int32_t* code_out, int32_t clear);
 AOAKV_API int aoakv_debug_wait_flag(const uint32_t* flag, uint32_t target, int32_t limit_us,
                                     void* stream);
 
+/* RoPE — replaces apply_rope_in_place (bsk_ops.h:23-27, page.cu:224-264,
+ * kernel decode_page.cuh:786-869). In place on q and k, NHD
+ * [seq_len, num_heads, head_dim] fp16: token t at position past_kv_len + t,
+ * channel i rotated with its partner i +- head_dim/2 by the angle
+ * position * (1/rope_scale) * (1/rope_theta)^(2 (i mod head_dim/2) / head_dim)
+ * (rotate-half convention). Angles are evaluated in fp32 with an accurate
+ * sine/cosine. */
+AOAKV_API int aoakv_apply_rope_in_place(void* q, void* k, int32_t seq_len, int32_t past_kv_len,
+                                        int32_t num_heads, int32_t head_dim, float rope_scale,
+                                        float rope_theta, void* stream);
+
 /* a1 — replaces append_kv_cache_decode
  *   (kernels/aoa_kv/quest/ops/csrc/bsk_ops.h:71-86, page.cu:6-105,
  *    kernel decode_page.cuh:392-506).

@@ -120,6 +120,27 @@ def estimate(q: np.ndarray, c: LayerCache, meta_indices: np.ndarray, kv_indices:
     return (F32(2.0 / math.sqrt(D)) * s + F32(2) * vl).astype(F32)
 
 
+def apply_rope(x: np.ndarray, past_kv_len: int, rope_scale: float = 1.0,
+               rope_theta: float = 1e4) -> np.ndarray:
+    """page.cu:224-264 / decode_page.cuh:786-869 (FlashInfer's llama rotate-
+    half RoPE): token t at position past_kv_len + t, channel i with
+    j = i mod D/2 rotated by angle pos * (1/scale) * (1/theta)^(2j/D) against
+    its partner i +- D/2. The frequency and the angle are fp32 products as in
+    the kernel; sine and cosine are exact. x [N, H, D] fp16 -> fp16."""
+    N, H, D = x.shape
+    half = D // 2
+    j = np.arange(half, dtype=np.float32)
+    f = (np.float32(1.0 / rope_scale) *
+         np.exp2(np.float32(np.log2(np.float32(1.0 / rope_theta))) * (np.float32(2) * j / D)))
+    pos = (past_kv_len + np.arange(N)).astype(np.float32)
+    ang = (pos[:, None] * f[None, :]).astype(np.float32).astype(np.float64)  # [N, half]
+    c, s = np.cos(ang)[:, None, :], np.sin(ang)[:, None, :]
+    xf = x.astype(np.float64)
+    x0, x1 = xf[..., :half], xf[..., half:]
+    out = np.concatenate([x0 * c - x1 * s, x1 * c + x0 * s], axis=-1)
+    return out.astype(np.float32).astype(F16)
+
+
 BITONIC_MAX_K = 256
 
 

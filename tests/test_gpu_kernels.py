@@ -232,3 +232,30 @@ def test_sparse_decode_shared_row_and_bad_page(cuda):
     assert np.abs(o.float().cpu().numpy() - want).max() < 2e-3
     assert _lib.device_error() == 1  # AOAKV_DEV_ERR_BAD_PAGE, then cleared
     assert _lib.device_error() == 0
+
+
+# -------------------------------------------------------------------- RoPE
+@pytest.mark.parametrize("N,past,D", [(1, 0, 128), (1, 8191, 128), (37, 100, 128), (5, 3000, 64)])
+def test_apply_rope_in_place_matches_oracle(cuda, N, past, D):
+    """utils/__init__.py:25-52 semantics: q and k rotated in place. Positions
+    stay below ~8K here: the angle is an fp32 product (as in the reference),
+    so at 100K+ one ulp of the frequency moves the angle by ~1e-2 rad."""
+    H = 8
+    g = np.random.default_rng(N * 31 + past)
+    q = g.standard_normal((N, H, D)).astype(np.float16)
+    k = g.standard_normal((N, H, D)).astype(np.float16)
+    qd, kd = _dev(q), _dev(k)
+    _lib.call("aoakv_apply_rope_in_place", ptr(qd), ptr(kd), N, past, H, D, 1.0, 1e4, stream())
+    torch.cuda.synchronize()
+    for got, x in ((qd, q), (kd, k)):
+        want = kt.apply_rope(x, past).astype(np.float32)
+        np.testing.assert_allclose(got.float().cpu().numpy(), want, rtol=2e-3, atol=3e-3)
+
+
+def test_apply_rope_zero_position_is_identity(cuda):
+    q = torch.randn(3, 4, 128, device="cuda").half()
+    k = torch.randn(3, 4, 128, device="cuda").half()
+    q0, k0 = q[:1].clone(), k[:1].clone()
+    _lib.call("aoakv_apply_rope_in_place", ptr(q), ptr(k), 3, 0, 4, 128, 1.0, 1e4, stream())
+    torch.cuda.synchronize()
+    assert torch.equal(q[:1], q0) and torch.equal(k[:1], k0)  # position 0: angle 0
