@@ -5,8 +5,8 @@ Public surface, named after the reference's quest.utils
 
     TensorLayout, KvCache, InferenceController, BatchDecodeWithPagedKVCacheWrapper,
     append_kv, decode_estimate, decode_topk, decode_sparse_attn,
-    apply_rope_in_place, prefill_forward and rms_norm_forward (these two are
-    not built here: they raise NotImplementedError)
+    apply_rope_in_place, rms_norm_forward, and prefill_forward (not built
+    here: it raises NotImplementedError)
 
 plus ``topk_filtering`` (the raw top-k op) and
 ``InferenceController.decode_step`` (append + estimate + top-k + decode in one

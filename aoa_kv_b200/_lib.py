@@ -32,6 +32,7 @@ SIGNATURES = {
     "aoakv_get_device_error": [_c_ip, _c_i32],
     "aoakv_debug_wait_flag": [_c_p, _c_i32, _c_i32, _c_p],
     "aoakv_apply_rope_in_place": [_c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_f, _c_f, _c_p],
+    "aoakv_rms_norm": [_c_p, _c_p, _c_p, _c_i32, _c_i32, _c_f, _c_p],
     "aoakv_append_kv_cache_decode": [_c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p,
                                      _c_i32, _c_i32, _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_p],
     "aoakv_append_kv_cache_prefill": [_c_p, _c_p, _c_i32, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p,

@@ -167,5 +167,15 @@ def apply_rope_in_place(q: torch.Tensor, k: torch.Tensor, past_kv_len: int,
               1e4 if rope_theta is None else float(rope_theta), _stream(q))
 
 
-def rms_norm_forward(input, weight, epsilon):
-    _not_built("rms_norm_forward", "utils/__init__.py:54-67")
+def rms_norm_forward(input: torch.Tensor, weight: torch.Tensor, epsilon: float) -> torch.Tensor:
+    """utils/__init__.py:54-67: RMSNorm over the last dimension of an fp16
+    tensor (a multiple of 8), scaled by weight; returns a new tensor."""
+    _check_half_cuda(input, "input")
+    _check_half_cuda(weight, "weight")
+    cols = input.size(-1)
+    if weight.numel() != cols:
+        raise RuntimeError("weight must have input.size(-1) elements")
+    o = torch.empty_like(input)
+    _lib.call("aoakv_rms_norm", _ptr(input), _ptr(weight), _ptr(o), input.numel() // cols, cols,
+              float(epsilon), _stream(input))
+    return o

@@ -115,5 +115,6 @@ def apply_rope_in_place(q, k, past_kv_len, rope_scale, rope_theta):
     _ops.apply_rope_in_place(q, k, past_kv_len, rope_scale, rope_theta)
 
 
-def rms_norm_forward(*args, **kwargs):
-    _ops._not_built("rms_norm_forward", "ops/csrc/rms_norm.cu")
+def rms_norm_forward(input, weight, output, epsilon):
+    """ops/csrc/rms_norm.cu (pybind rms_norm_forward): writes output."""
+    output.copy_(_ops.rms_norm_forward(input, weight, epsilon))

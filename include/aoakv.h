@@ -92,6 +92,13 @@ AOAKV_API int aoakv_apply_rope_in_place(void* q, void* k, int32_t seq_len, int32
                                         int32_t num_heads, int32_t head_dim, float rope_scale,
                                         float rope_theta, void* stream);
 
+/* RMSNorm — replaces rms_norm_forward (bsk_ops.h, ops/csrc/rms_norm.cu;
+ * py utils/__init__.py:54-67). Per row of `columns` fp16 values (a
+ * multiple of 8): out = x * rsqrt(mean(x^2) + epsilon) * weight, computed
+ * in fp32. input, out [rows, columns]; weight [columns]; 16-byte aligned. */
+AOAKV_API int aoakv_rms_norm(const void* input, const void* weight, void* out, int32_t rows,
+                             int32_t columns, float epsilon, void* stream);
+
 /* a1 — replaces append_kv_cache_decode
  *   (kernels/aoa_kv/quest/ops/csrc/bsk_ops.h:71-86, page.cu:6-105,
  *    kernel decode_page.cuh:392-506).

@@ -218,14 +218,16 @@ def test_sparse_decode_shared_row_and_bad_page(cuda):
     qd, o = _dev(q), torch.empty(H, D, dtype=torch.float16, device="cuda")
     ws_n = _lib.size_query("aoakv_decode_workspace_size", H, D, 40)
     ws = torch.zeros(ws_n, dtype=torch.uint8, device="cuda")
-    _lib.call("aoakv_sparse_decode", ptr(qd), ptr(o), ptr(lay.kv), cap, ptr(_dev(rows)), 0, 40, 50,
+    rows_d = _dev(rows)
+    _lib.call("aoakv_sparse_decode", ptr(qd), ptr(o), ptr(lay.kv), cap, ptr(rows_d), 0, 40, 50,
               9, H, D, P, 0, 0.0, ptr(ws), ws_n, stream())
     want = kt.sparse_decode(q, ref, rows, 50, 9)
     assert np.abs(o.float().cpu().numpy() - want).max() < 2e-3
     assert _lib.device_error() == 0
     bad = rows.copy()
     bad[3] = cap + 5
-    _lib.call("aoakv_sparse_decode", ptr(qd), ptr(o), ptr(lay.kv), cap, ptr(_dev(bad)), 0, 40, 50,
+    bad_d = _dev(bad)
+    _lib.call("aoakv_sparse_decode", ptr(qd), ptr(o), ptr(lay.kv), cap, ptr(bad_d), 0, 40, 50,
               9, H, D, P, 0, 0.0, ptr(ws), ws_n, stream())
     keep = np.delete(rows, 3)
     want = kt.sparse_decode(q, ref, keep, 50, 9)
@@ -259,3 +261,19 @@ def test_apply_rope_zero_position_is_identity(cuda):
     _lib.call("aoakv_apply_rope_in_place", ptr(q), ptr(k), 3, 0, 4, 128, 1.0, 1e4, stream())
     torch.cuda.synchronize()
     assert torch.equal(q[:1], q0) and torch.equal(k[:1], k0)  # position 0: angle 0
+
+
+# ----------------------------------------------------------------- RMSNorm
+@pytest.mark.parametrize("rows,cols", [(1, 4096), (7, 128), (3, 8)])
+def test_rms_norm_matches_numpy(cuda, rows, cols):
+    """rms_norm.cu semantics: fp32 mean of squares, out = x * rsqrt(. + eps) * w."""
+    g = np.random.default_rng(rows + cols)
+    x = (g.standard_normal((rows, cols)) * 3).astype(np.float16)
+    w = g.standard_normal(cols).astype(np.float16)
+    o = torch.empty(rows, cols, dtype=torch.float16, device="cuda")
+    xd, wd = _dev(x), _dev(w)  # keep both alive: a freed temporary's block is reused
+    _lib.call("aoakv_rms_norm", ptr(xd), ptr(wd), ptr(o), rows, cols, 1e-5, stream())
+    xf = x.astype(np.float32)
+    r = 1.0 / np.sqrt((xf * xf).mean(axis=1, keepdims=True) + 1e-5)
+    want = (xf * r * w.astype(np.float32)).astype(np.float16).astype(np.float32)
+    np.testing.assert_allclose(o.float().cpu().numpy(), want, rtol=2e-3, atol=2e-3)

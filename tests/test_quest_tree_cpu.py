@@ -44,4 +44,4 @@ def test_tree_resolves_inside_itself_and_exports_reference_names(quest_tree):
 def test_out_of_path_ops_raise_not_implemented(quest_tree):
     utils = importlib.import_module("quest.utils")
     with pytest.raises(NotImplementedError):
-        utils.rms_norm_forward(None, None, 1e-5)
+        utils.prefill_forward(None, None, 0)
