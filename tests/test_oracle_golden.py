@@ -140,3 +140,35 @@ def test_sim_budget_rule():
     assert sim.page_budget_k(32, 16, 100) == 3
     assert sim.page_budget_k(40, 16, 3) == 3
     assert math.isclose(float(sim.LOG_EPS), 1e-8)
+
+
+def test_topk_positions_against_brute_force_sort():
+    """The oracle's selection rule equals a plain sort by (-score, position)
+    with NaN last and -0 == +0, for random rows full of ties."""
+    from hypothesis import given, settings, strategies as st
+
+    @settings(max_examples=60, deadline=None)
+    @given(st.integers(1, 60), st.integers(0, 10_000), st.booleans())
+    def check(n, seed, sink):
+        g = np.random.default_rng(seed)
+        row = np.round(g.standard_normal(n) * 2).astype(np.float32)  # many ties
+        if n > 3:
+            row[g.integers(0, n)] = np.nan
+            row[g.integers(0, n)] = -0.0
+        k = int(g.integers(1, n + 1))
+        got = kt.topk_positions(row[None], k, sink)[0]
+
+        def key(i):
+            v = row[i]
+            if sink and i == 0:
+                return (0, 0.0, i)
+            if np.isnan(v):
+                return (2, 0.0, i)
+            return (1, -float(v) + 0.0, i)
+
+        want = sorted(range(n), key=key)[:k]
+        if k > kt.BITONIC_MAX_K:
+            want = sorted(want)
+        assert list(got) == want
+
+    check()
