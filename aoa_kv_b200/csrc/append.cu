@@ -281,6 +281,7 @@ extern "C" int aoakv_append_kv_cache_decode(
     int32_t num_metadata_pages, int32_t metadata_last_page_len,
     int32_t metadata_capacity_pages, void* v_log_norm, int32_t num_heads,
     int32_t head_dim, int32_t page_size, int32_t layout, void* stream) {
+  AOAKV_NVTX("aoakv_append_kv_cache_decode");
   int rc = check_common(k, v, kv_data, kv_indices, num_kv_pages,
                         kv_last_page_len, kv_capacity_pages, metadata_data,
                         metadata_indices, num_metadata_pages,
@@ -322,6 +323,7 @@ extern "C" int aoakv_append_kv_cache_prefill(
     int32_t metadata_last_page_len, int32_t metadata_capacity_pages,
     void* v_log_norm, int32_t num_heads, int32_t head_dim, int32_t page_size,
     int32_t layout, void* stream) {
+  AOAKV_NVTX("aoakv_append_kv_cache_prefill");
   int rc = check_common(k, v, kv_data, kv_indices, num_kv_pages,
                         kv_last_page_len, kv_capacity_pages, metadata_data,
                         metadata_indices, num_metadata_pages,

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <string>
 
 #include "../../include/aoakv.h"
@@ -27,6 +29,17 @@ int num_sms();
   do {                                                               \
     if (!(cond)) return ::aoakv::set_error(AOAKV_ERR_INVALID_ARG, msg); \
   } while (0)
+
+// NVTX range around a C-ABI call, so a profiler's timeline names every
+// library call (the reference wraps each stage in NVTX ranges,
+// QuestAttention.py:87-176); with no tool attached the calls do nothing.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
+#define AOAKV_NVTX(name) ::aoakv::NvtxRange aoakv_nvtx_range_(name)
 
 #define AOAKV_CUDA_TRY(expr, what)                                   \
   do {                                                               \

@@ -187,6 +187,7 @@ int sparse_decode_impl(const void* q, void* o, float* o_f32, float* lse, const v
                        int32_t last_page_len, int32_t num_heads, int32_t head_dim,
                        int32_t page_size, int32_t layout, float sm_scale, void* workspace,
                        size_t workspace_bytes, void* stream, bool allow_no_last) {
+  AOAKV_NVTX("aoakv_sparse_decode");
   int rc = check_decode_shape(num_heads, head_dim, page_size, kv_capacity_pages, layout);
   if (rc) return rc;
   AOAKV_CHECK_ARG(num_selected >= 0, "decode: num_selected must be >= 0");

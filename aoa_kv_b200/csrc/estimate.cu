@@ -151,6 +151,7 @@ extern "C" int aoakv_estimate_attn_score(
     int32_t kv_capacity_pages, const void* v_log_norm, int32_t num_heads,
     int32_t head_dim, int32_t page_size, int32_t layout, int32_t score_mode,
     void* stream) {
+  AOAKV_NVTX("aoakv_estimate_attn_score");
   AOAKV_CHECK_ARG(q && out && metadata_data && metadata_indices,
                   "estimate: NULL pointer argument");
   if (layout != AOAKV_LAYOUT_NHD)

@@ -56,6 +56,7 @@ using namespace aoakv;
 extern "C" int aoakv_map_pages(const int32_t* global_ids, int64_t count, int32_t page_lo,
                                int32_t n_local, const int32_t* local_kv_indices, int32_t* out,
                                void* stream) {
+  AOAKV_NVTX("aoakv_map_pages");
   AOAKV_CHECK_ARG(global_ids && local_kv_indices && out, "map_pages: NULL pointer argument");
   AOAKV_CHECK_ARG(count >= 0 && n_local >= 0, "map_pages: bad sizes");
   if (count == 0) return AOAKV_OK;
@@ -71,6 +72,7 @@ extern "C" int aoakv_map_pages(const int32_t* global_ids, int64_t count, int32_t
 extern "C" int aoakv_merge_states(const float* o_parts, const float* lse_parts,
                                   int32_t num_parts, int32_t num_heads, int32_t head_dim,
                                   void* o, float* lse_out, void* stream) {
+  AOAKV_NVTX("aoakv_merge_states");
   AOAKV_CHECK_ARG(o_parts && lse_parts && o, "merge_states: NULL pointer argument");
   AOAKV_CHECK_ARG(num_parts >= 1 && num_heads >= 1 && head_dim >= 1 && head_dim <= 1024,
                   "merge_states: bad sizes");

@@ -56,6 +56,7 @@ using namespace aoakv;
 
 extern "C" int aoakv_rms_norm(const void* input, const void* weight, void* out, int32_t rows,
                               int32_t columns, float epsilon, void* stream) {
+  AOAKV_NVTX("aoakv_rms_norm");
   AOAKV_CHECK_ARG(input && weight && out, "rms_norm: NULL pointer argument");
   AOAKV_CHECK_ARG(rows >= 0 && columns >= 8 && columns % 8 == 0,
                   "rms_norm: columns must be a positive multiple of 8");

@@ -48,6 +48,7 @@ using namespace aoakv;
 extern "C" int aoakv_apply_rope_in_place(void* q, void* k, int32_t seq_len, int32_t past_kv_len,
                                          int32_t num_heads, int32_t head_dim, float rope_scale,
                                          float rope_theta, void* stream) {
+  AOAKV_NVTX("aoakv_apply_rope_in_place");
   AOAKV_CHECK_ARG(q && k, "rope: NULL pointer argument");
   AOAKV_CHECK_ARG(seq_len >= 0 && past_kv_len >= 0 && num_heads >= 1, "rope: bad sizes");
   AOAKV_CHECK_ARG(head_dim >= 2 && head_dim % 2 == 0 && head_dim <= 1024,

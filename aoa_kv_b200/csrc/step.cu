@@ -137,6 +137,7 @@ int decode_step_impl(
     int32_t head_dim, int32_t page_size, int32_t page_budget, int32_t score_mode,
     int32_t sink_first_page, int32_t* selected_out, void* workspace,
     size_t workspace_bytes, void* stream, int max_ctas) {
+  AOAKV_NVTX("aoakv_decode_step");
   AOAKV_CHECK_ARG(q && k_new && v_new && o && kv_data && kv_indices && metadata_data &&
                       metadata_indices && v_log_norm,
                   "step: NULL pointer argument");

@@ -79,6 +79,7 @@ extern "C" int aoakv_topk_filtering(
     int32_t num_pages, int32_t k, void* out_values, int64_t out_values_row_stride,
     int32_t* out_indices, int64_t out_indices_row_stride, int32_t sink_first_page,
     void* stream) {
+  AOAKV_NVTX("aoakv_topk_filtering");
   AOAKV_CHECK_ARG(scores != nullptr, "topk: scores is NULL");
   AOAKV_CHECK_ARG(out_values || out_indices, "topk: no output requested");
   AOAKV_CHECK_ARG(scores_dtype == AOAKV_DTYPE_F16 || scores_dtype == AOAKV_DTYPE_F32,

@@ -93,6 +93,17 @@ def parse():
     return a
 
 
+def lib_md5() -> str:
+    """md5 of the loaded libaoakv.so (the reference's latency CSV records the
+    kernel build per row the same way, bench_latency.py:42-46)."""
+    import hashlib
+    from aoa_kv_b200 import _lib
+    try:
+        return hashlib.md5(Path(_lib.LIB_PATH).read_bytes()).hexdigest()
+    except OSError:
+        return "unknown"
+
+
 def workload_config(a, n_gpus):
     n_pages = (a.ctx + P - 1) // P
     return {
@@ -481,6 +492,7 @@ def run_ours(a):
                                   "avg_launch_us": round(est_us, 3)},
             "e2e": e2e, "gpu_launches": kernels_per_layer * a.layers * a.steps,
             "step_kernels_per_layer": kernels_per_layer, "clocks": clocks,
+            "library_md5": lib_md5(),
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
