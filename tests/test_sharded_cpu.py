@@ -156,6 +156,7 @@ CASES = [
     dict(H=4, D=16, P=4, S=300, budget=8, mode="quest", sink=False, ties=True, seed=4, world=2),
     dict(H=2, D=16, P=4, S=60, budget=40, mode="aoakv", sink=False, ties=False, seed=5, world=2),
     dict(H=2, D=16, P=4, S=61, budget=1, mode="quest", sink=False, ties=False, seed=6, world=2),
+    dict(H=3, D=16, P=2, S=203, budget=9, mode="aoakv", sink=True, ties=False, seed=7, world=4),
 ]
 
 
