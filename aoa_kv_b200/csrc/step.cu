@@ -16,6 +16,7 @@
 #include "estimate.cuh"
 #include "fused.h"
 #include "plan.h"
+#include "step_cluster.h"
 #include "topk.cuh"
 
 namespace aoakv {
@@ -66,20 +67,26 @@ StepWs step_ws_layout(int H, int D, int max_pages, int max_budget) {
 // measured slower at the headline shape: its scorers get half the SMs'
 // loads in flight) and =chain the chain (read on every call, for A/B
 // comparisons).
-enum class StepImpl { kPipe, kFused, kChain };
+enum class StepImpl { kCluster, kPipe, kFused, kChain };
 
 struct StepChoice {
   StepImpl impl;
   int grid, chunk, n_chunks;
   size_t smem;
+  ClusterPlan cp;
 };
 
 StepChoice choose_step(int H, int D, int P, int N, int k, int max_grid = 0) {
   const char* e = std::getenv("AOAKV_STEP_IMPL");
   const bool want_chain = e && std::strcmp(e, "chain") == 0;
   const bool want_pipe = e && std::strcmp(e, "pipe") == 0;
-  StepChoice c = {StepImpl::kChain, 0, 0, 0, 0};
+  const bool want_fused = e && std::strcmp(e, "fused") == 0;
+  StepChoice c = {StepImpl::kChain, 0, 0, 0, 0, {}};
   if (want_chain) return c;
+  if (!want_pipe && !want_fused && max_grid == 0 && cluster_step_plan(H, D, P, N, &c.cp)) {
+    c.impl = StepImpl::kCluster;
+    return c;
+  }
   if (want_pipe && pipe_supported(H, D, P, N - 1, k - 1, &c.grid, &c.smem, &c.chunk,
                                   &c.n_chunks)) {
     c.impl = StepImpl::kPipe;
@@ -120,8 +127,8 @@ extern "C" int aoakv_step_launches(int32_t num_heads, int32_t head_dim, int32_t 
   const int k = k_pages < N ? k_pages : N;
   const bool sparse = N > k && k > 1;
   int n = sparse ? 4 : 2;
-  if (sparse && choose_step(num_heads, head_dim, page_size, N, k).impl != StepImpl::kChain)
-    n = 1;
+  const StepImpl im = choose_step(num_heads, head_dim, page_size, N, k).impl;
+  if (im == StepImpl::kCluster || (sparse && im != StepImpl::kChain)) n = 1;
   if (want_selected && n > 1) ++n;
   *kernels_out = n;
   return AOAKV_OK;
@@ -170,8 +177,40 @@ int decode_step_impl(
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
 
+  const StepChoice sc = choose_step(H, D, P, N, k, max_ctas);
+  if (sc.impl == StepImpl::kCluster) {
+    ClusterStepArgs a = {};
+    a.q = static_cast<const __half*>(q);
+    a.k_new = static_cast<const __half*>(k_new);
+    a.v_new = static_cast<const __half*>(v_new);
+    a.o = static_cast<__half*>(o);
+    a.kv = static_cast<__half*>(kv_data);
+    a.kv_indices = kv_indices;
+    a.n_pages = N;
+    a.last_len = kv_last_page_len;
+    a.kv_cap = kv_capacity_pages;
+    a.meta = static_cast<__half*>(metadata_data);
+    a.meta_indices = metadata_indices;
+    a.meta_cap = metadata_capacity_pages;
+    a.vlog = static_cast<__half*>(v_log_norm);
+    a.H = H;
+    a.P = P;
+    a.k_slots = k;
+    a.sink = sink_first_page != 0;
+    a.mode = score_mode;
+    a.two_rsqrt_d = 2.f / std::sqrt(static_cast<float>(D));
+    a.scale_log2 = (1.f / std::sqrt(static_cast<float>(D))) * 1.4426950408889634f;
+    a.selected_out = selected_out;
+    a.sel_cols = k_pages;
+    a.err = dev_error_ptr();
+    CUtensorMap kmap, mmap;
+    rc = make_kv_tmap(&kmap, kv_data, H, D, P, kv_capacity_pages);
+    if (rc) return rc;
+    rc = make_kv_tmap(&mmap, metadata_data, H, D, P, metadata_capacity_pages);
+    if (rc) return rc;
+    return launch_cluster_step(a, kmap, mmap, D, sc.cp, s);
+  }
   if (sparse) {
-    const StepChoice sc = choose_step(H, D, P, N, k, max_ctas);
     const int grid = sc.grid, chunk = sc.chunk, n_chunks = sc.n_chunks;
     const size_t smem = sc.smem;
     if (sc.impl != StepImpl::kChain) {

@@ -48,21 +48,23 @@ __device__ __forceinline__ void append_prefetch(const FusedArgs& f, int h, int s
   cp_async_commit();
 }
 
-// Appends head h; st (may be NULL) holds its prefetched inputs in `slot`.
-template <int D>
-__device__ __forceinline__ void append_head(const FusedArgs& f, int h,
+// Appends head h with one warp (any warp of the CTA); st (may be NULL)
+// holds its prefetched inputs in `slot`. A is any argument struct with the
+// fields of FusedArgs that name the token, the page tables and the buffers.
+template <int D, typename A>
+__device__ __forceinline__ void append_head(const A& f, int h,
                                             const AppendStage* st = nullptr, int slot = 0) {
   const int H = f.H, P = f.P;
   constexpr int L = D / 8;
-  const int lane = threadIdx.x;
+  const int lane = threadIdx.x & 31;
   const int page_iter = f.n_pages - 1;
   const int entry = f.last_len - 1;
   if (st) {
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncwarp();
   }
-  const int pid = st ? st->ids[0] : __ldg(f.kv_indices + page_iter);
-  const int mpid = st ? st->ids[1] : __ldg(f.meta_indices + page_iter / P);
+  const int pid = st ? st->ids[0] : __ldcg(f.kv_indices + page_iter);
+  const int mpid = st ? st->ids[1] : __ldcg(f.meta_indices + page_iter / P);
   const int mentry = page_iter % P;
   const bool ok = pid >= 0 && pid < f.kv_cap && mpid >= 0 && mpid < f.meta_cap;
   if (!ok && lane == 0) raise_dev_error(f.err, AOAKV_DEV_ERR_BAD_PAGE);

@@ -1,0 +1,52 @@
+// Arguments and host helpers of the cluster step kernel (step_cluster.cu):
+// the whole per-layer decode step, one thread-block cluster per head.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace aoakv {
+
+struct ClusterStepArgs {
+  const __half* q;              // [H, D]
+  const __half* k_new;          // [H, D] the new token
+  const __half* v_new;
+  __half* o;                    // [H, D]
+  __half* kv;                   // [kv_cap, 2, P, H, D]
+  const int32_t* kv_indices;    // [n_pages] physical ids, last page last
+  int n_pages, last_len, kv_cap;
+  __half* meta;                 // [meta_cap, 2, P, H, D]
+  const int32_t* meta_indices;  // [ceil(n_pages / P)]
+  int meta_cap;
+  __half* vlog;                 // [kv_cap, H]
+  int H, P;
+  int k_slots;                  // attended pages, last page included: min(budget, N)
+  int sink;                     // page 0 always attended (simulation's `fixed`)
+  int mode;                     // AOAKV_SCORE_*
+  float two_rsqrt_d;            // 2 / sqrt(D)
+  float scale_log2;             // sm_scale * log2(e)
+  int32_t* selected_out;        // optional [H, sel_cols]
+  int sel_cols;
+  int* err;
+};
+
+// Launch shape of the cluster step for one problem size.
+struct ClusterPlan {
+  int cluster;      // CTAs per head (1, 2, 4 or 8)
+  int max_local;    // scored pages per CTA the shared memory is sized for
+  size_t smem;      // dynamic shared memory per CTA
+  int waves;        // clusters resident at once vs heads: 1 = one wave
+};
+
+// Returns 1 and the plan when the cluster step can run (H heads of head_dim
+// D, page size P, up to max_pages pages); 0 otherwise (the caller uses the
+// multi-kernel chain).
+int cluster_step_plan(int H, int D, int P, int max_pages, ClusterPlan* plan);
+int launch_cluster_step(const ClusterStepArgs& a, const CUtensorMap& kv_map,
+                        const CUtensorMap& meta_map, int D, const ClusterPlan& plan,
+                        cudaStream_t s);
+
+}  // namespace aoakv

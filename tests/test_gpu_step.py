@@ -109,11 +109,11 @@ def test_step_sink_matches_reference_simulation(cuda, method, S, B, dist):
         assert np.abs(got_o - out_s).max() < 2e-3
 
 
-@pytest.fixture(params=["pipe", "fused", "chain"])
+@pytest.fixture(params=["cluster", "pipe", "fused", "chain"])
 def step_impl(request, monkeypatch):
-    """Runs a test with the phase-by-phase fused kernel (the default), the
-    pipelined two-role kernel and the four-launch chain (AOAKV_STEP_IMPL is
-    read by the library on every call)."""
+    """Runs a test with the cluster kernel (the default), the cooperative
+    fused kernel, the pipelined two-role kernel and the four-launch chain
+    (AOAKV_STEP_IMPL is read by the library on every call)."""
     monkeypatch.setenv("AOAKV_STEP_IMPL", request.param)
     return request.param
 
@@ -251,4 +251,71 @@ def test_step_grid_capped_matches_oracle(cuda, max_ctas):
     assert not selection_mismatch(g_log, w_log, scores)
     if np.array_equal(g_log, w_log):
         assert np.abs(o.float().cpu().numpy() - want_o).max() < 2e-3
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("start_pages,budget,mode,sink", [
+    (41, 16, "aoakv", False), (300, 64, "aoakv", True), (590, 32, "quest", False)])
+def test_step_back_to_back_same_layer(cuda, start_pages, budget, mode, sink):
+    """Twenty steps of ONE layer issued back to back on one stream with
+    nothing between them (no copy, no synchronisation): every step reads the
+    page metadata, v_log_norm and KV rows that the previous step's append
+    wrote, across two page fills and two new pages, while under programmatic
+    dependent launch it may start before the previous step ends. Every
+    output and selection is checked against the oracle run step by step."""
+    H, D, P, T = 32, 128, 16, 20
+    S0 = (start_pages - 1) * P + 14  # tokens before the first step
+    q_all = np.stack([gen_qkv(7000 + i, H, 1, D, "normal")[0] for i in range(T)])
+    _, K, V = gen_qkv(start_pages + budget, H, S0 + T, D, "outlier")
+    cap = (S0 + T + P - 1) // P + 1
+    lay = GpuLayer(cap, H, D, P, seed=start_pages)
+    lay.fill(K[:S0], V[:S0])
+    torch.cuda.synchronize()
+    ref = lay.snapshot()
+    cols = max(3, budget) if sink else budget
+    ws_n = _lib.size_query("aoakv_step_workspace_size", H, D, cap, cols)
+    ws = torch.zeros(ws_n, dtype=torch.uint8, device="cuda")
+    qd = torch.from_numpy(q_all).cuda()
+    kd = torch.from_numpy(np.ascontiguousarray(K[S0:])).cuda()
+    vd = torch.from_numpy(np.ascontiguousarray(V[S0:])).cuda()
+    o = torch.empty(T, H, D, dtype=torch.float16, device="cuda")
+    sel = torch.full((T, H, cols), -9, dtype=torch.int32, device="cuda")
+    mode_id = _lib.SCORE_AOAKV if mode == "aoakv" else _lib.SCORE_QUEST
+    torch.cuda.synchronize()
+    for t in range(T):  # issued back to back; the host never waits
+        S = S0 + t + 1
+        n, last = (S + P - 1) // P, (S - 1) % P + 1
+        _lib.call("aoakv_decode_step", ptr(qd[t]), ptr(kd[t]), ptr(vd[t]), ptr(o[t]),
+                  ptr(lay.kv), ptr(lay.kv_idx), n, last, cap, ptr(lay.meta), ptr(lay.meta_idx),
+                  lay.mcap, ptr(lay.vlog), H, D, P, budget, mode_id, int(sink), ptr(sel[t]),
+                  ptr(ws), ws_n, stream())
+    torch.cuda.synchronize()
+    got_o, got_sel = o.float().cpu().numpy(), sel.cpu().numpy()
+    fills = 0
+    for t in range(T):
+        S = S0 + t + 1
+        n, last = (S + P - 1) // P, (S - 1) % P + 1
+        fills += last == P
+        want_o, want_sel = kt.step(q_all[t], K[S0 + t], V[S0 + t], ref, lay.kv_idx_np,
+                                   lay.meta_idx_np, n, last, budget, mode, sink)
+        kp = max(3, budget) if sink else budget
+        k = min(kp, n)
+        g_log = np.array(logical(got_sel[t], lay.kv_idx_np, n))
+        w_log = np.array(logical(want_sel, lay.kv_idx_np, n))
+        scores = kt.estimate(q_all[t], ref, lay.meta_idx_np, lay.kv_idx_np, n, mode)
+        scores = np.concatenate([scores, np.full((H, 1), np.inf, np.float32)], axis=1)
+        if sink:
+            scores[:, 0] = np.inf
+        assert not selection_mismatch(g_log, w_log, scores), t
+        assert np.all(got_sel[t][:, k - 1] == lay.kv_idx_np[n - 1]), t
+        phys = np.array([[int(p) for p in row[: k - 1]] for row in got_sel[t]], dtype=np.int64)
+        o_ref = kt.sparse_decode(q_all[t], ref, phys.reshape(H, k - 1),
+                                 int(lay.kv_idx_np[n - 1]), last)
+        assert np.abs(got_o[t] - o_ref).max() < 2e-3, t
+        if np.array_equal(g_log, w_log):
+            assert np.abs(got_o[t] - want_o).max() < 2e-3, t
+    assert fills == 2
+    after = lay.snapshot()
+    assert np.array_equal(after.meta, ref.meta)
+    assert np.abs(after.vlog.astype(np.float32) - ref.vlog.astype(np.float32)).max() <= 2e-3
     assert _lib.device_error() == 0
