@@ -83,7 +83,7 @@ StepChoice choose_step(int H, int D, int P, int N, int k, int max_grid = 0) {
   const bool want_fused = e && std::strcmp(e, "fused") == 0;
   StepChoice c = {StepImpl::kChain, 0, 0, 0, 0, {}};
   if (want_chain) return c;
-  if (!want_pipe && !want_fused && max_grid == 0 && cluster_step_plan(H, D, P, N, &c.cp)) {
+  if (!want_pipe && !want_fused && max_grid == 0 && cluster_step_plan(H, D, P, N, k, &c.cp)) {
     c.impl = StepImpl::kCluster;
     return c;
   }

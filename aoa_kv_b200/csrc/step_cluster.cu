@@ -66,49 +66,109 @@ constexpr int kCsWarps = kCsThreads / 32;
 constexpr int kCsBins = 2048;             // 0 NaN, 1 -inf, 2..2046 linear, 2047 +inf
 constexpr int kCsLinBins = kCsBins - 3;
 constexpr int kCsBinsPerThread = kCsBins / kCsThreads;
-constexpr int kCsMaxCand = 512;           // exact ranking of the threshold bin
+constexpr int kCsMaxCand = 512;           // fallback: exact ranking of the threshold bin
+constexpr int kCsGather = 2048;           // candidates gathered from the whole cluster
 constexpr int kCsMaxLevels = 6;
 constexpr int kCsMaxPage = 16;
 static_assert(kCsBinsPerThread == 4, "one uint4 of bins per thread");
 
 struct CsLayout {
-  int ring, scores, state, hist, cand, candall, sel, mrg, xo, total;
+  int ring, scores, state, pidl, hist, cand, lst, gkey, gpos, items, mrg, xo, total;
 };
 
 __host__ __device__ inline int cs_up(int x) { return (x + 127) / 128 * 128; }
 __host__ __device__ inline int cs_slot_bytes(int D, int P) { return cs_up(2 * P * D * 2); }
+__host__ __device__ inline int cs_capl(int C) { return kCsGather / C; }
+__host__ __device__ inline int cs_max_items(int C, int max_slots) {
+  const int a = cs_capl(C) + 2, b = (max_slots + C - 1) / C;
+  return a > b ? a : b;
+}
 
-__host__ __device__ inline CsLayout cs_layout(int D, int P, int max_local) {
+__host__ __device__ inline CsLayout cs_layout(int D, int P, int C, int max_local,
+                                              int max_slots) {
   CsLayout L;
+  const int capl = cs_capl(C);
+  const int capx = capl > kCsMaxCand ? capl : kCsMaxCand;
   int off = 0;
-  L.ring = off;
+  L.ring = off;  // one TMA slot per warp: metadata pages, then K/V pages
   off += kCsWarps * cs_slot_bytes(D, P);
   L.scores = off;
   off += cs_up(max_local * 4);
   L.state = off;
   off += cs_up(max_local);
+  L.pidl = off;  // page ids of the scored pages; the fallback's selection list
+  off += cs_up(max_local * 4);
   L.hist = off;
   off += kCsBins * 4;
-  L.cand = off;
-  off += kCsMaxCand * 8;
-  L.candall = off;
-  off += kCsMaxCand * 8;
-  L.sel = off;
-  off += cs_up(max_local * 4);
+  L.cand = off;  // local candidates {key, page, id}; the fallback's threshold bin
+  off += capx * 16;
+  L.lst = off;  // the same sorted by (score desc, page asc): read by peers
+  off += cs_up(capl * 16);
+  L.gkey = off;  // keys and pages of every CTA's sorted list, CTA after CTA
+  off += kCsGather * 4;
+  L.gpos = off;
+  off += kCsGather * 4;
+  L.items = off;  // page ids this CTA attends
+  off += cs_up(cs_max_items(C, max_slots) * 4);
   L.mrg = off;
   off += cs_up(kCsWarps * (D + 2) * 4);
-  L.xo = off;
-  off += cs_up(D * 4);
+  L.xo = off;  // CTA 0: every CTA's partial state (D numerators, max, sum)
+  off += cs_up(C * (D + 2) * 4);
   L.total = off;
   return L;
 }
 
 // What peer CTAs read from this CTA's shared memory besides the arrays.
 struct CsXchg {
-  float fmin, fmax;  // finite score range of this CTA's candidates
-  int n_sel;         // selected pages in the `sel` array
-  float M, L;        // decode partial: running max (log2 units), denominator
+  int m, ovf;        // local candidates published in `lst`; more than fit
+  float fmin, fmax;  // fallback: finite score range of this CTA's candidates
+  int n_sel;         // fallback: selected pages in the `sel` array
 };
+
+// ---------------------------------------------------------- cluster PTX
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+// Arrival that orders nothing: for barriers that only mark "done reading
+// peers' shared memory" (the values read are already consumed).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrives (release, cluster scope) on the mbarrier at the same shared
+// memory offset as `bar` in CTA `rank` of the cluster.
+__device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(bar)), "r"(rank));
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// L2 prefetch of one TMA box (no completion, no effect on correctness).
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c0, int c1,
+                                                   int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+
+// (key, page) of `a` ranks above that of `b`: higher score, then lower page.
+__device__ __forceinline__ bool cs_beats(uint32_t ka, uint32_t pa, uint32_t kb, uint32_t pb) {
+  return ka > kb || (ka == kb && pa < pb);
+}
 
 // Exclusive prefix sum over the CTA in thread order; *total = the sum.
 __device__ __forceinline__ int cs_block_scan(int v, int* total) {
@@ -182,6 +242,18 @@ __device__ __forceinline__ int cs_bin(float x, float gmin, float range) {
   return 2 + (b < 0 ? 0 : b);
 }
 
+// The same order-preserving binning with a precomputed scale (kCsLinBins /
+// range, 0 when the range is zero, infinite or overflows): monotone but not
+// identical to cs_bin, so it is used only where a superset suffices.
+__device__ __forceinline__ int cs_bin_mul(float x, float gmin, float scale) {
+  if (isnan(x)) return 0;
+  if (x == -INFINITY) return 1;
+  if (x == INFINITY) return kCsBins - 1;
+  const float t = (x - gmin) * scale;
+  const int b = t < static_cast<float>(kCsLinBins) ? __float2int_rz(t) : kCsLinBins - 1;
+  return 2 + (b < 0 ? 0 : b);
+}
+
 // Sums part[j] (j < 16) over the 32 lanes of the warp: afterwards every
 // lane holds the total of page j = (lane >> 1) & 15 (16 shuffles).
 __device__ __forceinline__ float cs_reduce16(const float part[16]) {
@@ -214,35 +286,150 @@ __device__ __forceinline__ float cs_reduce16(const float part[16]) {
   return r1 + __shfl_xor_sync(0xffffffffu, r1, 1);
 }
 
+// One warp attends the page tile in shared memory (K rows then V rows, P <=
+// 16 rows of D fp16 each, ntok valid): online softmax in the log2 domain,
+// q pre-scaled by sm_scale*log2(e); lane l owns channels [l*CPL, (l+1)*CPL).
+template <int D>
+__device__ __forceinline__ void cs_attend_page(const __half* Kt, const __half* Vt, int ntok,
+                                               const float* qs, float& m, float& l, float* o) {
+  constexpr int CPL = D / 32;
+  const int lane = threadIdx.x & 31;
+  float part[16];
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    part[t] = 0.f;
+    if (t < ntok) {
+      float kf[CPL];
+      load_row<CPL>(Kt + t * D + lane * CPL, kf);
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) part[t] = fmaf(qs[i], kf[i], part[t]);
+    }
+  }
+  const float sv = cs_reduce16(part);  // lanes 2t, 2t+1: token t
+  const int jt = (lane >> 1) & 15;
+  const float x = jt < ntok ? sv : -INFINITY;
+  float gmax = x;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, off));
+  const float m_new = fmaxf(m, gmax);  // finite: token 0 is valid
+  const float alpha = fast_exp2(m - m_new);
+  const float pw = jt < ntok ? fast_exp2(sv - m_new) : 0.f;
+  float ps = (lane & 1) ? 0.f : pw;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+  l = l * alpha + ps;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) o[i] *= alpha;
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    const float pt = __shfl_sync(0xffffffffu, pw, 2 * t);
+    if (t < ntok) {
+      float vf[CPL];
+      load_row<CPL>(Vt + t * D + lane * CPL, vf);
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) o[i] = fmaf(pt, vf[i], o[i]);
+    }
+  }
+  m = m_new;
+}
+
+// One warp: the bin b of hist (kCsBins counts) with above(b) < need <=
+// above(b) + hist[b]; bc = {b, above(b), hist[b]}. Two levels of suffix sums
+// over the lanes (64 bins per lane, then 2), no block barrier.
+__device__ __forceinline__ void cs_threshold_warp(const uint32_t* hist, int need, int* bc) {
+  const int lane = threadIdx.x & 31;
+  const uint4* h4 = reinterpret_cast<const uint4*>(hist);
+  int sl = 0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const uint4 v = h4[lane * 16 + ((j + lane) & 15)];  // rotated: no bank conflicts
+    sl += static_cast<int>(v.x + v.y + v.z + v.w);
+  }
+  int inc = sl;  // sum over this lane and the higher ones
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_down_sync(0xffffffffu, inc, o);
+    if (lane + o < 32) inc += y;
+  }
+  const int above1 = inc - sl;
+  const unsigned f1 = __ballot_sync(0xffffffffu, above1 < need && need <= above1 + sl);
+  const int L1 = __ffs(f1) - 1;
+  const int a1 = __shfl_sync(0xffffffffu, above1, L1);
+  const uint2 v2 = reinterpret_cast<const uint2*>(hist)[L1 * 32 + lane];
+  const int s2 = static_cast<int>(v2.x + v2.y);
+  int inc2 = s2;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_down_sync(0xffffffffu, inc2, o);
+    if (lane + o < 32) inc2 += y;
+  }
+  const int above2 = a1 + inc2 - s2;
+  const int hi = static_cast<int>(v2.y), lo = static_cast<int>(v2.x);
+  int b = -1, ab = 0, cnt = 0;
+  if (above2 < need && need <= above2 + hi) {
+    b = L1 * 64 + 2 * lane + 1;
+    ab = above2;
+    cnt = hi;
+  } else if (above2 + hi < need && need <= above2 + hi + lo) {
+    b = L1 * 64 + 2 * lane;
+    ab = above2 + hi;
+    cnt = lo;
+  }
+  const unsigned f2 = __ballot_sync(0xffffffffu, b >= 0);
+  if (lane == __ffs(f2) - 1) {
+    bc[0] = b;
+    bc[1] = ab;
+    bc[2] = cnt;
+  }
+}
+
+template <int CPL>
+struct LaneVec;  // the lane's CPL fp16 channels of one row
+template <>
+struct LaneVec<4> {
+  using T = uint2;
+};
+template <>
+struct LaneVec<2> {
+  using T = uint32_t;
+};
+
 template <int D, int C>
 __global__ void __launch_bounds__(kCsThreads, 1)
     cluster_step_kernel(const __grid_constant__ CUtensorMap kv_map,
                         const __grid_constant__ CUtensorMap meta_map, ClusterStepArgs a,
-                        int max_local) {
-  constexpr int CPL = D / 32;  // channels per lane
+                        CsShape shp) {
+  constexpr int CPL = D / 32;           // channels per lane
+  constexpr int CAPL = kCsGather / C;   // local candidates one CTA may publish
+  using Vec = typename LaneVec<CPL>::T;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
   __shared__ uint64_t bars[kCsWarps];
+  __shared__ uint64_t merge_bar;  // CTA 0: the other CTAs' partial states are in
   __shared__ CsXchg xs;
   __shared__ int bc[3];  // threshold bin, count above it, count in it
   __shared__ int peer_cnt[C], peer_off[C + 1];
   __shared__ float gsh[2];
-  __shared__ int cnt_s;
+  __shared__ uint32_t kmin_s, kmax_s;     // key range of this CTA's ranked scores
+  __shared__ int cnt_s, fast_s, nw_s;
 
   cg::cluster_group cluster = cg::this_cluster();
   const int c = static_cast<int>(cluster.block_rank());
   const int h = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int P = a.P, H = a.H;
-  const CsLayout lay = cs_layout(D, P, max_local);
+  const CsLayout lay = cs_layout(D, P, C, shp.max_local, shp.max_slots);
   uint8_t* slot = smem + lay.ring + warp * cs_slot_bytes(D, P);
   float* sc = reinterpret_cast<float*>(smem + lay.scores);
   uint8_t* st = smem + lay.state;
+  int* pidl = reinterpret_cast<int*>(smem + lay.pidl);
   uint32_t* hist = reinterpret_cast<uint32_t*>(smem + lay.hist);
-  uint2* cand = reinterpret_cast<uint2*>(smem + lay.cand);
-  uint2* candall = reinterpret_cast<uint2*>(smem + lay.candall);
-  int* sel = reinterpret_cast<int*>(smem + lay.sel);
+  uint4* cand = reinterpret_cast<uint4*>(smem + lay.cand);
+  uint4* lst = reinterpret_cast<uint4*>(smem + lay.lst);
+  uint32_t* gkey = reinterpret_cast<uint32_t*>(smem + lay.gkey);
+  uint32_t* gpos = reinterpret_cast<uint32_t*>(smem + lay.gpos);
+  int* items = reinterpret_cast<int*>(smem + lay.items);
   float* mrg = reinterpret_cast<float*>(smem + lay.mrg);
   float* xo = reinterpret_cast<float*>(smem + lay.xo);
   uint64_t* bar = &bars[warp];
@@ -250,11 +437,18 @@ __global__ void __launch_bounds__(kCsThreads, 1)
 
   if (tid == 0) {
     for (int i = 0; i < kCsWarps; ++i) mbar_init(&bars[i], 1);
+    mbar_init(&merge_bar, C > 1 ? C - 1 : 1);
     fence_mbar_init();
     tma_prefetch_desc(&kv_map);
     tma_prefetch_desc(&meta_map);
+    kmin_s = 0xffffffffu;
+    kmax_s = 0u;
+    cnt_s = 0;
   }
+  for (int b = tid; b < kCsBins; b += kCsThreads) hist[b] = 0u;
   __syncthreads();
+  cluster_arrive_relaxed();  // merge_bar initialised (fence.mbarrier_init above; waited for
+                             // before any remote access)
   // Everything in global memory may be written by the previous kernel on
   // the stream (under programmatic dependent launch it can still be
   // running), so every global read comes after this wait.
@@ -270,7 +464,18 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   const int pos_lo = st_lo * P;
   const int nloc = sparse ? max(0, min(n, st_hi * P) - pos_lo) : 0;
   const int r_lo = a.sink ? 1 : 0;
-  const bool appender = c == C - 1 && warp == kCsWarps - 1;
+  // attended slots: the selected pages, then the last page; CTA c decodes
+  // slots [s_lo, s_hi), so the last page falls to CTA C-1
+  const int T = sparse ? k : (N <= k ? N : 1);
+  const int s_lo = (c * T) / C, s_hi = ((c + 1) * T) / C;
+  const int w_last = c == C - 1 ? (T - 1 - s_lo) % kCsWarps : -1;
+  // ids of the last page (attended by CTA C-1, which also appends to it)
+  const int last_pid = __ldcg(a.kv_indices + N - 1);
+  const int app_mpid = c == C - 1 ? __ldcg(a.meta_indices + (N - 1) / P) : 0;
+  if (warp == w_last && lane == 0 && last_pid >= 0 && last_pid < a.kv_cap) {  // warm L2
+    tma_prefetch_l2_3d(&kv_map, 0, h, last_pid * 2 * P);
+    tma_prefetch_l2_3d(&kv_map, 0, h, last_pid * 2 * P + P);
+  }
 
   float qv[CPL];
   load_row<CPL>(a.q + static_cast<size_t>(h) * D + lane * CPL, qv);
@@ -281,17 +486,29 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   uint32_t par = 0;  // phase of this warp's ring-slot barrier
 
   // ------------------------------------------------------------ 1 scoring
-  float fmin_l = INFINITY, fmax_l = -INFINITY;
   if (sparse) {
     const int jp = (lane >> 1) & 15;           // page of the stage this lane scores
     const bool writer = (lane & 1) == 0 && jp < P;
-    auto issue = [&](int t) -> bool {
+    // the metadata page of stage t and the lane's page id / v_log_norm
+    auto meta_of = [&](int t) -> int { return lane == 0 ? __ldcg(a.meta_indices + t) : 0; };
+    auto page_of = [&](int t, float* vlo) -> int {
+      const int pos = t * P + jp;
+      *vlo = 0.f;
+      if (!writer || pos >= n) return -1;
+      const int pid = __ldcg(a.kv_indices + pos);
+      if (pid < 0 || pid >= a.kv_cap) {
+        raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
+        *vlo = NAN;
+        return -1;
+      }
+      if (aoa) *vlo = __half2float(__ldcg(a.vlog + static_cast<size_t>(pid) * H + h));
+      return pid;
+    };
+    auto issue = [&](int mp) -> bool {
       int ok = 0;
       if (lane == 0) {
-        const int mp = __ldcg(a.meta_indices + t);
         if (mp >= 0 && mp < a.meta_cap) {
           ok = 1;
-          fence_proxy_async_smem();
           mbar_arrive_expect_tx(bar, 2u * tile_bytes);
           tma_load_3d(slot, &meta_map, 0, h, mp * 2 * P, bar);
           tma_load_3d(slot + tile_bytes, &meta_map, 0, h, mp * 2 * P + P, bar);
@@ -301,25 +518,17 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       }
       return __shfl_sync(0xffffffffu, ok, 0) != 0;
     };
-    // v_log_norm of the lane's page of stage t (AOA-KV), NaN for a bad id
-    auto vlog_of = [&](int t) -> float {
-      const int pos = t * P + jp;
-      if (!aoa || !writer || pos >= n) return 0.f;
-      const int pid = __ldcg(a.kv_indices + pos);
-      if (pid < 0 || pid >= a.kv_cap) {
-        raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
-        return NAN;
-      }
-      return __half2float(__ldcg(a.vlog + static_cast<size_t>(pid) * H + h));
-    };
+    uint32_t kmin_l = 0xffffffffu, kmax_l = 0u;
     int t = st_lo + warp;
     bool ok = false;
     float vl = 0.f;
+    int pg = -1;
+    int mp_next = 0;
     if (t < st_hi) {
-      ok = issue(t);
-      vl = vlog_of(t);
+      ok = issue(meta_of(t));
+      pg = page_of(t, &vl);
+      if (t + kCsWarps < st_hi) mp_next = meta_of(t + kCsWarps);  // one stage ahead
     }
-    if (appender) append_head<D>(a, h);  // while the first boxes are in flight
     for (; t < st_hi; t += kCsWarps) {
       bool got = ok;
       if (ok) {
@@ -353,192 +562,170 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       }
       const float s = cs_reduce16(part);
       const float vl_t = vl;
+      const int pg_t = pg;
       const int pos = t * P + jp;
-      __syncwarp();  // every lane is done with the slot before it is refilled
+      // Every lane has consumed the slot (its values are in `part`) before
+      // lane 0 refills it: the TMA write cannot overtake these reads.
+      __syncwarp();
       const int tn = t + kCsWarps;
       if (tn < st_hi) {
-        ok = issue(tn);
-        vl = vlog_of(tn);
+        ok = issue(mp_next);
+        pg = page_of(tn, &vl);
+        if (tn + kCsWarps < st_hi) mp_next = meta_of(tn + kCsWarps);
       }
       if (writer && pos < n) {
         const float score = !got ? NAN : (aoa ? a.two_rsqrt_d * s + 2.f * vl_t : s);
         const int i = pos - pos_lo;
         sc[i] = score;
+        pidl[i] = pg_t;
         const uint8_t s0 = pos >= r_lo ? 1 : 2;  // the sink page is forced
         st[i] = s0;
         if (s0 == 1 && isfinite(score)) {
-          fmin_l = fminf(fmin_l, score);
-          fmax_l = fmaxf(fmax_l, score);
+          const uint32_t kk = float_to_key(score);
+          kmin_l = min(kmin_l, kk);
+          kmax_l = max(kmax_l, kk);
         }
       }
     }
-  } else if (appender) {
-    append_head<D>(a, h);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      kmin_l = min(kmin_l, __shfl_xor_sync(0xffffffffu, kmin_l, o));
+      kmax_l = max(kmax_l, __shfl_xor_sync(0xffffffffu, kmax_l, o));
+    }
+    if (lane == 0 && kmin_l <= kmax_l) {
+      atomicMin(&kmin_s, kmin_l);
+      atomicMax(&kmax_s, kmax_l);
+    }
   }
   __syncthreads();
+  cluster_wait_acquire();  // every CTA's merge_bar is initialised
 
   // ---------------------------------------------------------- 2 selection
+  // Fast path: each CTA sorts its local candidates — every ranked page whose
+  // score reaches the bin of the CTA's K-th largest, a superset of its share
+  // of the global top-K — by (score desc, page asc); its winners are a
+  // prefix of that list. Before the one cluster barrier it starts the TMA
+  // loads of its first candidates' K/V pages into the ring (and warms L2
+  // with a few more); after it, each CTA copies the other lists and ranks
+  // its own candidates by binary search in them: a rank below K is a
+  // winner, attended by this CTA. A CTA with more than CAPL candidates
+  // (many equal scores) sends the whole cluster to the level-by-level
+  // fallback, whose winners are spread evenly over the cluster.
+  int32_t* sel_row =
+      a.selected_out ? a.selected_out + static_cast<size_t>(h) * a.sel_cols : nullptr;
+  const bool sink_owner = sparse && a.sink && st_lo == 0 && st_hi > 0;
+  // pages attended whatever the selection: the last page (CTA C-1, first),
+  // the sink page (its owner)
+  const int n_special = (c == C - 1 ? 1 : 0) + (sink_owner ? 1 : 0);
+  int n_spec = 0;    // items whose pages were loaded before the selection ended
+  int n_items = 0;   // pages this CTA attends
+  int last_item = -1;
+  bool spec_issued = false;  // this warp's slot holds a speculative load
+  bool fast = true;
+  auto load_page = [&](int pid) {  // lane 0: the page's K and V tiles into the warp's slot
+    fence_proxy_async_smem();  // the slot may hold rows written by this warp (the append)
+    mbar_arrive_expect_tx(bar, 2u * tile_bytes);
+    tma_load_3d(slot, &kv_map, 0, h, pid * 2 * P, bar);
+    tma_load_3d(slot + tile_bytes, &kv_map, 0, h, pid * 2 * P + P, bar);
+  };
   if (sparse) {
-    int need = (k - 1) - r_lo;  // pages to choose among the ranked ones
-    bool done = need <= 0;
-    for (int level = 0; !done; ++level) {
-      // A: finite range of the candidates (state 1), cluster-wide
-      float lo = fmin_l, hi = fmax_l;
-      if (level > 0) {
-        lo = INFINITY;
-        hi = -INFINITY;
-        for (int i = tid; i < nloc; i += kCsThreads) {
-          if (st[i] != 1) continue;
-          const float x = sc[i];
-          if (isfinite(x)) {
-            lo = fminf(lo, x);
-            hi = fmaxf(hi, x);
-          }
-        }
+    const int K = (k - 1) - r_lo;  // pages to choose among the ranked ones (>= 1)
+    const int rk0 = min(nloc, max(0, r_lo - pos_lo));  // first ranked local index
+    const int n_rank = nloc - rk0;
+    int lb = -1;  // local threshold bin; -1: every ranked page is a candidate
+    float lmin = 0.f, lscale = 0.f;
+    if (n_rank > K) {
+      if (kmin_s <= kmax_s) {
+        lmin = key_to_float(kmin_s);
+        const float lmax = key_to_float(kmax_s);
+        const float r = lmax - lmin;
+        const float sc0 = static_cast<float>(kCsLinBins) / r;
+        lscale = (r > 0.f && r < INFINITY && sc0 < INFINITY) ? sc0 : 0.f;
       }
-      cs_block_minmax(lo, hi, &xs.fmin, &xs.fmax);
-      cluster.sync();  // ranges published; peers are done with this CTA's histogram
-      if (warp == 0) {
-        float gl = INFINITY, gh = -INFINITY;
-        if (lane < C) {
-          const CsXchg* px = cluster.map_shared_rank(&xs, lane);
-          gl = px->fmin;
-          gh = px->fmax;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          gl = fminf(gl, __shfl_xor_sync(0xffffffffu, gl, o));
-          gh = fmaxf(gh, __shfl_xor_sync(0xffffffffu, gh, o));
-        }
-        if (lane == 0) {
-          gsh[0] = gl;
-          gsh[1] = gh;
-        }
-      }
-      for (int b = tid; b < kCsBins; b += kCsThreads) hist[b] = 0u;
+      for (int i = rk0 + tid; i < nloc; i += kCsThreads)
+        atomicAdd(&hist[cs_bin_mul(sc[i], lmin, lscale)], 1u);
       __syncthreads();
-      const float gmin = gsh[0], gmax = gsh[1];
-      const float range = (gmax > gmin && gmax - gmin < INFINITY) ? gmax - gmin : 0.f;
-      // B: histogram of the candidates, cluster-wide
-      for (int i = tid; i < nloc; i += kCsThreads)
-        if (st[i] == 1) atomicAdd(&hist[cs_bin(sc[i], gmin, range)], 1u);
+      if (warp == 0) cs_threshold_warp(hist, K, bc);
       __syncthreads();
-      cluster.sync();  // histograms published
-      // C: the bin holding the need-th largest candidate
-      uint4 pv[C];
-      uint32_t tot[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-      for (int cc = 0; cc < C; ++cc) {
-        pv[cc] = reinterpret_cast<const uint4*>(cluster.map_shared_rank(hist, cc))[tid];
-        tot[0] += pv[cc].x;
-        tot[1] += pv[cc].y;
-        tot[2] += pv[cc].z;
-        tot[3] += pv[cc].w;
-      }
-      const int mine = static_cast<int>(tot[0] + tot[1] + tot[2] + tot[3]);
-      int all_cnt;
-      const int excl = cs_block_scan(mine, &all_cnt);
-      int run = all_cnt - excl - mine;  // candidates in higher bins (higher threads)
-#pragma unroll
-      for (int j = 3; j >= 0; --j) {
-        const int tj = static_cast<int>(tot[j]);
-        if (run < need && need <= run + tj) {
-          bc[0] = tid * 4 + j;
-          bc[1] = run;
-          bc[2] = tj;
-        }
-        run += tj;
-      }
-      __syncthreads();
-      const int bstar = bc[0], above = bc[1], cnt = bc[2];
-      if (tid == (bstar >> 2)) {  // each CTA's share of the threshold bin
-#pragma unroll
-        for (int cc = 0; cc < C; ++cc) {
-          const uint32_t v4[4] = {pv[cc].x, pv[cc].y, pv[cc].z, pv[cc].w};
-          peer_cnt[cc] = static_cast<int>(v4[bstar & 3]);
-        }
-      }
-      __syncthreads();
-      const int need2 = need - above;  // 1 <= need2 <= cnt
-      const bool take_all = need2 == cnt;
-      const bool by_page = !take_all && (bstar < 2 || bstar == kCsBins - 1 ||
-                                         !(range > 0.f) || level == kCsMaxLevels - 1);
-      const bool exact = !take_all && !by_page && cnt <= kCsMaxCand;
-      for (int i = tid; i < nloc; i += kCsThreads) {
-        if (st[i] != 1) continue;
-        const int b = cs_bin(sc[i], gmin, range);
-        st[i] = b > bstar ? 2 : (b < bstar ? 0 : (take_all ? 2 : 1));
-      }
-      __syncthreads();
-      if (take_all) break;
-      if (by_page) {
-        // equal scores: the lower pages win; pages of lower CTAs are lower
-        int base = 0;
-        for (int cc = 0; cc < c; ++cc) base += peer_cnt[cc];
-        const int ch = (nloc + kCsThreads - 1) / kCsThreads;
-        const int i0 = min(nloc, tid * ch), i1 = min(nloc, i0 + ch);
-        int m = 0;
-        for (int i = i0; i < i1; ++i) m += st[i] == 1;
-        int tot_m;
-        int r = base + cs_block_scan(m, &tot_m);
-        for (int i = i0; i < i1; ++i)
-          if (st[i] == 1) st[i] = (r++ < need2) ? 2 : 0;
-        __syncthreads();
-        break;
-      }
-      if (exact) {
-        // few candidates: rank each by (score, page) against all of them
-        if (tid == 0) cnt_s = 0;
-        __syncthreads();
-        for (int i = tid; i < nloc; i += kCsThreads)
-          if (st[i] == 1)
-            cand[atomicAdd(&cnt_s, 1)] =
-                make_uint2(float_to_key(sc[i]), static_cast<uint32_t>(pos_lo + i));
-        __syncthreads();
-        cluster.sync();  // candidate lists published
-        for (int g = tid; g < cnt; g += kCsThreads) {
-          int cc = 0, off = 0;
-          while (cc < C - 1 && g >= off + peer_cnt[cc]) off += peer_cnt[cc++];
-          candall[g] = cluster.map_shared_rank(cand, cc)[g - off];
-        }
-        __syncthreads();
-        for (int i = tid; i < cnt_s; i += kCsThreads) {
-          const uint2 me = cand[i];
-          int r = 0;
-          for (int g = 0; g < cnt; ++g) {
-            const uint2 o = candall[g];
-            r += (o.x > me.x) || (o.x == me.x && o.y < me.y);
-          }
-          st[me.y - pos_lo] = r < need2 ? 2 : 0;
-        }
-        __syncthreads();
-        break;
-      }
-      need = need2;  // refine inside the threshold bin
+      lb = bc[0];
     }
-    // this CTA's selected pages in page order, as physical ids
-    {
-      const int ch = (nloc + kCsThreads - 1) / kCsThreads;
-      const int i0 = min(nloc, tid * ch), i1 = min(nloc, i0 + ch);
-      int m = 0;
-      for (int i = i0; i < i1; ++i) m += st[i] == 2;
-      int tot_sel;
-      int w = cs_block_scan(m, &tot_sel);
-      for (int i = i0; i < i1; ++i) {
-        if (st[i] != 2) continue;
-        int pid = __ldcg(a.kv_indices + pos_lo + i);
-        if (pid < 0 || pid >= a.kv_cap) {
-          raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
-          pid = -1;
-        }
-        sel[w++] = pid;
-      }
-      if (tid == 0) xs.n_sel = tot_sel;
+    for (int i0 = rk0 + warp * 32; i0 < nloc; i0 += kCsThreads) {  // one atomic per warp
+      const int i = i0 + lane;
+      const bool in = i < nloc && (lb < 0 || cs_bin_mul(sc[i], lmin, lscale) >= lb);
+      const unsigned bal = __ballot_sync(0xffffffffu, in);
+      int base = 0;
+      if (lane == 0 && bal) base = atomicAdd(&cnt_s, __popc(bal));
+      base = __shfl_sync(0xffffffffu, base, 0);
+      const int j = base + __popc(bal & ((1u << lane) - 1u));
+      if (in && j < CAPL)
+        cand[j] = make_uint4(float_to_key(sc[i]), static_cast<uint32_t>(pos_lo + i),
+                             static_cast<uint32_t>(pidl[i]), 0u);
     }
     __syncthreads();
-    cluster.sync();  // selections published
+    const int m_c = cnt_s;
+    if (m_c <= CAPL) {
+      // sort by counting, TPC threads per candidate
+      int m2 = 1;
+      while (m2 < m_c) m2 <<= 1;
+      const int tpc = m2 >= kCsThreads ? 1 : (kCsThreads / m2 > 32 ? 32 : kCsThreads / m2);
+      for (int base = 0; base < m_c; base += kCsThreads / tpc) {
+        const int i = base + tid / tpc, sub = tid % tpc;
+        int r = 0;
+        uint4 me = make_uint4(0u, 0u, 0u, 0u);
+        if (i < m_c) {
+          me = cand[i];
+          int j = sub;
+          for (; j + 3 * tpc < m_c; j += 4 * tpc) {  // four independent loads in flight
+            const uint4 o0 = cand[j], o1 = cand[j + tpc], o2 = cand[j + 2 * tpc],
+                        o3 = cand[j + 3 * tpc];
+            r += cs_beats(o0.x, o0.y, me.x, me.y) + cs_beats(o1.x, o1.y, me.x, me.y) +
+                 cs_beats(o2.x, o2.y, me.x, me.y) + cs_beats(o3.x, o3.y, me.x, me.y);
+          }
+          for (; j < m_c; j += tpc) {
+            const uint4 o = cand[j];
+            r += cs_beats(o.x, o.y, me.x, me.y);
+          }
+        }
+        for (int off = tpc >> 1; off > 0; off >>= 1) r += __shfl_xor_sync(0xffffffffu, r, off);
+        if (i < m_c && sub == 0) lst[r] = me;
+      }
+    }
+    if (tid == 0) {
+      xs.m = m_c;
+      xs.ovf = m_c > CAPL;
+    }
+    __syncthreads();
+    // Publish (release) first, then start the likely winners' loads, so the
+    // release never waits for them: K/V of the first candidates into the
+    // ring, a few more warmed in L2.
+    cluster_arrive_release();
+    if (m_c <= CAPL) {
+      n_spec = min(kCsWarps, n_special + m_c);
+      if (warp < n_spec) {
+        const int pid = warp < n_special
+                            ? ((c == C - 1 && warp == 0) ? last_pid : __ldcg(a.kv_indices))
+                            : static_cast<int>(lst[warp - n_special].z);
+        spec_issued = pid >= 0 && pid < a.kv_cap;
+        if (lane == 0 && spec_issued) load_page(pid);
+      }
+      const int npf = min(m_c, (5 * K + 4 * C - 1) / (4 * C) + 2);
+      const int j0 = kCsWarps - n_special;
+      if (tid + j0 < npf) {
+        const int pid = static_cast<int>(lst[tid + j0].z);
+        if (pid >= 0) {
+          tma_prefetch_l2_3d(&kv_map, 0, h, pid * 2 * P);
+          tma_prefetch_l2_3d(&kv_map, 0, h, pid * 2 * P + P);
+        }
+      }
+    }
+    cluster_wait_acquire();  // local candidate lists published
     if (warp == 0) {
-      int v = lane < C ? cluster.map_shared_rank(&xs, lane)->n_sel : 0;
+      int v = 0, ov = 0;
+      if (lane < C) {
+        const CsXchg* px = cluster.map_shared_rank(&xs, lane);
+        v = px->m;
+        ov = px->ovf;
+      }
       int x = v;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -547,71 +734,367 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       }
       if (lane < C) peer_off[lane] = x - v;
       if (lane == C - 1) peer_off[C] = x;
+      const unsigned any = __ballot_sync(0xffffffffu, ov != 0);
+      if (lane == 0) {
+        fast_s = any == 0u;
+        nw_s = 0;
+      }
     }
     __syncthreads();
+    fast = fast_s != 0;
+    if (fast) {
+      const int M = peer_off[C];  // K <= M <= kCsGather
+      for (int g = tid; g < M; g += kCsThreads) {  // every list, keys and pages apart
+        int cc = 0;
+        while (cc < C - 1 && g >= peer_off[cc + 1]) ++cc;
+        const uint4 e = cluster.map_shared_rank(lst, cc)[g - peer_off[cc]];
+        gkey[g] = e.x;
+        gpos[g] = e.y;
+      }
+      __syncthreads();
+      bool win = false;
+      if (tid < m_c) {
+        const uint32_t mk = gkey[peer_off[c] + tid], mpos = gpos[peer_off[c] + tid];
+        // the entries of every other list that beat mine: binary searches
+        // of all lists in lockstep (independent loads in flight)
+        int lo[C], hi[C];
+#pragma unroll
+        for (int cc = 0; cc < C; ++cc) {
+          lo[cc] = cc == c ? 0 : peer_off[cc];
+          hi[cc] = cc == c ? 0 : peer_off[cc + 1];
+        }
+        bool more = true;
+        while (more) {
+          more = false;
+#pragma unroll
+          for (int cc = 0; cc < C; ++cc) {
+            if (lo[cc] < hi[cc]) {
+              const int mid = (lo[cc] + hi[cc]) >> 1;
+              if (cs_beats(gkey[mid], gpos[mid], mk, mpos)) lo[cc] = mid + 1;
+              else hi[cc] = mid;
+              more = true;
+            }
+          }
+        }
+        int r = tid;  // rank within its own list
+#pragma unroll
+        for (int cc = 0; cc < C; ++cc)
+          if (cc != c) r += lo[cc] - peer_off[cc];
+        win = r < K;
+        if (win && sel_row) sel_row[r + r_lo] = static_cast<int>(lst[tid].z);
+      }
+      const int w_c = __syncthreads_count(win);  // the winners are lst[0, w_c)
+      n_items = n_special + w_c;
+      for (int j = tid; j < n_items; j += kCsThreads)
+        items[j] = j < n_special ? ((c == C - 1 && j == 0) ? last_pid : __ldcg(a.kv_indices))
+                                 : static_cast<int>(lst[j - n_special].z);
+      if (c == C - 1) last_item = 0;
+      if (sel_row && tid == 0) {
+        if (sink_owner) sel_row[0] = __ldcg(a.kv_indices);
+        if (c == C - 1) sel_row[T - 1] = last_pid;
+      }
+    } else {
+      // ---- fallback: exact selection by levels over the whole cluster
+      uint2* candall = reinterpret_cast<uint2*>(gkey);  // gkey and gpos: 2 * kCsGather words
+      uint2* cand2 = reinterpret_cast<uint2*>(cand);
+      int* sel = pidl;  // this CTA's selected pages (positions), page order
+      int need = K;
+      for (int level = 0; need > 0; ++level) {
+        // A: finite range of the candidates (state 1), cluster-wide
+        float lo = INFINITY, hi = -INFINITY;
+        for (int i = tid; i < nloc; i += kCsThreads) {
+          if (st[i] != 1) continue;
+          const float x = sc[i];
+          if (isfinite(x)) {
+            lo = fminf(lo, x);
+            hi = fmaxf(hi, x);
+          }
+        }
+        cs_block_minmax(lo, hi, &xs.fmin, &xs.fmax);
+        cluster.sync();  // ranges published; peers are done with this CTA's histogram
+        if (warp == 0) {
+          float gl = INFINITY, gh = -INFINITY;
+          if (lane < C) {
+            const CsXchg* px = cluster.map_shared_rank(&xs, lane);
+            gl = px->fmin;
+            gh = px->fmax;
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            gl = fminf(gl, __shfl_xor_sync(0xffffffffu, gl, o));
+            gh = fmaxf(gh, __shfl_xor_sync(0xffffffffu, gh, o));
+          }
+          if (lane == 0) {
+            gsh[0] = gl;
+            gsh[1] = gh;
+          }
+        }
+        for (int b = tid; b < kCsBins; b += kCsThreads) hist[b] = 0u;
+        __syncthreads();
+        const float gmin = gsh[0], gmax = gsh[1];
+        const float range = (gmax > gmin && gmax - gmin < INFINITY) ? gmax - gmin : 0.f;
+        // B: histogram of the candidates, cluster-wide
+        for (int i = tid; i < nloc; i += kCsThreads)
+          if (st[i] == 1) atomicAdd(&hist[cs_bin(sc[i], gmin, range)], 1u);
+        __syncthreads();
+        cluster.sync();  // histograms published
+        // C: the bin holding the need-th largest candidate
+        uint4 pv[C];
+        uint32_t tot[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int cc = 0; cc < C; ++cc) {
+          pv[cc] = reinterpret_cast<const uint4*>(cluster.map_shared_rank(hist, cc))[tid];
+          tot[0] += pv[cc].x;
+          tot[1] += pv[cc].y;
+          tot[2] += pv[cc].z;
+          tot[3] += pv[cc].w;
+        }
+        const int mine = static_cast<int>(tot[0] + tot[1] + tot[2] + tot[3]);
+        int all_cnt;
+        const int excl = cs_block_scan(mine, &all_cnt);
+        int run = all_cnt - excl - mine;  // candidates in higher bins (higher threads)
+#pragma unroll
+        for (int j = 3; j >= 0; --j) {
+          const int tj = static_cast<int>(tot[j]);
+          if (run < need && need <= run + tj) {
+            bc[0] = tid * 4 + j;
+            bc[1] = run;
+            bc[2] = tj;
+          }
+          run += tj;
+        }
+        __syncthreads();
+        const int bstar = bc[0], above = bc[1], cnt = bc[2];
+        if (tid == (bstar >> 2)) {  // each CTA's share of the threshold bin
+#pragma unroll
+          for (int cc = 0; cc < C; ++cc) {
+            const uint32_t v4[4] = {pv[cc].x, pv[cc].y, pv[cc].z, pv[cc].w};
+            peer_cnt[cc] = static_cast<int>(v4[bstar & 3]);
+          }
+        }
+        __syncthreads();
+        const int need2 = need - above;  // 1 <= need2 <= cnt
+        const bool take_all = need2 == cnt;
+        const bool by_page = !take_all && (bstar < 2 || bstar == kCsBins - 1 ||
+                                           !(range > 0.f) || level == kCsMaxLevels - 1);
+        const bool exact = !take_all && !by_page && cnt <= kCsMaxCand;
+        for (int i = tid; i < nloc; i += kCsThreads) {
+          if (st[i] != 1) continue;
+          const int b = cs_bin(sc[i], gmin, range);
+          st[i] = b > bstar ? 2 : (b < bstar ? 0 : (take_all ? 2 : 1));
+        }
+        __syncthreads();
+        if (take_all) break;
+        if (by_page) {
+          // equal scores: the lower pages win; pages of lower CTAs are lower
+          int base = 0;
+          for (int cc = 0; cc < c; ++cc) base += peer_cnt[cc];
+          const int ch = (nloc + kCsThreads - 1) / kCsThreads;
+          const int i0 = min(nloc, tid * ch), i1 = min(nloc, i0 + ch);
+          int m = 0;
+          for (int i = i0; i < i1; ++i) m += st[i] == 1;
+          int tot_m;
+          int r = base + cs_block_scan(m, &tot_m);
+          for (int i = i0; i < i1; ++i)
+            if (st[i] == 1) st[i] = (r++ < need2) ? 2 : 0;
+          __syncthreads();
+          break;
+        }
+        if (exact) {
+          // few candidates: rank each by (score, page) against all of them
+          if (tid == 0) cnt_s = 0;
+          __syncthreads();
+          for (int i = tid; i < nloc; i += kCsThreads)
+            if (st[i] == 1)
+              cand2[atomicAdd(&cnt_s, 1)] =
+                  make_uint2(float_to_key(sc[i]), static_cast<uint32_t>(pos_lo + i));
+          __syncthreads();
+          cluster.sync();  // candidate lists published
+          for (int g = tid; g < cnt; g += kCsThreads) {
+            int cc = 0, off = 0;
+            while (cc < C - 1 && g >= off + peer_cnt[cc]) off += peer_cnt[cc++];
+            candall[g] = cluster.map_shared_rank(cand2, cc)[g - off];
+          }
+          __syncthreads();
+          for (int i = tid; i < cnt_s; i += kCsThreads) {
+            const uint2 me = cand2[i];
+            int r = 0;
+            for (int g = 0; g < cnt; ++g) {
+              const uint2 o = candall[g];
+              r += cs_beats(o.x, o.y, me.x, me.y);
+            }
+            st[me.y - pos_lo] = r < need2 ? 2 : 0;
+          }
+          __syncthreads();
+          break;
+        }
+        need = need2;  // refine inside the threshold bin
+      }
+      {  // this CTA's selected pages in page order (sink page 0 included)
+        const int ch = (nloc + kCsThreads - 1) / kCsThreads;
+        const int i0 = min(nloc, tid * ch), i1 = min(nloc, i0 + ch);
+        int m = 0;
+        for (int i = i0; i < i1; ++i) m += st[i] == 2;
+        int tot_sel;
+        int w = cs_block_scan(m, &tot_sel);
+        for (int i = i0; i < i1; ++i)
+          if (st[i] == 2) sel[w++] = pos_lo + i;
+        if (tid == 0) xs.n_sel = tot_sel;
+      }
+      __syncthreads();
+      cluster.sync();  // selections published
+      if (warp == 0) {
+        int v = lane < C ? cluster.map_shared_rank(&xs, lane)->n_sel : 0;
+        int x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, x, o);
+          if (lane >= o) x += y;
+        }
+        if (lane < C) peer_off[lane] = x - v;
+        if (lane == C - 1) peer_off[C] = x;
+      }
+      __syncthreads();
+      // the page ids of this CTA's decode slots, from the owners' lists
+      for (int sl = s_lo + tid; sl < min(s_hi, T - 1); sl += kCsThreads) {
+        int pid = -1;
+        if (sl < peer_off[C]) {
+          int cc = 0;
+          while (cc < C - 1 && sl >= peer_off[cc + 1]) ++cc;
+          const int pos = cluster.map_shared_rank(sel, cc)[sl - peer_off[cc]];
+          if (pos >= 0 && pos < N) pid = __ldcg(a.kv_indices + pos);
+        }
+        items[sl - s_lo] = pid;
+        if (sel_row) sel_row[sl] = pid;
+      }
+    }
+  } else {
+    for (int sl = s_lo + tid; sl < min(s_hi, T - 1); sl += kCsThreads) {  // every page
+      const int pid = __ldcg(a.kv_indices + sl);
+      items[sl - s_lo] = pid;
+      if (sel_row) sel_row[sl] = pid;
+    }
   }
+  if (!sparse || !fast) {
+    n_items = s_hi - s_lo;
+    if (c == C - 1) {
+      last_item = T - 1 - s_lo;
+      if (tid == 0) {
+        items[last_item] = last_pid;
+        if (sel_row) sel_row[T - 1] = last_pid;
+      }
+    }
+  }
+  if (sel_row && c == C - 1)
+    for (int i = T + tid; i < a.sel_cols; i += kCsThreads) sel_row[i] = -1;
+  __syncthreads();
+  // no shared memory of a peer is read after this point (the values read are
+  // consumed), so the arrival need not order anything
+  cluster_arrive_relaxed();
 
   // ------------------------------------------------------------- 3 decode
-  // slots: the selected pages (in page order), then the last page
-  const int T = sparse ? k : (N <= k ? N : 1);
-  const int last_pid = __ldcg(a.kv_indices + N - 1);
-  if (a.selected_out) {
-    int32_t* row = a.selected_out + static_cast<size_t>(h) * a.sel_cols;
-    if (sparse) {
-      for (int i = tid; i < xs.n_sel; i += kCsThreads)
-        if (peer_off[c] + i < T - 1) row[peer_off[c] + i] = sel[i];
-    } else if (c == 0) {
-      for (int i = tid; i < T - 1; i += kCsThreads) row[i] = __ldcg(a.kv_indices + i);
-    }
-    if (c == C - 1)
-      for (int i = T - 1 + tid; i < a.sel_cols; i += kCsThreads) row[i] = i == T - 1 ? last_pid : -1;
-  }
-  const int s_lo = (c * T) / C, s_hi = ((c + 1) * T) / C;
   float qs[CPL];
 #pragma unroll
   for (int i = 0; i < CPL; ++i) qs[i] = qv[i] * a.scale_log2;
   float m = -INFINITY, l = 0.f, o[CPL];
 #pragma unroll
   for (int i = 0; i < CPL; ++i) o[i] = 0.f;
-  for (int s = s_lo + warp; s < s_hi; s += kCsWarps) {
-    int ntok = 0;
-    if (lane == 0) {
-      int pid = -1;
-      if (s == T - 1) {
-        pid = last_pid;
-        ntok = a.last_len;
-      } else if (sparse) {
-        int cc = 0;
-        while (cc < C - 1 && s >= peer_off[cc + 1]) ++cc;
-        if (s < peer_off[C]) pid = cluster.map_shared_rank(sel, cc)[s - peer_off[cc]];
-        ntok = P;
-      } else {
-        pid = __ldcg(a.kv_indices + s);
-        ntok = P;
-      }
-      if (pid < 0 || pid >= a.kv_cap) {
-        raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
-        ntok = 0;
-      }
-      if (ntok > 0) {
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(bar, 2u * tile_bytes);
-        tma_load_3d(slot, &kv_map, 0, h, pid * 2 * P, bar);
-        tma_load_3d(slot + tile_bytes, &kv_map, 0, h, pid * 2 * P + P, bar);
-      }
-    }
-    ntok = __shfl_sync(0xffffffffu, ntok, 0);
-    if (ntok > 0) {
-      const bool got = mbar_wait_bounded(bar, par, a.err);
-      par ^= 1u;
-      if (got) {
-        const __half* Kt = reinterpret_cast<const __half*>(slot);
-        for (int t0 = 0; t0 < ntok; t0 += 8) attend8<D>(Kt, Kt + P * D, t0, ntok, P, qs, m, l, o);
-      }
-    }
-    __syncwarp();
+  const size_t HD = static_cast<size_t>(H) * D;
+  const size_t col = static_cast<size_t>(h) * D + lane * CPL;
+  const bool preloaded = sparse && fast;  // items [0, n_spec) sit in the warps' slots
+  if (spec_issued && (!preloaded || warp >= n_items)) {  // loaded but not attended: drain
+    mbar_wait_bounded(bar, par, a.err);
+    par ^= 1u;
   }
-  // merge the warps of this CTA
+  for (int j = warp; j < n_items; j += kCsWarps) {
+    const bool is_last = j == last_item;
+    int pid = items[j];
+    if (pid < 0 || pid >= a.kv_cap) {
+      if (lane == 0) raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
+      continue;
+    }
+    if (!(preloaded && j < n_spec)) {  // (a preloaded item's load is spec_issued)
+      if (lane == 0) load_page(pid);
+      __syncwarp();
+    }
+    const int ntok = is_last ? a.last_len : P;
+    // the new token (a1, decode_page.cuh:392-506) and the last page's
+    // running key max/min, read while the tiles are in flight
+    Vec kn, vn, mxo, mno;
+    const int entry = a.last_len - 1, mentry = (N - 1) % P;
+    const bool meta_ok = app_mpid >= 0 && app_mpid < a.meta_cap;
+    __half* mk = a.meta + ((static_cast<size_t>(app_mpid) * 2 + 0) * P + mentry) * HD + col;
+    __half* mv = a.meta + ((static_cast<size_t>(app_mpid) * 2 + 1) * P + mentry) * HD + col;
+    if (is_last) {
+      kn = *reinterpret_cast<const Vec*>(a.k_new + col);
+      vn = *reinterpret_cast<const Vec*>(a.v_new + col);
+      if (entry > 0 && meta_ok) {
+        mxo = *reinterpret_cast<const Vec*>(mk);
+        mno = *reinterpret_cast<const Vec*>(mv);
+      }
+    }
+    const bool got = mbar_wait_bounded(bar, par, a.err);
+    par ^= 1u;
+    if (!got) continue;
+    __half* Kt = reinterpret_cast<__half*>(slot);
+    __half* Vt = Kt + P * D;
+    if (is_last) {  // the new token is row `entry` of the page
+      *reinterpret_cast<Vec*>(Kt + entry * D + lane * CPL) = kn;
+      *reinterpret_cast<Vec*>(Vt + entry * D + lane * CPL) = vn;
+      __syncwarp();
+    }
+    cs_attend_page<D>(Kt, Vt, ntok, qs, m, l, o);
+    if (is_last) {
+      // write the token, the max/min (init -+65504 on a new page) and, when
+      // the token fills the page, v_log_norm = log(||mean_t V||_2 + 1e-6)
+      *reinterpret_cast<Vec*>(a.kv + (static_cast<size_t>(pid) * 2 * P + entry) * HD + col) = kn;
+      *reinterpret_cast<Vec*>(a.kv + ((static_cast<size_t>(pid) * 2 + 1) * P + entry) * HD +
+                              col) = vn;
+      if (meta_ok) {
+        if (entry == 0) {
+          const __half2 lo2 = __float2half2_rn(-65504.f), hi2 = __float2half2_rn(65504.f);
+#pragma unroll
+          for (int i = 0; i < CPL / 2; ++i) {
+            reinterpret_cast<__half2*>(&mxo)[i] = lo2;
+            reinterpret_cast<__half2*>(&mno)[i] = hi2;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < CPL / 2; ++i) {
+          const __half2 k2 = reinterpret_cast<const __half2*>(&kn)[i];
+          reinterpret_cast<__half2*>(&mxo)[i] =
+              __hmax2(reinterpret_cast<const __half2*>(&mxo)[i], k2);
+          reinterpret_cast<__half2*>(&mno)[i] =
+              __hmin2(reinterpret_cast<const __half2*>(&mno)[i], k2);
+        }
+        *reinterpret_cast<Vec*>(mk) = mxo;
+        *reinterpret_cast<Vec*>(mv) = mno;
+      } else if (lane == 0) {
+        raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
+      }
+      if (entry + 1 == P) {
+        float sum[CPL];
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) sum[i] = 0.f;
+        for (int t = 0; t < P; ++t) {
+          float f[CPL];
+          load_row<CPL>(Vt + t * D + lane * CPL, f);
+#pragma unroll
+          for (int i = 0; i < CPL; ++i) sum[i] += f[i];
+        }
+        const float inv = 1.f / P;
+        float l2 = 0.f;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) l2 += (sum[i] * inv) * (sum[i] * inv);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) l2 += __shfl_xor_sync(0xffffffffu, l2, off);
+        if (lane == 0)
+          a.vlog[static_cast<size_t>(pid) * H + h] = __float2half_rn(logf(sqrtf(l2) + 1e-6f));
+      }
+    }
+    __syncwarp();  // the slot is consumed before this warp's next load
+  }
+  // merge the warps of this CTA, then push the CTA's state to CTA 0
   {
     float* mw = mrg + warp * (D + 2);
 #pragma unroll
@@ -622,6 +1105,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     }
   }
   __syncthreads();
+  float* xo0 = cluster.map_shared_rank(xo, 0) + c * (D + 2);
   if (tid < D) {
     float M = -INFINITY;
 #pragma unroll
@@ -635,36 +1119,47 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         O += f * mrg[w * (D + 2) + tid];
       }
     }
-    xo[tid] = O;
+    xo0[tid] = O;
     if (tid == 0) {
-      xs.M = M;
-      xs.L = Ls;
+      xo0[D] = M;
+      xo0[D + 1] = Ls;
     }
   }
   __syncthreads();
-  cluster.sync();  // partial states published
-  constexpr int DPC = D / C;
-  if (tid < DPC) {
-    const int d = c * DPC + tid;
-    float MM = -INFINITY;
-#pragma unroll
-    for (int cc = 0; cc < C; ++cc) MM = fmaxf(MM, cluster.map_shared_rank(&xs, cc)->M);
-    float LL = 0.f, OO = 0.f;
-    if (MM != -INFINITY) {
-#pragma unroll
-      for (int cc = 0; cc < C; ++cc) {
-        const CsXchg* px = cluster.map_shared_rank(&xs, cc);
-        const float f = fast_exp2(px->M - MM);
-        LL += f * px->L;
-        OO += f * cluster.map_shared_rank(xo, cc)[d];
-      }
+  if (c != 0) {
+    if (tid == 0) {
+      asm volatile("fence.acq_rel.cluster;" ::: "memory");
+      mbar_arrive_remote(&merge_bar, 0);
     }
-    a.o[static_cast<size_t>(h) * D + d] = __float2half_rn(LL > 0.f ? OO / LL : 0.f);
+  } else {
+    if (C > 1) {  // bounded wait for the other CTAs' states
+      bool arrived = false;
+      for (uint32_t i = 0; i < (1u << 26) && !arrived; ++i) {
+        arrived = mbar_try_wait_cluster(&merge_bar, 0u);
+        if (!arrived && i > 64) __nanosleep(32);
+      }
+      if (!arrived && tid == 0) raise_dev_error(a.err, AOAKV_DEV_ERR_TIMEOUT);
+    }
+    if (tid < D) {
+      float MM = -INFINITY;
+#pragma unroll
+      for (int cc = 0; cc < C; ++cc) MM = fmaxf(MM, xo[cc * (D + 2) + D]);
+      float LL = 0.f, OO = 0.f;
+      if (MM != -INFINITY) {
+#pragma unroll
+        for (int cc = 0; cc < C; ++cc) {
+          const float f = fast_exp2(xo[cc * (D + 2) + D] - MM);
+          LL += f * xo[cc * (D + 2) + D + 1];
+          OO += f * xo[cc * (D + 2) + tid];
+        }
+      }
+      a.o[static_cast<size_t>(h) * D + tid] = __float2half_rn(LL > 0.f ? OO / LL : 0.f);
+    }
   }
-  cluster.sync();  // no CTA leaves while a peer still reads its shared memory
+  cluster_wait_acquire();  // every peer is past its last read of this CTA's memory
 }
 
-using KernelFn = void (*)(CUtensorMap, CUtensorMap, ClusterStepArgs, int);
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, ClusterStepArgs, CsShape);
 
 template <int D>
 const void* kernel_for(int C) {
@@ -693,22 +1188,27 @@ std::atomic<int> g_cluster_pdl{-1};
 
 }  // namespace
 
-int cluster_step_plan(int H, int D, int P, int max_pages, ClusterPlan* plan) {
-  if ((D != 64 && D != 128) || P < 1 || P > kCsMaxPage || H < 1 || H > 65535 || max_pages < 1)
+int cluster_step_plan(int H, int D, int P, int max_pages, int max_slots, ClusterPlan* plan) {
+  if ((D != 64 && D != 128) || P < 1 || P > kCsMaxPage || H < 1 || H > 65535 || max_pages < 1 ||
+      max_slots < 1)
     return 0;
+  if (max_slots > max_pages) max_slots = max_pages;
   const int sms = num_sms();
   int C = 8;
   while (C > 1 && H * C > sms) C >>= 1;
   int n_st = (max_pages - 1 + P - 1) / P;
   if (n_st < 1) n_st = 1;
-  int max_local = (n_st + C - 1) / C * P;
-  size_t smem = static_cast<size_t>(cs_layout(D, P, max_local).total) + 128;
+  auto smem_for = [&](int cl) {
+    const int ml = (n_st + cl - 1) / cl * P;
+    return static_cast<size_t>(cs_layout(D, P, cl, ml, max_slots).total) + 128;
+  };
+  size_t smem = smem_for(C);
   while (smem > 200 * 1024 && C < 8) {  // long sequences: more CTAs per head
     C <<= 1;
-    max_local = (n_st + C - 1) / C * P;
-    smem = static_cast<size_t>(cs_layout(D, P, max_local).total) + 128;
+    smem = smem_for(C);
   }
   if (smem > 200 * 1024) return 0;
+  const int max_local = (n_st + C - 1) / C * P;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
   const void* fn = kernel_ptr(D, C);
@@ -743,7 +1243,8 @@ int cluster_step_plan(int H, int D, int P, int max_pages, ClusterPlan* plan) {
     fs.max_clusters = ncl;
   }
   plan->cluster = C;
-  plan->max_local = max_local;
+  plan->shape.max_local = max_local;
+  plan->shape.max_slots = max_slots;
   plan->smem = fs.smem_set;
   plan->waves = (H + fs.max_clusters - 1) / fs.max_clusters;
   return 1;
@@ -775,7 +1276,7 @@ int launch_cluster_step(const ClusterStepArgs& a, const CUtensorMap& kv_map,
   }
   if (pdl != 0) {
     cfg.numAttrs = 2;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, kv_map, meta_map, a, plan.max_local);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, kv_map, meta_map, a, plan.shape);
     if (e == cudaSuccess) {
       g_cluster_pdl.store(1);
       return AOAKV_OK;
@@ -785,7 +1286,7 @@ int launch_cluster_step(const ClusterStepArgs& a, const CUtensorMap& kv_map,
     g_cluster_pdl.store(0);
   }
   cfg.numAttrs = 1;
-  AOAKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, kv_map, meta_map, a, plan.max_local),
+  AOAKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, kv_map, meta_map, a, plan.shape),
                  "cluster step launch");
   return AOAKV_OK;
 }

@@ -33,18 +33,24 @@ struct ClusterStepArgs {
   int* err;
 };
 
+// Sizes the kernel's shared memory is carved for.
+struct CsShape {
+  int max_local;    // scored pages per CTA
+  int max_slots;    // attended pages per head, last page included
+};
+
 // Launch shape of the cluster step for one problem size.
 struct ClusterPlan {
   int cluster;      // CTAs per head (1, 2, 4 or 8)
-  int max_local;    // scored pages per CTA the shared memory is sized for
+  CsShape shape;
   size_t smem;      // dynamic shared memory per CTA
   int waves;        // clusters resident at once vs heads: 1 = one wave
 };
 
 // Returns 1 and the plan when the cluster step can run (H heads of head_dim
-// D, page size P, up to max_pages pages); 0 otherwise (the caller uses the
-// multi-kernel chain).
-int cluster_step_plan(int H, int D, int P, int max_pages, ClusterPlan* plan);
+// D, page size P, up to max_pages pages of which up to max_slots are
+// attended); 0 otherwise (the caller uses the multi-kernel chain).
+int cluster_step_plan(int H, int D, int P, int max_pages, int max_slots, ClusterPlan* plan);
 int launch_cluster_step(const ClusterStepArgs& a, const CUtensorMap& kv_map,
                         const CUtensorMap& meta_map, int D, const ClusterPlan& plan,
                         cudaStream_t s);
