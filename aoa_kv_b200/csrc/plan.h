@@ -27,6 +27,10 @@ void carve_decode_ws(void* ws, int H, int D, int max_slots, DecodeArgs& a);
 int check_decode_shape(int H, int D, int P, int kv_cap, int layout);
 // 3-D tensor map over one layer's KV pages: dims {D, H, cap*2*P}, box {D,1,P}.
 int make_kv_tmap(CUtensorMap* map, const void* kv, int H, int D, int P, int cap);
+// The same view with box {64, 1, P} and the 128-byte swizzle: a page's K (or
+// V) rows arrive as D/64 tiles of P rows x 128 bytes, 16-byte units of row r
+// permuted by r mod 8 (bank-conflict-free 8x8 matrix loads).
+int make_kv_tmap_sw128(CUtensorMap* map, const void* kv, int H, int D, int P, int cap);
 // 3-D tensor map over one layer's metadata pages: dims {D, H, meta_cap*2*P},
 // box {D, box_heads, 1} (one page's max or min block for box_heads heads).
 int make_meta_tmap(CUtensorMap* map, const void* meta, int H, int D, int P, int meta_cap,

@@ -204,7 +204,7 @@ int decode_step_impl(
     a.sel_cols = k_pages;
     a.err = dev_error_ptr();
     CUtensorMap kmap, mmap;
-    rc = make_kv_tmap(&kmap, kv_data, H, D, P, kv_capacity_pages);
+    rc = make_kv_tmap_sw128(&kmap, kv_data, H, D, P, kv_capacity_pages);
     if (rc) return rc;
     rc = make_kv_tmap(&mmap, metadata_data, H, D, P, metadata_capacity_pages);
     if (rc) return rc;

@@ -77,7 +77,15 @@ struct CsLayout {
 };
 
 __host__ __device__ inline int cs_up(int x) { return (x + 127) / 128 * 128; }
-__host__ __device__ inline int cs_slot_bytes(int D, int P) { return cs_up(2 * P * D * 2); }
+// One ring slot: a metadata page's max and min tiles (scoring) or a KV page's
+// K and V as D/64 swizzled 16-row tiles of 128-byte rows (decode), 1024-byte
+// aligned (the 128-byte swizzle repeats every 8 rows).
+constexpr int kCsSubTile = 16 * 128;
+__host__ __device__ inline int cs_slot_bytes(int D, int P) {
+  const int score = 2 * P * D * 2, dec = 2 * (D / 64) * kCsSubTile;
+  const int b = score > dec ? score : dec;
+  return (b + 1023) / 1024 * 1024;
+}
 __host__ __device__ inline int cs_capl(int C) { return kCsGather / C; }
 __host__ __device__ inline int cs_max_items(int C, int max_slots) {
   const int a = cs_capl(C) + 2, b = (max_slots + C - 1) / C;
@@ -286,49 +294,100 @@ __device__ __forceinline__ float cs_reduce16(const float part[16]) {
   return r1 + __shfl_xor_sync(0xffffffffu, r1, 1);
 }
 
-// One warp attends the page tile in shared memory (K rows then V rows, P <=
-// 16 rows of D fp16 each, ntok valid): online softmax in the log2 domain,
-// q pre-scaled by sm_scale*log2(e); lane l owns channels [l*CPL, (l+1)*CPL).
+// ------------------------------------------------ tensor-core page attention
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr)
+               : "memory");
+}
+// d += a (16x16 fp16, row) * b (16x8 fp16, col), fp32 accumulate
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Byte offset of 16-byte unit `unit` of row `row` in a 1024-byte-aligned tile
+// of 128-byte rows written by TMA with the 128-byte swizzle.
+__device__ __forceinline__ uint32_t sw128(int row, int unit) {
+  return static_cast<uint32_t>(row * 128 + ((unit ^ (row & 7)) << 4));
+}
+// Shared-memory byte offset of the lane's CPL channels in row `row` of a
+// page's K (or V) tiles (D/64 tiles of kCsSubTile bytes).
 template <int D>
-__device__ __forceinline__ void cs_attend_page(const __half* Kt, const __half* Vt, int ntok,
-                                               const float* qs, float& m, float& l, float* o) {
+__device__ __forceinline__ uint32_t sw_lane_off(int row) {
   constexpr int CPL = D / 32;
-  const int lane = threadIdx.x & 31;
-  float part[16];
+  const int ch = (threadIdx.x & 31) * CPL;
+  return static_cast<uint32_t>((ch >> 6) * kCsSubTile) + sw128(row, (ch & 63) >> 3) +
+         static_cast<uint32_t>((ch & 7) * 2);
+}
+
+// One warp attends one page (ntok valid rows) on the tensor cores:
+// S^T = K q^T (M = 16 tokens, K = D channels; q is column 0 of B) and
+// O^T += V^T P^T (M = 16 channels per tile, K = 16 tokens; P is column 0 of
+// B, rounded to fp16 — the softmax sum adds the same rounded values).
+// Online softmax in the log2 domain. Only column 0 of every C fragment is
+// meaningful: lane 4g holds tokens g, g+8 (S) and channels 16mm+g, 16mm+g+8
+// (acc[mm][0], acc[mm][2]). Rows >= ntok of V must hold finite values (the
+// caller zeroes them).
+template <int D>
+__device__ __forceinline__ void cs_attend_page_tc(uint32_t kb, uint32_t vb, int ntok,
+                                                  const uint32_t (&qb)[D / 16][2],
+                                                  float scale_log2, float& m, float& l,
+                                                  float (&acc)[D / 16][4]) {
+  constexpr int NK = D / 16;
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, mi = lane >> 3, r8 = lane & 7;
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int t = 0; t < 16; ++t) {
-    part[t] = 0.f;
-    if (t < ntok) {
-      float kf[CPL];
-      load_row<CPL>(Kt + t * D + lane * CPL, kf);
-#pragma unroll
-      for (int i = 0; i < CPL; ++i) part[t] = fmaf(qs[i], kf[i], part[t]);
-    }
+  for (int kk = 0; kk < NK; ++kk) {
+    uint32_t a0, a1, a2, a3;
+    ldsm_x4(kb + (kk >> 2) * kCsSubTile + sw128((mi & 1) * 8 + r8, (kk & 3) * 2 + (mi >> 1)), a0,
+            a1, a2, a3);
+    mma16816(s4, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
   }
-  const float sv = cs_reduce16(part);  // lanes 2t, 2t+1: token t
-  const int jt = (lane >> 1) & 15;
-  const float x = jt < ntok ? sv : -INFINITY;
-  float gmax = x;
+  const bool v0 = t == 0 && g < ntok, v1 = t == 0 && g + 8 < ntok;
+  const float x0 = v0 ? s4[0] * scale_log2 : -INFINITY;
+  const float x1 = v1 ? s4[2] * scale_log2 : -INFINITY;
+  float mx = fmaxf(x0, x1);
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, off));
-  const float m_new = fmaxf(m, gmax);  // finite: token 0 is valid
+  for (int off = 4; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  mx = __shfl_sync(0xffffffffu, mx, 0);
+  const float m_new = fmaxf(m, mx);  // finite: token 0 is valid
   const float alpha = fast_exp2(m - m_new);
-  const float pw = jt < ntok ? fast_exp2(sv - m_new) : 0.f;
-  float ps = (lane & 1) ? 0.f : pw;
+  const float p0 = v0 ? __half2float(__float2half_rn(fast_exp2(x0 - m_new))) : 0.f;
+  const float p1 = v1 ? __half2float(__float2half_rn(fast_exp2(x1 - m_new))) : 0.f;
+  float ps = p0 + p1;
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+  for (int off = 4; off < 32; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+  ps = __shfl_sync(0xffffffffu, ps, 0);
   l = l * alpha + ps;
+  // P^T as B: lane t (group 0) holds tokens 2t, 2t+1 and 2t+8, 2t+9
+  const float pa = __shfl_sync(0xffffffffu, p0, 8 * t), pb = __shfl_sync(0xffffffffu, p0, 8 * t + 4);
+  const float pc = __shfl_sync(0xffffffffu, p1, 8 * t), pd = __shfl_sync(0xffffffffu, p1, 8 * t + 4);
+  uint32_t b0 = 0u, b1 = 0u;
+  if (g == 0) {
+    const __half2 h01 = __floats2half2_rn(pa, pb), h89 = __floats2half2_rn(pc, pd);
+    b0 = *reinterpret_cast<const uint32_t*>(&h01);
+    b1 = *reinterpret_cast<const uint32_t*>(&h89);
+  }
 #pragma unroll
-  for (int i = 0; i < CPL; ++i) o[i] *= alpha;
+  for (int mm = 0; mm < NK; ++mm) {
 #pragma unroll
-  for (int t = 0; t < 16; ++t) {
-    const float pt = __shfl_sync(0xffffffffu, pw, 2 * t);
-    if (t < ntok) {
-      float vf[CPL];
-      load_row<CPL>(Vt + t * D + lane * CPL, vf);
-#pragma unroll
-      for (int i = 0; i < CPL; ++i) o[i] = fmaf(pt, vf[i], o[i]);
-    }
+    for (int i = 0; i < 4; ++i) acc[mm][i] *= alpha;
+    uint32_t a0, a1, a2, a3;
+    ldsm_x4_t(vb + (mm >> 2) * kCsSubTile + sw128((mi >> 1) * 8 + r8, (mm & 3) * 2 + (mi & 1)), a0,
+              a1, a2, a3);
+    mma16816(acc[mm], a0, a1, a2, a3, b0, b1);
   }
   m = m_new;
 }
@@ -404,7 +463,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   using Vec = typename LaneVec<CPL>::T;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   __shared__ uint64_t bars[kCsWarps];
   __shared__ uint64_t merge_bar;  // CTA 0: the other CTAs' partial states are in
   __shared__ CsXchg xs;
@@ -473,8 +532,11 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   const int last_pid = __ldcg(a.kv_indices + N - 1);
   const int app_mpid = c == C - 1 ? __ldcg(a.meta_indices + (N - 1) / P) : 0;
   if (warp == w_last && lane == 0 && last_pid >= 0 && last_pid < a.kv_cap) {  // warm L2
-    tma_prefetch_l2_3d(&kv_map, 0, h, last_pid * 2 * P);
-    tma_prefetch_l2_3d(&kv_map, 0, h, last_pid * 2 * P + P);
+#pragma unroll
+    for (int sub = 0; sub < D / 64; ++sub) {
+      tma_prefetch_l2_3d(&kv_map, 64 * sub, h, last_pid * 2 * P);
+      tma_prefetch_l2_3d(&kv_map, 64 * sub, h, last_pid * 2 * P + P);
+    }
   }
 
   float qv[CPL];
@@ -625,8 +687,18 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   auto load_page = [&](int pid) {  // lane 0: the page's K and V tiles into the warp's slot
     fence_proxy_async_smem();  // the slot may hold rows written by this warp (the append)
     mbar_arrive_expect_tx(bar, 2u * tile_bytes);
-    tma_load_3d(slot, &kv_map, 0, h, pid * 2 * P, bar);
-    tma_load_3d(slot + tile_bytes, &kv_map, 0, h, pid * 2 * P + P, bar);
+#pragma unroll
+    for (int sub = 0; sub < D / 64; ++sub) {
+      tma_load_3d(slot + sub * kCsSubTile, &kv_map, 64 * sub, h, pid * 2 * P, bar);
+      tma_load_3d(slot + (D / 64 + sub) * kCsSubTile, &kv_map, 64 * sub, h, pid * 2 * P + P, bar);
+    }
+  };
+  auto warm_page = [&](int pid) {  // L2 prefetch of a page's K and V
+#pragma unroll
+    for (int sub = 0; sub < D / 64; ++sub) {
+      tma_prefetch_l2_3d(&kv_map, 64 * sub, h, pid * 2 * P);
+      tma_prefetch_l2_3d(&kv_map, 64 * sub, h, pid * 2 * P + P);
+    }
   };
   if (sparse) {
     const int K = (k - 1) - r_lo;  // pages to choose among the ranked ones (>= 1)
@@ -712,10 +784,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       const int j0 = kCsWarps - n_special;
       if (tid + j0 < npf) {
         const int pid = static_cast<int>(lst[tid + j0].z);
-        if (pid >= 0) {
-          tma_prefetch_l2_3d(&kv_map, 0, h, pid * 2 * P);
-          tma_prefetch_l2_3d(&kv_map, 0, h, pid * 2 * P + P);
-        }
+        if (pid >= 0) warm_page(pid);
       }
     }
     cluster_wait_acquire();  // local candidate lists published
@@ -993,12 +1062,25 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   cluster_arrive_relaxed();
 
   // ------------------------------------------------------------- 3 decode
-  float qs[CPL];
+  // q as column 0 of the B operand of S^T = K q^T (lanes 0..3: channels
+  // 16kk + 2t, +1 and 16kk + 2t + 8, +9)
+  constexpr int NK = D / 16;
+  uint32_t qb[NK][2];
 #pragma unroll
-  for (int i = 0; i < CPL; ++i) qs[i] = qv[i] * a.scale_log2;
-  float m = -INFINITY, l = 0.f, o[CPL];
+  for (int kk = 0; kk < NK; ++kk) {
+    qb[kk][0] = qb[kk][1] = 0u;
+    if (lane < 4) {
+      const uint32_t* qw = reinterpret_cast<const uint32_t*>(a.q + static_cast<size_t>(h) * D);
+      qb[kk][0] = __ldcg(qw + kk * 8 + lane);
+      qb[kk][1] = __ldcg(qw + kk * 8 + 4 + lane);
+    }
+  }
+  float m = -INFINITY, l = 0.f, acc[NK][4];
 #pragma unroll
-  for (int i = 0; i < CPL; ++i) o[i] = 0.f;
+  for (int mm = 0; mm < NK; ++mm)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[mm][i] = 0.f;
+  const uint32_t kb = smem_addr(slot), vb = kb + (D / 64) * kCsSubTile;
   const size_t HD = static_cast<size_t>(H) * D;
   const size_t col = static_cast<size_t>(h) * D + lane * CPL;
   const bool preloaded = sparse && fast;  // items [0, n_spec) sit in the warps' slots
@@ -1036,14 +1118,19 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     const bool got = mbar_wait_bounded(bar, par, a.err);
     par ^= 1u;
     if (!got) continue;
-    __half* Kt = reinterpret_cast<__half*>(slot);
-    __half* Vt = Kt + P * D;
+    uint8_t* Kt = slot;
+    uint8_t* Vt = slot + (D / 64) * kCsSubTile;
     if (is_last) {  // the new token is row `entry` of the page
-      *reinterpret_cast<Vec*>(Kt + entry * D + lane * CPL) = kn;
-      *reinterpret_cast<Vec*>(Vt + entry * D + lane * CPL) = vn;
-      __syncwarp();
+      *reinterpret_cast<Vec*>(Kt + sw_lane_off<D>(entry)) = kn;
+      *reinterpret_cast<Vec*>(Vt + sw_lane_off<D>(entry)) = vn;
     }
-    cs_attend_page<D>(Kt, Vt, ntok, qs, m, l, o);
+    for (int r = ntok; r < 16; ++r) {  // rows past the page's tokens: finite zeros
+      Vec z;
+      memset(&z, 0, sizeof(z));
+      *reinterpret_cast<Vec*>(Vt + sw_lane_off<D>(r)) = z;
+    }
+    __syncwarp();
+    cs_attend_page_tc<D>(kb, vb, ntok, qb, a.scale_log2, m, l, acc);
     if (is_last) {
       // write the token, the max/min (init -+65504 on a new page) and, when
       // the token fills the page, v_log_norm = log(||mean_t V||_2 + 1e-6)
@@ -1078,7 +1165,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         for (int i = 0; i < CPL; ++i) sum[i] = 0.f;
         for (int t = 0; t < P; ++t) {
           float f[CPL];
-          load_row<CPL>(Vt + t * D + lane * CPL, f);
+          load_row<CPL>(reinterpret_cast<const __half*>(Vt + sw_lane_off<D>(t)), f);
 #pragma unroll
           for (int i = 0; i < CPL; ++i) sum[i] += f[i];
         }
@@ -1097,8 +1184,13 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   // merge the warps of this CTA, then push the CTA's state to CTA 0
   {
     float* mw = mrg + warp * (D + 2);
+    if ((lane & 3) == 0) {  // column 0 of the O^T fragments
 #pragma unroll
-    for (int i = 0; i < CPL; ++i) mw[lane * CPL + i] = o[i];
+      for (int mm = 0; mm < NK; ++mm) {
+        mw[mm * 16 + (lane >> 2)] = acc[mm][0];
+        mw[mm * 16 + (lane >> 2) + 8] = acc[mm][2];
+      }
+    }
     if (lane == 0) {
       mw[D] = m;
       mw[D + 1] = l;
@@ -1200,7 +1292,7 @@ int cluster_step_plan(int H, int D, int P, int max_pages, int max_slots, Cluster
   if (n_st < 1) n_st = 1;
   auto smem_for = [&](int cl) {
     const int ml = (n_st + cl - 1) / cl * P;
-    return static_cast<size_t>(cs_layout(D, P, cl, ml, max_slots).total) + 128;
+    return static_cast<size_t>(cs_layout(D, P, cl, ml, max_slots).total) + 1024;  // + alignment
   };
   size_t smem = smem_for(C);
   while (smem > 200 * 1024 && C < 8) {  // long sequences: more CTAs per head
