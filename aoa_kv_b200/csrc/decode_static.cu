@@ -2,19 +2,25 @@
 // cannot allocate device memory.
 //
 // Who needs it: a serving engine that reserves all device memory for its own
-// pool at start-up and forbids later allocations, a plugin that is called
-// while its host runtime is capturing a stream (where cudaMalloc is not
-// allowed), or a latency-critical caller that must not risk the device-wide
+// pool at start-up, so that any later cudaMalloc fails or is forbidden; a
+// plugin whose host runtime owns every allocation and gives its plugins no
+// allocator; a latency-critical caller that must not risk the device-wide
 // synchronisation cudaMalloc/cudaFree can cause. aoakv_sparse_decode needs a
 // caller-provided workspace for the partial softmax states of its page
 // chunks; this variant keeps them in a fixed device array that the library
 // owns instead.
 //
+// The limit: the partial states of one call, num_heads x chunks x
+// (8 + 4 * head_dim) bytes plus the tickets, must fit the array; a chunk holds
+// up to 8 pages. For 32 heads of head_dim 128 that is num_selected <= 503
+// pages (about 8,000 tokens at page size 16); larger problems are refused.
+//
 // The array is a file-scope __device__ variable of kScratchBytes (1 MiB). It
 // exists once per GPU that loads the library and lives until the process
 // exits. Host code cannot use the array's name as a device address, so the
 // first call on each device resolves the address with cudaGetSymbolAddress
-// while that device is current, and caches it. Because every call shares the
+// while that device is current, and caches it; make that first call before
+// any stream capture. Because every call shares the
 // one array, calls whose kernels overlap on the GPU (two streams, or two host
 // threads on one device) race on it: serialise them. The chunk tickets at the
 // start of the array must be zero when a call starts; each call clears them
@@ -37,7 +43,7 @@ std::mutex g_scratch_mu;
 void* g_scratch_addr[kMaxDev] = {nullptr};
 
 // Device address of g_decode_scratch on the current device (set-up on the
-// first call per device; must not run inside a stream capture).
+// first call per device).
 int scratch_address(void** out) {
   int dev = 0;
   AOAKV_CUDA_TRY(cudaGetDevice(&dev), "noalloc decode: cudaGetDevice");
@@ -66,6 +72,7 @@ extern "C" int aoakv_sparse_decode_noalloc(const void* q, void* o, const void* k
                                            int32_t num_heads, int32_t head_dim,
                                            int32_t page_size, int32_t layout, float sm_scale,
                                            void* stream) {
+  AOAKV_NVTX("aoakv_sparse_decode_noalloc");
   AOAKV_CHECK_ARG(q && o && kv_data, "noalloc decode: NULL pointer argument");
   int rc = check_decode_shape(num_heads, head_dim, page_size, kv_capacity_pages, layout);
   if (rc) return rc;

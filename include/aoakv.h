@@ -209,17 +209,20 @@ AOAKV_API int aoakv_sparse_decode(
  * aoakv_sparse_decode, but the partial softmax states of the page chunks go
  * to a fixed 1 MiB array inside the library (one per GPU that loads it, kept
  * until the process exits) instead of a caller workspace. It calls no
- * cudaMalloc/cudaFree. Use it when the caller's memory is all pre-reserved,
- * when it is invoked during someone else's stream capture, or when an
- * allocation's possible device synchronisation is unacceptable.
+ * cudaMalloc/cudaFree. For callers that cannot allocate: a runtime that
+ * pre-reserves all device memory for its own pool, a host that gives its
+ * plugins no allocator, or a caller that cannot accept the device
+ * synchronisation an allocation may cause.
  *   - The first call on each device resolves the array's address
  *     (cudaGetSymbolAddress); make that first call before any stream capture.
  *   - Every call shares the array: calls that overlap on the GPU race, so
  *     serialise them (one stream per device). Each call zeroes the chunk
  *     tickets it needs on its own stream first.
- *   - Problems whose num_heads x page chunks need more than 1 MiB of partial
- *     states (e.g. 32 heads of head_dim 128 with more than ~60 chunks) return
- *     AOAKV_ERR_UNSUPPORTED; use aoakv_sparse_decode with a workspace. */
+ *   - The partial states, num_heads x chunks x (8 + 4 * head_dim) bytes (a
+ *     chunk holds up to 8 pages), must fit 1 MiB: for 32 heads of head_dim
+ *     128 that allows num_selected <= 503 pages (about 8,000 tokens at page
+ *     size 16). Larger problems return AOAKV_ERR_UNSUPPORTED; use
+ *     aoakv_sparse_decode with a workspace. */
 AOAKV_API int aoakv_sparse_decode_noalloc(
     const void* q, void* o,
     const void* kv_data, int32_t kv_capacity_pages,
