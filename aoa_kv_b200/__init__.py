@@ -8,9 +8,9 @@ Public surface, named after the reference's quest.utils
     apply_rope_in_place, rms_norm_forward, and prefill_forward (not built
     here: it raises NotImplementedError)
 
-plus ``topk_filtering`` (the raw top-k op) and
+plus ``topk_filtering`` (the raw top-k op),
 ``InferenceController.decode_step`` (append + estimate + top-k + decode in one
-library call). The kernels live in libaoakv.so (C ABI: include/aoakv.h).
+library call) and ``StepPlan`` (that step planned once per layer). The kernels live in libaoakv.so (C ABI: include/aoakv.h).
 """
 from . import _lib
 from ._lib import AoaKvError, check_device, device_error
@@ -18,12 +18,13 @@ from .controller import InferenceController, KvCache, KvPool, TensorLayout
 from .decode_wrapper import BatchDecodeWithPagedKVCacheWrapper
 from .ops import (append_kv, apply_rope_in_place, decode_estimate, decode_sparse_attn,
                   decode_topk, prefill_forward, rms_norm_forward, topk_filtering)
+from .step_plan import StepPlan
 
 __all__ = [
     "TensorLayout", "KvCache", "KvPool", "InferenceController",
     "BatchDecodeWithPagedKVCacheWrapper", "append_kv", "prefill_forward", "decode_estimate",
     "decode_topk", "decode_sparse_attn", "rms_norm_forward", "apply_rope_in_place",
-    "topk_filtering", "AoaKvError", "check_device", "device_error",
+    "topk_filtering", "StepPlan", "AoaKvError", "check_device", "device_error",
 ]
 
 

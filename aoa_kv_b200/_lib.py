@@ -24,6 +24,8 @@ _c_i32, _c_i64, _c_p, _c_f = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ct
 _c_size = ctypes.c_size_t
 _c_ip = ctypes.POINTER(ctypes.c_int32)
 _c_sizep = ctypes.POINTER(ctypes.c_size_t)
+_c_pp = ctypes.POINTER(ctypes.c_void_p)
+PLAN_CHAIN = 1
 
 # name -> argtypes (restype is int unless listed in _RESTYPE)
 SIGNATURES = {
@@ -57,6 +59,12 @@ SIGNATURES = {
     "aoakv_decode_step": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p,
                           _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p,
                           _c_size, _c_p],
+    "aoakv_step_plan_create": [_c_pp, _c_p, _c_i32, _c_p, _c_i32, _c_p, _c_i32, _c_i32, _c_i32,
+                               _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32],
+    "aoakv_step_plan_run": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_p,
+                            _c_size, _c_p],
+    "aoakv_step_plan_info": [_c_p, _c_i32, _c_i32, _c_ip, _c_ip],
+    "aoakv_step_plan_destroy": [_c_p],
     "aoakv_decode_step_grid": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p,
                                _c_p, _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                                _c_i32, _c_p, _c_p, _c_size, _c_i32, _c_p],

@@ -160,6 +160,7 @@ class InferenceController:
         self._step_ws = None
         self._step_ws_key = None
         self._layer_ptrs: dict = {}
+        self._plans: dict = {}  # layer -> StepPlan (aoakv_step_plan_*)
 
     @property
     def score_mode(self) -> int:
@@ -261,29 +262,37 @@ class InferenceController:
             self._layer_ptrs[layer_idx] = t
         return t
 
+    def step_plan(self, layer_idx: int, max_ctas: int = 0):
+        """The layer's StepPlan for the current budget (created on first use,
+        re-created only when the budget or the CTA cap changes)."""
+        from .step_plan import StepPlan
+        budget = self.step_page_budget()
+        plan = self._plans.get(layer_idx)
+        if plan is None or plan.page_budget != budget or plan.max_ctas != max_ctas:
+            kv_p, kv_cap, meta_p, meta_cap, vlog_p = self._layer_buffers(layer_idx)
+            if plan is not None:
+                plan.close()
+            plan = StepPlan(kv_p, kv_cap, meta_p, meta_cap, vlog_p, self.num_heads,
+                            self.head_dim, self.page_size, budget, self.score_mode,
+                            self.sink_first_page, max_ctas=max_ctas)
+            self._plans[layer_idx] = plan
+        return plan
+
     def decode_step(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, layer_idx: int,
                     out: torch.Tensor | None = None, selected: torch.Tensor | None = None,
                     max_ctas: int = 0):
         """Append k, v and attend q in one library call (append, estimate,
-        top-k, sparse decode). Call after prepare_metadata(1) and
-        begin_forward(1). q, k, v: [1, H, D] or [H, D] fp16. Returns o like q.
-        max_ctas > 0 caps the fused kernel's grid (several requests' steps on
-        separate streams then run side by side)."""
-        from .ops import _check_half_cuda, _ptr, _stream
+        top-k, sparse decode) through the layer's StepPlan. Call after
+        prepare_metadata(1) and begin_forward(1). q, k, v: [1, H, D] or [H, D]
+        fp16. Returns o like q. max_ctas > 0 caps the step's CTAs (several
+        requests' steps on separate streams then run side by side)."""
+        from .ops import _check_half_cuda, _stream
         for name, t in (("q", q), ("k", k), ("v", v)):
             _check_half_cuda(t, name)
         o = torch.empty_like(q) if out is None else out
+        plan = self.step_plan(layer_idx, max_ctas)
         ws = self._ensure_step_workspace()
-        kv_p, kv_cap, meta_p, meta_cap, vlog_p = self._layer_buffers(layer_idx)
-        args = (_ptr(q), _ptr(k), _ptr(v), _ptr(o), kv_p,
-                _ptr(self.kv_indices_with_last), len(self.kv_cache.indicies),
-                self.kv_cache.last_page_len, kv_cap, meta_p,
-                _ptr(self.metadata_indices), meta_cap, vlog_p, self.num_heads, self.head_dim,
-                self.page_size, self.step_page_budget(), self.score_mode,
-                int(self.sink_first_page), _ptr(selected) if selected is not None else None,
-                _ptr(ws), ws.numel())
-        if max_ctas:
-            _lib.call("aoakv_decode_step_grid", *args, int(max_ctas), _stream(q))
-        else:
-            _lib.call("aoakv_decode_step", *args, _stream(q))
+        plan.run(q, k, v, o, self.kv_indices_with_last, len(self.kv_cache.indicies),
+                 self.kv_cache.last_page_len, self.metadata_indices, selected, ws, ws.numel(),
+                 _stream(q))
         return o

@@ -1,23 +1,48 @@
 // Per-layer decode step for one request: append -> estimate -> top-k ->
-// sparse decode, stream-ordered with programmatic dependent launch, no host
-// synchronisation and no allocation.
+// sparse decode, stream-ordered, with no host synchronisation and no
+// allocation; planned once per layer (aoakv_step_plan_*), run per token.
 //
 // Reference call order: kernels/aoa_kv/quest/models/QuestAttention.py:99-157
 // (append_kv, then need_estimate() ? estimate + topk + sparse decode : decode
 // over every page), with the page budget of controller.py:118-127 and
 // utils/__init__.py:237 (top-(k-1) plus the last page) or, with the sink,
 // filtering/filter_util.py:226-231 and :373-377 (page 0 and the last page
-// forced, k = min(max(3, budget), N)).
+// forced, k = min(max(3, budget), N)). The plan replaces the reference's
+// BatchDecodeHandler begin/forward/end (decode_handler.cuh:73-136,
+// approx_attn.cu:27-151), which re-plans with a device synchronisation and
+// an allocation on every step.
+//
+// Two ways to run a step:
+//   cluster  one launch of step_cluster.cu (the default whenever the shape
+//            fits: head_dim 64/128, page_size <= 16);
+//   chain    append, estimate, top-k and decode as four launches with
+//            programmatic dependent launch (other shapes, or on request).
 #include <cmath>
-#include <cstdlib>
 #include <cstring>
+#include <new>
 
 #include "decode.cuh"
 #include "estimate.cuh"
-#include "fused.h"
 #include "plan.h"
 #include "step_cluster.h"
 #include "topk.cuh"
+
+// The opaque plan behind aoakv_step_plan.
+struct aoakv_step_plan_s {
+  int device;
+  int H, D, P;
+  void* kv;
+  int kv_cap;
+  void* meta;
+  int meta_cap;
+  void* vlog;
+  int budget, mode, sink, max_pages;
+  bool cluster_ok;               // the cluster kernel runs this layer
+  aoakv::ClusterPlan cp;
+  CUtensorMap kv_sw;             // cluster: K/V tiles, 128-byte swizzle
+  CUtensorMap meta_map;          // cluster: metadata tiles
+  CUtensorMap kv_plain;          // chain: the decode kernel's K/V boxes
+};
 
 namespace aoakv {
 namespace {
@@ -39,18 +64,17 @@ __global__ void fill_selected_kernel(int32_t* out, int budget, const int32_t* id
   }
 }
 
-// Workspace: [sync words][decode partials][fp32 scores][selected ids]. The
-// sync words and the decode tickets must be zero between calls.
+// Chain workspace: [decode partials][fp32 scores][selected ids]. The decode
+// tickets must be zero between calls (zeroed once; the kernels re-arm them).
 struct StepWs {
-  size_t sync_off, dec_off, scores_off, idx_off, total;
+  size_t dec_off, scores_off, idx_off, total;
 };
 
 StepWs step_ws_layout(int H, int D, int max_pages, int max_budget) {
   auto up = [](size_t x) { return (x + 255) / 256 * 256; };
   const int max_slots = max_budget < 3 ? 3 : max_budget;
   StepWs w;
-  w.sync_off = 0;
-  size_t off = up(fused_sync_bytes(H));
+  size_t off = 0;
   w.dec_off = off;
   off += up(decode_ws_bytes(H, D, max_slots));
   w.scores_off = off;
@@ -61,41 +85,207 @@ StepWs step_ws_layout(int H, int D, int max_pages, int max_budget) {
   return w;
 }
 
-// Which kernel(s) run a sparse step: the phase-by-phase fused kernel
-// (step_fused.cu) when the shape allows, else the four-launch chain.
-// AOAKV_STEP_IMPL=pipe selects the pipelined two-role kernel (step_pipe.cu;
-// measured slower at the headline shape: its scorers get half the SMs'
-// loads in flight) and =chain the chain (read on every call, for A/B
-// comparisons).
-enum class StepImpl { kCluster, kPipe, kFused, kChain };
+// Pages attended per head: k_pages from the budget rule, k = min(k_pages, N).
+void step_budget(int N, int budget, int sink, int* k_pages, int* k) {
+  *k_pages = sink ? (budget < 3 ? 3 : budget) : budget;
+  *k = *k_pages < N ? *k_pages : N;
+}
 
-struct StepChoice {
-  StepImpl impl;
-  int grid, chunk, n_chunks;
-  size_t smem;
-  ClusterPlan cp;
-};
+int check_plan_args(int H, int D, int P, int kv_cap, int meta_cap, int budget, int mode) {
+  int rc = check_decode_shape(H, D, P, kv_cap, AOAKV_LAYOUT_NHD);
+  if (rc) return rc;
+  AOAKV_CHECK_ARG(budget >= 1, "step: page_budget must be >= 1");
+  AOAKV_CHECK_ARG(mode == AOAKV_SCORE_QUEST || mode == AOAKV_SCORE_AOAKV,
+                  "step: score_mode must be QUEST or AOAKV");
+  AOAKV_CHECK_ARG(meta_cap >= (kv_cap + P - 1) / P,
+                  "step: metadata capacity below ceil(kv_capacity_pages / page_size)");
+  return AOAKV_OK;
+}
 
-StepChoice choose_step(int H, int D, int P, int N, int k, int max_grid = 0) {
-  const char* e = std::getenv("AOAKV_STEP_IMPL");
-  const bool want_chain = e && std::strcmp(e, "chain") == 0;
-  const bool want_pipe = e && std::strcmp(e, "pipe") == 0;
-  const bool want_fused = e && std::strcmp(e, "fused") == 0;
-  StepChoice c = {StepImpl::kChain, 0, 0, 0, 0, {}};
-  if (want_chain) return c;
-  if (!want_pipe && !want_fused && max_grid == 0 && cluster_step_plan(H, D, P, N, k, &c.cp)) {
-    c.impl = StepImpl::kCluster;
-    return c;
+// Fills *p (no allocation): the launch shape, kernel attributes and tensor
+// maps of one layer.
+int plan_init(aoakv_step_plan_s* p, void* kv, int kv_cap, void* meta, int meta_cap, void* vlog,
+              int H, int D, int P, int budget, int mode, int sink, int max_pages, int max_ctas,
+              int flags) {
+  AOAKV_CHECK_ARG(kv && meta && vlog, "step plan: NULL buffer");
+  int rc = check_plan_args(H, D, P, kv_cap, meta_cap, budget, mode);
+  if (rc) return rc;
+  AOAKV_CHECK_ARG(max_pages >= 0 && max_pages <= kv_cap,
+                  "step plan: max_pages must be in [0, kv_capacity_pages]");
+  AOAKV_CHECK_ARG(max_ctas >= 0, "step plan: max_ctas must be >= 0");
+  AOAKV_CHECK_ARG((flags & ~AOAKV_PLAN_CHAIN) == 0, "step plan: unknown flag");
+  AOAKV_CUDA_TRY(cudaGetDevice(&p->device), "step plan: cudaGetDevice");
+  p->H = H;
+  p->D = D;
+  p->P = P;
+  p->kv = kv;
+  p->kv_cap = kv_cap;
+  p->meta = meta;
+  p->meta_cap = meta_cap;
+  p->vlog = vlog;
+  p->budget = budget;
+  p->mode = mode;
+  p->sink = sink != 0;
+  p->max_pages = max_pages ? max_pages : kv_cap;
+  int k_pages, k;
+  step_budget(p->max_pages, budget, p->sink, &k_pages, &k);
+  p->cluster_ok = !(flags & AOAKV_PLAN_CHAIN) &&
+                  cluster_step_plan(H, D, P, p->max_pages, k_pages, max_ctas, &p->cp);
+  if (p->cluster_ok) {
+    rc = make_kv_tmap_sw128(&p->kv_sw, kv, H, D, P, kv_cap);
+    if (rc) return rc;
+    rc = make_kv_tmap(&p->meta_map, meta, H, D, P, meta_cap);
+    if (rc) return rc;
   }
-  if (want_pipe && pipe_supported(H, D, P, N - 1, k - 1, &c.grid, &c.smem, &c.chunk,
-                                  &c.n_chunks)) {
-    c.impl = StepImpl::kPipe;
-    return c;
+  return make_kv_tmap(&p->kv_plain, kv, H, D, P, kv_cap);
+}
+
+int run_cluster(const aoakv_step_plan_s* p, const void* q, const void* k_new, const void* v_new,
+                void* o, const int32_t* kv_indices, int N, int last_len,
+                const int32_t* meta_indices, int32_t* selected_out, int k_pages, int k,
+                cudaStream_t s) {
+  ClusterStepArgs a;
+  a.q = static_cast<const __half*>(q);
+  a.k_new = static_cast<const __half*>(k_new);
+  a.v_new = static_cast<const __half*>(v_new);
+  a.o = static_cast<__half*>(o);
+  a.kv = static_cast<__half*>(p->kv);
+  a.kv_indices = kv_indices;
+  a.n_pages = N;
+  a.last_len = last_len;
+  a.kv_cap = p->kv_cap;
+  a.meta = static_cast<__half*>(p->meta);
+  a.meta_indices = meta_indices;
+  a.meta_cap = p->meta_cap;
+  a.vlog = static_cast<__half*>(p->vlog);
+  a.H = p->H;
+  a.P = p->P;
+  a.k_slots = k;
+  a.sink = p->sink;
+  a.mode = p->mode;
+  a.two_rsqrt_d = 2.f / std::sqrt(static_cast<float>(p->D));
+  a.scale_log2 = (1.f / std::sqrt(static_cast<float>(p->D))) * 1.4426950408889634f;
+  a.selected_out = selected_out;
+  a.sel_cols = k_pages;
+  a.err = dev_error_ptr();
+  return launch_cluster_step(a, p->kv_sw, p->meta_map, p->D, p->cp, s);
+}
+
+int run_chain(const aoakv_step_plan_s* p, const void* q, const void* k_new, const void* v_new,
+              void* o, const int32_t* kv_indices, int N, int last_len,
+              const int32_t* meta_indices, int32_t* selected_out, void* workspace,
+              size_t workspace_bytes, int k_pages, int k, cudaStream_t s) {
+  const int H = p->H, D = p->D, P = p->P;
+  const bool sparse = N > k && k > 1;  // k == 1 keeps only the last page: nothing to score
+  AOAKV_CHECK_ARG(!sparse || N - 1 <= kTopkMaxN, "step: more than 49153 pages");
+  const StepWs lay = step_ws_layout(H, D, N, k_pages);
+  AOAKV_CHECK_ARG(workspace != nullptr, "step: workspace is NULL");
+  if (workspace_bytes < lay.total)
+    return set_error(AOAKV_ERR_WORKSPACE,
+                     "step: workspace smaller than aoakv_step_workspace_size(...) = " +
+                         std::to_string(lay.total));
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const int n_meta = (N + P - 1) / P;
+  int rc = aoakv_append_kv_cache_decode(k_new, v_new, p->kv, kv_indices, N, last_len, p->kv_cap,
+                                        p->meta, meta_indices, n_meta, (N - 1) % P + 1,
+                                        p->meta_cap, p->vlog, H, D, P, AOAKV_LAYOUT_NHD, s);
+  if (rc) return rc;
+  DecodeArgs da = {};
+  da.q = static_cast<const __half*>(q);
+  da.o = static_cast<__half*>(o);
+  da.last_len = last_len;
+  da.last_page_ptr = kv_indices + (N - 1);
+  da.H = H;
+  da.P = P;
+  da.kv_cap = p->kv_cap;
+  da.scale_log2 = (1.f / std::sqrt(static_cast<float>(D))) * 1.4426950408889634f;
+  da.err = dev_error_ptr();
+  int32_t* sel_idx = reinterpret_cast<int32_t*>(ws + lay.idx_off);
+  if (sparse) {
+    EstimateArgs ea;
+    ea.q = static_cast<const __half*>(q);
+    ea.meta = static_cast<const __half*>(p->meta);
+    ea.meta_indices = meta_indices;
+    ea.kv_indices = kv_indices;
+    ea.vlog = static_cast<const __half*>(p->vlog);
+    ea.out = ws + lay.scores_off;
+    ea.out_stride = N;
+    ea.out_f32 = 1;
+    ea.n_score = N - 1;
+    ea.H = H;
+    ea.P = P;
+    ea.meta_cap = p->meta_cap;
+    ea.kv_cap = p->kv_cap;
+    ea.mode = p->mode;
+    ea.two_rsqrt_d = 2.f / std::sqrt(static_cast<float>(D));
+    ea.err = da.err;
+    rc = launch_estimate(ea, D, s);
+    if (rc) return rc;
+    TopkArgs ta;
+    ta.scores = ws + lay.scores_off;
+    ta.s_stride = N;
+    ta.in_idx = kv_indices;
+    ta.in_stride = 0;
+    ta.out_vals = nullptr;
+    ta.ov_stride = 0;
+    ta.out_idx = sel_idx;
+    ta.oi_stride = k - 1;
+    ta.f32 = 1;
+    ta.n = N - 1;
+    ta.k = k - 1;
+    ta.sink = p->sink;
+    rc = launch_topk(ta, H, s, true);
+    if (rc) return rc;
+    da.indices = sel_idx;
+    da.idx_stride = k - 1;
+    da.n_sel = k - 1;
+  } else {
+    da.indices = kv_indices;
+    da.idx_stride = 0;
+    da.n_sel = N > k ? 0 : N - 1;  // k == 1: last page only; else every page
   }
-  if (fused_supported(H, D, P, N - 1, k - 1, &c.grid, &c.smem, &c.chunk, &c.n_chunks,
-                      max_grid))
-    c.impl = StepImpl::kFused;
-  return c;
+  const DecodePlan pl = plan_decode(H, da.n_sel + 1, D, P);
+  da.chunk_pages = pl.chunk_pages;
+  da.n_chunks = pl.n_chunks;
+  carve_decode_ws(ws + lay.dec_off, H, D, da.n_sel + 1, da);
+  rc = launch_decode(da, p->kv_plain, D, pl, s, sparse);
+  if (rc) return rc;
+  if (selected_out) {
+    fill_selected_kernel<<<H, 128, 0, s>>>(selected_out, k_pages, da.indices, da.idx_stride,
+                                           da.n_sel, da.last_page_ptr, H);
+    AOAKV_CUDA_TRY(cudaGetLastError(), "fill_selected launch");
+  }
+  return AOAKV_OK;
+}
+
+int plan_run(const aoakv_step_plan_s* p, const void* q, const void* k_new, const void* v_new,
+             void* o, const int32_t* kv_indices, int N, int last_len,
+             const int32_t* meta_indices, int32_t* selected_out, void* workspace,
+             size_t workspace_bytes, void* stream) {
+  AOAKV_NVTX("aoakv_decode_step");
+  AOAKV_CHECK_ARG(q && k_new && v_new && o && kv_indices && meta_indices,
+                  "step: NULL pointer argument");
+  AOAKV_CHECK_ARG(N >= 1 && N <= p->max_pages,
+                  "step: num_kv_pages must be in [1, the plan's max_pages]");
+  AOAKV_CHECK_ARG(last_len >= 1 && last_len <= p->P,
+                  "step: kv_last_page_len must be in [1, page_size]");
+  int k_pages, k;
+  step_budget(N, p->budget, p->sink, &k_pages, &k);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p->cluster_ok)
+    return run_cluster(p, q, k_new, v_new, o, kv_indices, N, last_len, meta_indices,
+                       selected_out, k_pages, k, s);
+  return run_chain(p, q, k_new, v_new, o, kv_indices, N, last_len, meta_indices, selected_out,
+                   workspace, workspace_bytes, k_pages, k, s);
+}
+
+// Kernels one step launches: 1 (cluster), else the chain's count.
+int plan_kernels(const aoakv_step_plan_s* p, int N, bool want_selected) {
+  if (p->cluster_ok) return 1;
+  int k_pages, k;
+  step_budget(N, p->budget, p->sink, &k_pages, &k);
+  const bool sparse = N > k && k > 1;
+  return (sparse ? 4 : 2) + (want_selected ? 1 : 0);
 }
 
 }  // namespace
@@ -114,6 +304,53 @@ extern "C" int aoakv_step_workspace_size(int32_t num_heads, int32_t head_dim,
   return AOAKV_OK;
 }
 
+extern "C" int aoakv_step_plan_create(aoakv_step_plan* plan_out, void* kv_data,
+                                      int32_t kv_capacity_pages, void* metadata_data,
+                                      int32_t metadata_capacity_pages, void* v_log_norm,
+                                      int32_t num_heads, int32_t head_dim, int32_t page_size,
+                                      int32_t page_budget, int32_t score_mode,
+                                      int32_t sink_first_page, int32_t max_pages,
+                                      int32_t max_ctas, int32_t flags) {
+  AOAKV_CHECK_ARG(plan_out != nullptr, "step plan: plan_out is NULL");
+  *plan_out = nullptr;
+  aoakv_step_plan_s* p = new (std::nothrow) aoakv_step_plan_s();
+  if (!p) return set_error(AOAKV_ERR_INVALID_ARG, "step plan: out of host memory");
+  const int rc = plan_init(p, kv_data, kv_capacity_pages, metadata_data, metadata_capacity_pages,
+                           v_log_norm, num_heads, head_dim, page_size, page_budget, score_mode,
+                           sink_first_page, max_pages, max_ctas, flags);
+  if (rc) {
+    delete p;
+    return rc;
+  }
+  *plan_out = p;
+  return AOAKV_OK;
+}
+
+extern "C" int aoakv_step_plan_run(aoakv_step_plan plan, const void* q, const void* k_new,
+                                   const void* v_new, void* o, const int32_t* kv_indices,
+                                   int32_t num_kv_pages, int32_t kv_last_page_len,
+                                   const int32_t* metadata_indices, int32_t* selected_out,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  AOAKV_CHECK_ARG(plan != nullptr, "step plan: plan is NULL");
+  return plan_run(plan, q, k_new, v_new, o, kv_indices, num_kv_pages, kv_last_page_len,
+                  metadata_indices, selected_out, workspace, workspace_bytes, stream);
+}
+
+extern "C" int aoakv_step_plan_info(aoakv_step_plan plan, int32_t num_kv_pages,
+                                    int32_t want_selected, int32_t* kernels_out,
+                                    int32_t* cluster_out) {
+  AOAKV_CHECK_ARG(plan != nullptr, "step plan: plan is NULL");
+  AOAKV_CHECK_ARG(num_kv_pages >= 1, "step plan: num_kv_pages must be >= 1");
+  if (kernels_out) *kernels_out = plan_kernels(plan, num_kv_pages, want_selected != 0);
+  if (cluster_out) *cluster_out = plan->cluster_ok ? plan->cp.cluster : 0;
+  return AOAKV_OK;
+}
+
+extern "C" int aoakv_step_plan_destroy(aoakv_step_plan plan) {
+  delete plan;
+  return AOAKV_OK;
+}
+
 extern "C" int aoakv_step_launches(int32_t num_heads, int32_t head_dim, int32_t page_size,
                                    int32_t num_kv_pages, int32_t page_budget,
                                    int32_t sink_first_page, int32_t want_selected,
@@ -122,254 +359,37 @@ extern "C" int aoakv_step_launches(int32_t num_heads, int32_t head_dim, int32_t 
   AOAKV_CHECK_ARG(num_heads >= 1 && (head_dim == 64 || head_dim == 128) && page_size >= 1 &&
                       num_kv_pages >= 1 && page_budget >= 1,
                   "step_launches: bad arguments");
-  const int N = num_kv_pages;
-  const int k_pages = sink_first_page ? (page_budget < 3 ? 3 : page_budget) : page_budget;
-  const int k = k_pages < N ? k_pages : N;
-  const bool sparse = N > k && k > 1;
-  int n = sparse ? 4 : 2;
-  const StepImpl im = choose_step(num_heads, head_dim, page_size, N, k).impl;
-  if (im == StepImpl::kCluster || (sparse && im != StepImpl::kChain)) n = 1;
-  if (want_selected && n > 1) ++n;
-  *kernels_out = n;
+  aoakv_step_plan_s p = {};
+  p.budget = page_budget;
+  p.sink = sink_first_page != 0;
+  int k_pages, k;
+  step_budget(num_kv_pages, page_budget, p.sink, &k_pages, &k);
+  p.cluster_ok = cluster_step_plan(num_heads, head_dim, page_size, num_kv_pages, k_pages, 0,
+                                   &p.cp) != 0;
+  *kernels_out = plan_kernels(&p, num_kv_pages, want_selected != 0);
   return AOAKV_OK;
 }
 
 namespace {
 
-int decode_step_impl(
-    const void* q, const void* k_new, const void* v_new, void* o, void* kv_data,
-    const int32_t* kv_indices, int32_t num_kv_pages, int32_t kv_last_page_len,
-    int32_t kv_capacity_pages, void* metadata_data, const int32_t* metadata_indices,
-    int32_t metadata_capacity_pages, void* v_log_norm, int32_t num_heads,
-    int32_t head_dim, int32_t page_size, int32_t page_budget, int32_t score_mode,
-    int32_t sink_first_page, int32_t* selected_out, void* workspace,
-    size_t workspace_bytes, void* stream, int max_ctas) {
-  AOAKV_NVTX("aoakv_decode_step");
-  AOAKV_CHECK_ARG(q && k_new && v_new && o && kv_data && kv_indices && metadata_data &&
-                      metadata_indices && v_log_norm,
-                  "step: NULL pointer argument");
-  int rc = check_decode_shape(num_heads, head_dim, page_size, kv_capacity_pages,
-                              AOAKV_LAYOUT_NHD);
-  if (rc) return rc;
-  AOAKV_CHECK_ARG(page_budget >= 1, "step: page_budget must be >= 1");
-  AOAKV_CHECK_ARG(score_mode == AOAKV_SCORE_QUEST || score_mode == AOAKV_SCORE_AOAKV,
-                  "step: score_mode must be QUEST or AOAKV");
+// The stateless entry points: a plan on the stack for one call.
+int decode_step_once(const void* q, const void* k_new, const void* v_new, void* o,
+                     void* kv_data, const int32_t* kv_indices, int32_t num_kv_pages,
+                     int32_t kv_last_page_len, int32_t kv_capacity_pages, void* metadata_data,
+                     const int32_t* metadata_indices, int32_t metadata_capacity_pages,
+                     void* v_log_norm, int32_t num_heads, int32_t head_dim, int32_t page_size,
+                     int32_t page_budget, int32_t score_mode, int32_t sink_first_page,
+                     int32_t* selected_out, void* workspace, size_t workspace_bytes,
+                     int32_t max_ctas, void* stream) {
   AOAKV_CHECK_ARG(num_kv_pages >= 1 && num_kv_pages <= kv_capacity_pages,
                   "step: num_kv_pages must be in [1, kv_capacity_pages]");
-  const int N = num_kv_pages, P = page_size, H = num_heads, D = head_dim;
-  const int n_meta = (N + P - 1) / P;
-  const int meta_last = (N - 1) % P + 1;
-  const int k_pages = sink_first_page ? (page_budget < 3 ? 3 : page_budget) : page_budget;
-  const int k = k_pages < N ? k_pages : N;
-  // k == 1 keeps only the last page: nothing to score.
-  const bool sparse = N > k && k > 1;
-  AOAKV_CHECK_ARG(!sparse || N - 1 <= kTopkMaxN, "step: more than 49153 pages");
-  const StepWs lay = step_ws_layout(H, D, N, k_pages);
-  AOAKV_CHECK_ARG(workspace != nullptr, "step: workspace is NULL");
-  if (workspace_bytes < lay.total)
-    return set_error(AOAKV_ERR_WORKSPACE,
-                     "step: workspace smaller than aoakv_step_workspace_size(...) = " +
-                         std::to_string(lay.total));
-  AOAKV_CHECK_ARG(kv_last_page_len >= 1 && kv_last_page_len <= P,
-                  "step: kv_last_page_len must be in [1, page_size]");
-  AOAKV_CHECK_ARG(metadata_capacity_pages >= n_meta,
-                  "step: metadata capacity below ceil(num_kv_pages / page_size)");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-
-  const StepChoice sc = choose_step(H, D, P, N, k, max_ctas);
-  if (sc.impl == StepImpl::kCluster) {
-    ClusterStepArgs a = {};
-    a.q = static_cast<const __half*>(q);
-    a.k_new = static_cast<const __half*>(k_new);
-    a.v_new = static_cast<const __half*>(v_new);
-    a.o = static_cast<__half*>(o);
-    a.kv = static_cast<__half*>(kv_data);
-    a.kv_indices = kv_indices;
-    a.n_pages = N;
-    a.last_len = kv_last_page_len;
-    a.kv_cap = kv_capacity_pages;
-    a.meta = static_cast<__half*>(metadata_data);
-    a.meta_indices = metadata_indices;
-    a.meta_cap = metadata_capacity_pages;
-    a.vlog = static_cast<__half*>(v_log_norm);
-    a.H = H;
-    a.P = P;
-    a.k_slots = k;
-    a.sink = sink_first_page != 0;
-    a.mode = score_mode;
-    a.two_rsqrt_d = 2.f / std::sqrt(static_cast<float>(D));
-    a.scale_log2 = (1.f / std::sqrt(static_cast<float>(D))) * 1.4426950408889634f;
-    a.selected_out = selected_out;
-    a.sel_cols = k_pages;
-    a.err = dev_error_ptr();
-    CUtensorMap kmap, mmap;
-    rc = make_kv_tmap_sw128(&kmap, kv_data, H, D, P, kv_capacity_pages);
-    if (rc) return rc;
-    rc = make_kv_tmap(&mmap, metadata_data, H, D, P, metadata_capacity_pages);
-    if (rc) return rc;
-    return launch_cluster_step(a, kmap, mmap, D, sc.cp, s);
-  }
-  if (sparse) {
-    const int grid = sc.grid, chunk = sc.chunk, n_chunks = sc.n_chunks;
-    const size_t smem = sc.smem;
-    if (sc.impl != StepImpl::kChain) {
-      FusedArgs f = {};
-      f.k_new = static_cast<const __half*>(k_new);
-      f.v_new = static_cast<const __half*>(v_new);
-      f.kv = static_cast<__half*>(kv_data);
-      f.kv_indices = kv_indices;
-      f.n_pages = N;
-      f.last_len = kv_last_page_len;
-      f.kv_cap = kv_capacity_pages;
-      f.meta = static_cast<__half*>(metadata_data);
-      f.meta_indices = metadata_indices;
-      f.meta_cap = metadata_capacity_pages;
-      f.vlog = static_cast<__half*>(v_log_norm);
-      f.H = H;
-      f.P = P;
-      f.k_sel = k - 1;
-      f.sink = sink_first_page != 0;
-      f.sel = reinterpret_cast<int32_t*>(ws + lay.idx_off);
-      f.sync = reinterpret_cast<uint32_t*>(ws + lay.sync_off);
-      f.selected_out = selected_out;
-      f.sel_cols = k_pages;
-      f.err = dev_error_ptr();
-      const int per_cta = (N - 1 + grid - 1) / grid;
-      const char* est_impl = std::getenv("AOAKV_EST_IMPL");  // "regs": A/B comparisons
-      f.est_tma = H * (D / 8) == kFusedThreads && H % 8 == 0 && per_cta <= kEstMaxRange &&
-                  reinterpret_cast<uintptr_t>(metadata_data) % 16 == 0 &&
-                  (score_mode != AOAKV_SCORE_AOAKV ||
-                   reinterpret_cast<uintptr_t>(v_log_norm) % 16 == 0) &&
-                  !(est_impl && std::strcmp(est_impl, "regs") == 0);
-      EstimateArgs& ea = f.est;
-      ea.q = static_cast<const __half*>(q);
-      ea.meta = f.meta;
-      ea.meta_indices = metadata_indices;
-      ea.kv_indices = kv_indices;
-      ea.vlog = f.vlog;
-      ea.out = ws + lay.scores_off;
-      ea.out_stride = N;
-      ea.out_f32 = 1;
-      ea.n_score = N - 1;
-      ea.H = H;
-      ea.P = P;
-      ea.meta_cap = metadata_capacity_pages;
-      ea.kv_cap = kv_capacity_pages;
-      ea.mode = score_mode;
-      ea.two_rsqrt_d = 2.f / std::sqrt(static_cast<float>(D));
-      ea.err = f.err;
-      DecodeArgs& dd = f.dec;
-      dd.q = ea.q;
-      dd.o = static_cast<__half*>(o);
-      dd.indices = f.sel;
-      dd.idx_stride = k - 1;
-      dd.n_sel = k - 1;
-      dd.last_len = kv_last_page_len;
-      dd.last_page_ptr = kv_indices + (N - 1);
-      dd.H = H;
-      dd.P = P;
-      dd.kv_cap = kv_capacity_pages;
-      dd.chunk_pages = chunk;
-      dd.n_chunks = n_chunks;
-      dd.scale_log2 = (1.f / std::sqrt(static_cast<float>(D))) * 1.4426950408889634f;
-      dd.err = f.err;
-      carve_decode_ws(ws + lay.dec_off, H, D, k, dd);
-      CUtensorMap tmap, mtmap;
-      rc = make_kv_tmap(&tmap, kv_data, H, D, P, kv_capacity_pages);
-      if (rc) return rc;
-      if (sc.impl == StepImpl::kPipe) {
-        rc = make_meta_tmap(&mtmap, metadata_data, H, D, P, metadata_capacity_pages,
-                            pipe_group_heads());
-        if (rc) return rc;
-        return launch_pipe(tmap, mtmap, f, D, grid, smem, s);
-      }
-      if (f.est_tma) {
-        rc = make_meta_tmap(&mtmap, metadata_data, H, D, P, metadata_capacity_pages, H);
-        if (rc) return rc;
-      } else {
-        mtmap = tmap;  // unused
-      }
-      return launch_fused(tmap, mtmap, f, D, grid, smem, s);
-    }
-  }
-
-  rc = aoakv_append_kv_cache_decode(k_new, v_new, kv_data, kv_indices, N,
-                                    kv_last_page_len, kv_capacity_pages, metadata_data,
-                                    metadata_indices, n_meta, meta_last,
-                                    metadata_capacity_pages, v_log_norm, H, D, P,
-                                    AOAKV_LAYOUT_NHD, stream);
+  aoakv_step_plan_s p = {};
+  const int rc = plan_init(&p, kv_data, kv_capacity_pages, metadata_data,
+                           metadata_capacity_pages, v_log_norm, num_heads, head_dim, page_size,
+                           page_budget, score_mode, sink_first_page, num_kv_pages, max_ctas, 0);
   if (rc) return rc;
-
-  DecodeArgs da = {};
-  da.q = static_cast<const __half*>(q);
-  da.o = static_cast<__half*>(o);
-  da.last_len = kv_last_page_len;
-  da.last_page_ptr = kv_indices + (N - 1);
-  da.H = H;
-  da.P = P;
-  da.kv_cap = kv_capacity_pages;
-  da.scale_log2 = (1.f / std::sqrt(static_cast<float>(D))) * 1.4426950408889634f;
-  da.err = dev_error_ptr();
-  int32_t* sel_idx = reinterpret_cast<int32_t*>(ws + lay.idx_off);
-  if (sparse) {
-    EstimateArgs ea;
-    ea.q = static_cast<const __half*>(q);
-    ea.meta = static_cast<const __half*>(metadata_data);
-    ea.meta_indices = metadata_indices;
-    ea.kv_indices = kv_indices;
-    ea.vlog = static_cast<const __half*>(v_log_norm);
-    ea.out = ws + lay.scores_off;
-    ea.out_stride = N;
-    ea.out_f32 = 1;
-    ea.n_score = N - 1;
-    ea.H = H;
-    ea.P = P;
-    ea.meta_cap = metadata_capacity_pages;
-    ea.kv_cap = kv_capacity_pages;
-    ea.mode = score_mode;
-    ea.two_rsqrt_d = 2.f / std::sqrt(static_cast<float>(D));
-    ea.err = da.err;
-    rc = launch_estimate(ea, D, s);
-    if (rc) return rc;
-    TopkArgs ta;
-    ta.scores = ws + lay.scores_off;
-    ta.s_stride = N;
-    ta.in_idx = kv_indices;
-    ta.in_stride = 0;
-    ta.out_vals = nullptr;
-    ta.ov_stride = 0;
-    ta.out_idx = sel_idx;
-    ta.oi_stride = k - 1;
-    ta.f32 = 1;
-    ta.n = N - 1;
-    ta.k = k - 1;
-    ta.sink = sink_first_page != 0;
-    rc = launch_topk(ta, H, s, true);
-    if (rc) return rc;
-    da.indices = sel_idx;
-    da.idx_stride = k - 1;
-    da.n_sel = k - 1;
-  } else {
-    da.indices = kv_indices;
-    da.idx_stride = 0;
-    da.n_sel = N > k ? 0 : N - 1;  // k == 1: last page only; else every page
-  }
-  const DecodePlan pl = plan_decode(H, da.n_sel + 1, D, P);
-  da.chunk_pages = pl.chunk_pages;
-  da.n_chunks = pl.n_chunks;
-  carve_decode_ws(ws + lay.dec_off, H, D, da.n_sel + 1, da);
-  CUtensorMap tmap;
-  rc = make_kv_tmap(&tmap, kv_data, H, D, P, kv_capacity_pages);
-  if (rc) return rc;
-  rc = launch_decode(da, tmap, D, pl, s, sparse);
-  if (rc) return rc;
-  if (selected_out) {
-    fill_selected_kernel<<<H, 128, 0, s>>>(selected_out, k_pages, da.indices,
-                                           da.idx_stride, da.n_sel, da.last_page_ptr, H);
-    AOAKV_CUDA_TRY(cudaGetLastError(), "fill_selected launch");
-  }
-  return AOAKV_OK;
+  return plan_run(&p, q, k_new, v_new, o, kv_indices, num_kv_pages, kv_last_page_len,
+                  metadata_indices, selected_out, workspace, workspace_bytes, stream);
 }
 
 }  // namespace
@@ -382,11 +402,11 @@ extern "C" int aoakv_decode_step(
     int32_t head_dim, int32_t page_size, int32_t page_budget, int32_t score_mode,
     int32_t sink_first_page, int32_t* selected_out, void* workspace,
     size_t workspace_bytes, void* stream) {
-  return decode_step_impl(q, k_new, v_new, o, kv_data, kv_indices, num_kv_pages,
+  return decode_step_once(q, k_new, v_new, o, kv_data, kv_indices, num_kv_pages,
                           kv_last_page_len, kv_capacity_pages, metadata_data, metadata_indices,
                           metadata_capacity_pages, v_log_norm, num_heads, head_dim, page_size,
                           page_budget, score_mode, sink_first_page, selected_out, workspace,
-                          workspace_bytes, stream, 0);
+                          workspace_bytes, 0, stream);
 }
 
 extern "C" int aoakv_decode_step_grid(
@@ -398,9 +418,9 @@ extern "C" int aoakv_decode_step_grid(
     int32_t sink_first_page, int32_t* selected_out, void* workspace,
     size_t workspace_bytes, int32_t max_ctas, void* stream) {
   AOAKV_CHECK_ARG(max_ctas >= 0, "step: max_ctas must be >= 0");
-  return decode_step_impl(q, k_new, v_new, o, kv_data, kv_indices, num_kv_pages,
+  return decode_step_once(q, k_new, v_new, o, kv_data, kv_indices, num_kv_pages,
                           kv_last_page_len, kv_capacity_pages, metadata_data, metadata_indices,
                           metadata_capacity_pages, v_log_norm, num_heads, head_dim, page_size,
                           page_budget, score_mode, sink_first_page, selected_out, workspace,
-                          workspace_bytes, stream, max_ctas);
+                          workspace_bytes, max_ctas, stream);
 }

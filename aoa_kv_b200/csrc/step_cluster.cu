@@ -53,7 +53,6 @@
 
 #include "common.cuh"
 #include "decode.cuh"
-#include "step_append.cuh"
 #include "step_cluster.h"
 
 namespace cg = cooperative_groups;
@@ -1280,14 +1279,15 @@ std::atomic<int> g_cluster_pdl{-1};
 
 }  // namespace
 
-int cluster_step_plan(int H, int D, int P, int max_pages, int max_slots, ClusterPlan* plan) {
+int cluster_step_plan(int H, int D, int P, int max_pages, int max_slots, int max_ctas,
+                      ClusterPlan* plan) {
   if ((D != 64 && D != 128) || P < 1 || P > kCsMaxPage || H < 1 || H > 65535 || max_pages < 1 ||
       max_slots < 1)
     return 0;
   if (max_slots > max_pages) max_slots = max_pages;
-  const int sms = num_sms();
+  const int ctas = max_ctas > 0 ? max_ctas : num_sms();
   int C = 8;
-  while (C > 1 && H * C > sms) C >>= 1;
+  while (C > 1 && H * C > ctas) C >>= 1;
   int n_st = (max_pages - 1 + P - 1) / P;
   if (n_st < 1) n_st = 1;
   auto smem_for = [&](int cl) {

@@ -49,8 +49,10 @@ struct ClusterPlan {
 
 // Returns 1 and the plan when the cluster step can run (H heads of head_dim
 // D, page size P, up to max_pages pages of which up to max_slots are
-// attended); 0 otherwise (the caller uses the multi-kernel chain).
-int cluster_step_plan(int H, int D, int P, int max_pages, int max_slots, ClusterPlan* plan);
+// attended, at most max_ctas CTAs when max_ctas > 0); 0 otherwise (the
+// caller uses the multi-kernel chain).
+int cluster_step_plan(int H, int D, int P, int max_pages, int max_slots, int max_ctas,
+                      ClusterPlan* plan);
 int launch_cluster_step(const ClusterStepArgs& a, const CUtensorMap& kv_map,
                         const CUtensorMap& meta_map, int D, const ClusterPlan& plan,
                         cudaStream_t s);

@@ -31,14 +31,6 @@
 
 #include "topk_bitonic.cuh"
 
-// Development timing hook (a phase stamp); compiled to nothing unless the
-// including file defines it.
-#ifndef AOAKV_TOPK_STAMP
-#define AOAKV_TOPK_STAMP(i) \
-  do {                      \
-  } while (0)
-#endif
-
 namespace aoakv {
 
 constexpr int kHistBins = 4096;
@@ -244,9 +236,7 @@ __device__ __forceinline__ bool topk_row_hist_regs(const TopkArgs& a, int row, H
     if (b[u] >= 0) atomicAdd(&hs.hist[b[u]], 1u);
   }
   __syncthreads();
-  AOAKV_TOPK_STAMP(5);
   hist_find_bin(hs, a.k);
-  AOAKV_TOPK_STAMP(6);
   if (hs.cnt > kHistMaxCand) return false;  // uniform: every thread reads it
   const int bstar = hs.bstar;
   uint32_t m[4], wc = 0;
@@ -275,7 +265,6 @@ __device__ __forceinline__ bool topk_row_hist_regs(const TopkArgs& a, int row, H
     off += __popc(m[u]);
   }
   __syncthreads();
-  AOAKV_TOPK_STAMP(7);
   hist_rank_emit<kL2>(a, row, hs, static_cast<int>(c_all), win, win_lo, win_hi);
   return true;
 }
@@ -377,10 +366,8 @@ __device__ __forceinline__ bool topk_row_hist(const TopkArgs& a, int row, uint8_
     atomicAdd(&hs.hist[bin], 1u);
   }
   __syncthreads();
-  AOAKV_TOPK_STAMP(5);
   // 3. the bin of the k-th largest
   hist_find_bin(hs, k);
-  AOAKV_TOPK_STAMP(6);
   if (hs.cnt > kHistMaxCand) return false;  // uniform: every thread reads it
   // 4. gather the candidates with their ids: warp w owns positions
   // w*32 + it*nt + lane; slots come from a prefix over per-warp counts (no
@@ -414,7 +401,6 @@ __device__ __forceinline__ bool topk_row_hist(const TopkArgs& a, int row, uint8_
     off += __popc(m);
   }
   __syncthreads();
-  AOAKV_TOPK_STAMP(7);
   // 5. rank
   hist_rank_emit<kL2>(a, row, hs, static_cast<int>(c_all), win, win_lo, win_hi);
   return true;

@@ -280,25 +280,64 @@ AOAKV_API int aoakv_map_pages(const int32_t* global_ids, int64_t count, int32_t 
  *       k = min(max(3, page_budget), N); page 0, top-(k-2) of 1..N-2, N-1.
  *   If N <= k every page is attended and no scoring runs.
  * selected_out (optional, [num_heads, B] with B = page_budget, or
- * max(3, page_budget) with the sink) receives the attended page ids per head
- * in slot order (last page after the selected ones); unused slots are -1.
- * The workspace is sized by aoakv_step_workspace_size, zero-filled once by
- * the caller, and kept zeroed by every call. */
+ * max(3, page_budget) with the sink) receives the attended page ids per head:
+ * slot 0 the sink page (with the sink), then the selected pages (descending
+ * score when one kernel runs the step, ascending page otherwise), slot k-1
+ * the last page; unused slots are -1.
+ * The workspace (used only when the step runs as a chain of kernels, see
+ * aoakv_step_plan_info) is sized by aoakv_step_workspace_size, zero-filled
+ * once by the caller, and kept zeroed by every call. */
 AOAKV_API int aoakv_step_workspace_size(int32_t num_heads, int32_t head_dim,
                               int32_t max_pages, int32_t max_page_budget,
                               size_t* bytes);
 
-/* Reports how aoakv_decode_step will run this problem on the current device:
- * *kernels_out = 1 (one fused cooperative kernel: append, scoring, top-k and
- * decode), 2 (append + decode, nothing to score), 4 (append, estimate,
- * top-k, decode launched back to back with programmatic dependent launch;
- * AOAKV_STEP_IMPL=chain forces it), plus 1 when selected_out is requested on
- * the multi-kernel paths. */
+/* The step planned once per layer — replaces BatchDecodeHandler's
+ * BeginForward / Forward / EndForward (decode_handler.cuh:73-136,
+ * approx_attn.cu:27-151), which re-plan with a device synchronisation and an
+ * allocation on every step. aoakv_step_plan_create binds one layer's
+ * kv_data / metadata_data / v_log_norm and the step's parameters, chooses how
+ * the step runs on the current device (one launch of thread-block clusters
+ * when head_dim is 64 or 128 and page_size <= 16, else the four-kernel chain)
+ * and encodes its tensor maps; it allocates host memory only.
+ *   max_pages  the largest num_kv_pages the plan will run (0 = capacity);
+ *              shared memory is sized for it.
+ *   max_ctas   0 = the whole GPU, else at most this many CTAs per step (so
+ *              several requests' steps can share the GPU).
+ *   flags      AOAKV_PLAN_CHAIN forces the four-kernel chain.
+ * aoakv_step_plan_run runs one step (arguments as aoakv_decode_step) on the
+ * device the plan was created on; it does not synchronise, allocate or
+ * re-plan. Plans are immutable: one plan may serve several streams. */
+enum { AOAKV_PLAN_CHAIN = 1 };
+typedef struct aoakv_step_plan_s* aoakv_step_plan;
+
+AOAKV_API int aoakv_step_plan_create(aoakv_step_plan* plan_out, void* kv_data,
+                                     int32_t kv_capacity_pages, void* metadata_data,
+                                     int32_t metadata_capacity_pages, void* v_log_norm,
+                                     int32_t num_heads, int32_t head_dim, int32_t page_size,
+                                     int32_t page_budget, int32_t score_mode,
+                                     int32_t sink_first_page, int32_t max_pages,
+                                     int32_t max_ctas, int32_t flags);
+AOAKV_API int aoakv_step_plan_run(aoakv_step_plan plan, const void* q, const void* k_new,
+                                  const void* v_new, void* o, const int32_t* kv_indices,
+                                  int32_t num_kv_pages, int32_t kv_last_page_len,
+                                  const int32_t* metadata_indices, int32_t* selected_out,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+/* *kernels_out: launches per step for num_kv_pages pages (1 = one cluster
+ * launch; 2 append + decode or 4 append, estimate, top-k, decode for the
+ * chain, plus 1 with selected_out); *cluster_out: CTAs per head of the
+ * cluster launch (0 = chain). Either may be NULL. */
+AOAKV_API int aoakv_step_plan_info(aoakv_step_plan plan, int32_t num_kv_pages,
+                                   int32_t want_selected, int32_t* kernels_out,
+                                   int32_t* cluster_out);
+AOAKV_API int aoakv_step_plan_destroy(aoakv_step_plan plan);
+
+/* aoakv_step_plan_info for a problem without a plan (the default plan). */
 AOAKV_API int aoakv_step_launches(int32_t num_heads, int32_t head_dim, int32_t page_size,
                                   int32_t num_kv_pages, int32_t page_budget,
                                   int32_t sink_first_page, int32_t want_selected,
                                   int32_t* kernels_out);
 
+/* One step without a plan (plans it on every call). */
 AOAKV_API int aoakv_decode_step(
     const void* q, const void* k_new, const void* v_new, void* o,
     void* kv_data, const int32_t* kv_indices, int32_t num_kv_pages,
@@ -311,11 +350,9 @@ AOAKV_API int aoakv_decode_step(
     int32_t* selected_out, void* workspace, size_t workspace_bytes,
     void* stream);
 
-/* aoakv_decode_step with the fused kernel's grid capped at max_ctas CTAs
- * (0 = the whole GPU; no reference counterpart). A capped step leaves the
- * rest of the GPU free, so the steps of several independent requests can
- * run concurrently on separate streams (batched decode); results are the
- * same as with the whole GPU. */
+/* aoakv_decode_step on at most max_ctas CTAs (0 = the whole GPU; no
+ * reference counterpart): several independent requests' steps can run
+ * concurrently on separate streams; results are the same. */
 AOAKV_API int aoakv_decode_step_grid(
     const void* q, const void* k_new, const void* v_new, void* o, void* kv_data,
     const int32_t* kv_indices, int32_t num_kv_pages, int32_t kv_last_page_len,

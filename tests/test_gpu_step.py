@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from aoa_kv_b200 import _lib
+from aoa_kv_b200 import StepPlan, _lib
 from gen import gen_qkv
 from gpu_util import GpuLayer, ptr, stream
 from helpers import selection_mismatch
@@ -21,7 +21,9 @@ from oracle import sim
 pytestmark = pytest.mark.gpu
 
 
-def run_step(lay, q, k, v, n, last, budget, mode, sink):
+def run_step(lay, q, k, v, n, last, budget, mode, sink, impl=None):
+    """One step through aoakv_decode_step, or through a StepPlan when impl
+    is "cluster" (the default plan) or "chain" (AOAKV_PLAN_CHAIN)."""
     H, D, P = lay.H, lay.D, lay.P
     cols = max(3, budget) if sink else budget
     ws_n = _lib.size_query("aoakv_step_workspace_size", H, D, lay.cap, cols)
@@ -29,10 +31,18 @@ def run_step(lay, q, k, v, n, last, budget, mode, sink):
     sel = torch.full((H, cols), -9, dtype=torch.int32, device="cuda")
     o = torch.empty(H, D, dtype=torch.float16, device="cuda")
     qd, kd, vd = (torch.from_numpy(x).cuda() for x in (q, k, v))
-    _lib.call("aoakv_decode_step", ptr(qd), ptr(kd), ptr(vd), ptr(o), ptr(lay.kv), ptr(lay.kv_idx),
-              n, last, lay.cap, ptr(lay.meta), ptr(lay.meta_idx), lay.mcap, ptr(lay.vlog), H, D, P,
-              budget, _lib.SCORE_AOAKV if mode == "aoakv" else _lib.SCORE_QUEST, int(sink),
-              ptr(sel), ptr(ws), ws_n, stream())
+    score = _lib.SCORE_AOAKV if mode == "aoakv" else _lib.SCORE_QUEST
+    if impl is None:
+        _lib.call("aoakv_decode_step", ptr(qd), ptr(kd), ptr(vd), ptr(o), ptr(lay.kv),
+                  ptr(lay.kv_idx), n, last, lay.cap, ptr(lay.meta), ptr(lay.meta_idx), lay.mcap,
+                  ptr(lay.vlog), H, D, P, budget, score, int(sink), ptr(sel), ptr(ws), ws_n,
+                  stream())
+    else:
+        plan = StepPlan(lay.kv, lay.cap, lay.meta, lay.mcap, lay.vlog, H, D, P, budget, score,
+                        sink, chain=impl == "chain")
+        kernels, cluster = plan.info(n)
+        assert (cluster == 0) if impl == "chain" else (kernels == 1 and cluster >= 1)
+        plan.run(qd, kd, vd, o, lay.kv_idx, n, last, lay.meta_idx, sel, ws, ws_n, stream())
     torch.cuda.synchronize()
     return o.float().cpu().numpy(), sel.cpu().numpy()
 
@@ -109,12 +119,10 @@ def test_step_sink_matches_reference_simulation(cuda, method, S, B, dist):
         assert np.abs(got_o - out_s).max() < 2e-3
 
 
-@pytest.fixture(params=["cluster", "pipe", "fused", "chain"])
-def step_impl(request, monkeypatch):
-    """Runs a test with the cluster kernel (the default), the cooperative
-    fused kernel, the pipelined two-role kernel and the four-launch chain
-    (AOAKV_STEP_IMPL is read by the library on every call)."""
-    monkeypatch.setenv("AOAKV_STEP_IMPL", request.param)
+@pytest.fixture(params=["cluster", "chain"])
+def step_impl(request):
+    """Runs a test through a StepPlan: the one cluster launch (the default)
+    and the four-kernel chain (AOAKV_PLAN_CHAIN)."""
     return request.param
 
 
@@ -129,7 +137,7 @@ def test_step_impls_agree_with_oracle(cuda, step_impl, mode, sink, S, budget):
     lay.fill(K[:-1], V[:-1])
     torch.cuda.synchronize()
     ref = lay.snapshot()
-    got_o, got_sel = run_step(lay, q, K[-1], V[-1], n, last, budget, mode, sink)
+    got_o, got_sel = run_step(lay, q, K[-1], V[-1], n, last, budget, mode, sink, step_impl)
     kp = max(3, budget) if sink else budget
     k = min(kp, n)
     want_o, want_sel = kt.step(q, K[-1], V[-1], ref, lay.kv_idx_np, lay.meta_idx_np, n, last,
@@ -155,7 +163,7 @@ def test_step_impls_agree_with_oracle(cuda, step_impl, mode, sink, S, budget):
 
 
 def test_step_captured_in_cuda_graph(cuda, step_impl):
-    """The step (cooperative fused kernel or PDL chain) captures into a CUDA
+    """The planned step (cluster launch or PDL chain) captures into a CUDA
     graph and replays with the same result; the workspace stays clean."""
     H, D, P, B = 32, 128, 16, 64
     S = 8192
@@ -168,11 +176,12 @@ def test_step_captured_in_cuda_graph(cuda, step_impl):
     o = torch.empty(H, D, dtype=torch.float16, device="cuda")
     qd, kd, vd = (torch.from_numpy(x).cuda() for x in (q, K[-1], V[-1]))
 
+    plan = StepPlan(lay.kv, lay.cap, lay.meta, lay.mcap, lay.vlog, H, D, P, B, _lib.SCORE_AOAKV,
+                    False, chain=step_impl == "chain")
+
     def call():
-        _lib.call("aoakv_decode_step", ptr(qd), ptr(kd), ptr(vd), ptr(o), ptr(lay.kv),
-                  ptr(lay.kv_idx), n, last, lay.cap, ptr(lay.meta), ptr(lay.meta_idx), lay.mcap,
-                  ptr(lay.vlog), H, D, P, B, _lib.SCORE_AOAKV, 0, None, ptr(ws), ws_n,
-                  torch.cuda.current_stream().cuda_stream)
+        plan.run(qd, kd, vd, o, lay.kv_idx, n, last, lay.meta_idx, None, ws, ws_n,
+                 torch.cuda.current_stream().cuda_stream)
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
         call()
@@ -222,8 +231,8 @@ def test_step_repeated_calls_keep_workspace_clean(cuda):
 
 @pytest.mark.parametrize("max_ctas", [64, 74, 148])
 def test_step_grid_capped_matches_oracle(cuda, max_ctas):
-    """aoakv_decode_step_grid: the fused kernel on a fraction of the GPU (the
-    batched-decode configuration) gives the oracle's selection and output."""
+    """aoakv_decode_step_grid: the step on a fraction of the GPU (the cluster
+    launch with fewer CTAs per head) gives the oracle's selection and output."""
     H, D, P, budget, S, mode = 32, 128, 16, 64, 8192 + 5, "aoakv"
     q, K, V = gen_qkv(S + max_ctas, H, S, D, "outlier")
     n, last = (S + P - 1) // P, (S - 1) % P + 1
