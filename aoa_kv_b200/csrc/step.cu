@@ -144,7 +144,7 @@ int run_cluster(const aoakv_step_plan_s* p, const void* q, const void* k_new, co
                 void* o, const int32_t* kv_indices, int N, int last_len,
                 const int32_t* meta_indices, int32_t* selected_out, int k_pages, int k,
                 cudaStream_t s) {
-  ClusterStepArgs a;
+  ClusterStepArgs a = {};
   a.q = static_cast<const __half*>(q);
   a.k_new = static_cast<const __half*>(k_new);
   a.v_new = static_cast<const __half*>(v_new);
@@ -423,4 +423,70 @@ extern "C" int aoakv_decode_step_grid(
                           metadata_capacity_pages, v_log_norm, num_heads, head_dim, page_size,
                           page_budget, score_mode, sink_first_page, selected_out, workspace,
                           workspace_bytes, max_ctas, stream);
+}
+
+extern "C" int aoakv_decode_step_batched(
+    const void* q, const void* k_new, const void* v_new, void* o, void* kv_data,
+    int32_t kv_capacity_pages, const int32_t* kv_indptr, const int32_t* kv_indices,
+    const int32_t* kv_last_page_len, void* metadata_data, int32_t metadata_capacity_pages,
+    const int32_t* metadata_indptr, const int32_t* metadata_indices, void* v_log_norm,
+    int32_t num_requests, int32_t max_pages, int32_t num_heads, int32_t head_dim,
+    int32_t page_size, int32_t page_budget, int32_t score_mode, int32_t sink_first_page,
+    int32_t* selected_out, void* stream) {
+  AOAKV_NVTX("aoakv_decode_step_batched");
+  AOAKV_CHECK_ARG(q && k_new && v_new && o && kv_data && kv_indptr && kv_indices &&
+                      kv_last_page_len && metadata_data && metadata_indptr && metadata_indices &&
+                      v_log_norm,
+                  "batched step: NULL pointer argument");
+  AOAKV_CHECK_ARG(num_requests >= 1 && num_requests <= 65535,
+                  "batched step: num_requests must be in [1, 65535]");
+  int rc = check_plan_args(num_heads, head_dim, page_size, kv_capacity_pages,
+                           metadata_capacity_pages, page_budget, score_mode);
+  if (rc) return rc;
+  AOAKV_CHECK_ARG(max_pages >= 1 && max_pages <= kv_capacity_pages,
+                  "batched step: max_pages must be in [1, kv_capacity_pages]");
+  const int H = num_heads, D = head_dim, P = page_size;
+  int k_pages, k;
+  step_budget(max_pages, page_budget, sink_first_page != 0, &k_pages, &k);
+  // about one wave of (request, head) clusters: fewer CTAs per head when
+  // there are many requests
+  const int per_req = num_sms() / num_requests;
+  ClusterPlan cp;
+  if (!cluster_step_plan(H, D, P, max_pages, k_pages, per_req > 1 ? per_req : 1, &cp))
+    return set_error(AOAKV_ERR_UNSUPPORTED,
+                     "batched step: needs head_dim 64/128, page_size <= 16 and max_pages that "
+                     "fit the kernel's shared memory");
+  CUtensorMap kv_sw, meta_map;
+  rc = make_kv_tmap_sw128(&kv_sw, kv_data, H, D, P, kv_capacity_pages);
+  if (rc) return rc;
+  rc = make_kv_tmap(&meta_map, metadata_data, H, D, P, metadata_capacity_pages);
+  if (rc) return rc;
+  ClusterStepArgs a = {};
+  a.q = static_cast<const __half*>(q);
+  a.k_new = static_cast<const __half*>(k_new);
+  a.v_new = static_cast<const __half*>(v_new);
+  a.o = static_cast<__half*>(o);
+  a.kv = static_cast<__half*>(kv_data);
+  a.kv_indices = kv_indices;
+  a.kv_cap = kv_capacity_pages;
+  a.meta = static_cast<__half*>(metadata_data);
+  a.meta_indices = metadata_indices;
+  a.meta_cap = metadata_capacity_pages;
+  a.vlog = static_cast<__half*>(v_log_norm);
+  a.H = H;
+  a.P = P;
+  a.sink = sink_first_page != 0;
+  a.mode = score_mode;
+  a.two_rsqrt_d = 2.f / std::sqrt(static_cast<float>(D));
+  a.scale_log2 = (1.f / std::sqrt(static_cast<float>(D))) * 1.4426950408889634f;
+  a.selected_out = selected_out;
+  a.sel_cols = k_pages;
+  a.err = dev_error_ptr();
+  a.kv_indptr = kv_indptr;
+  a.meta_indptr = metadata_indptr;
+  a.last_lens = kv_last_page_len;
+  a.budget = page_budget;
+  a.max_pages = max_pages;
+  return launch_cluster_step(a, kv_sw, meta_map, D, cp, static_cast<cudaStream_t>(stream),
+                             num_requests);
 }

@@ -455,7 +455,7 @@ struct LaneVec<2> {
 template <int D, int C>
 __global__ void __launch_bounds__(kCsThreads, 1)
     cluster_step_kernel(const __grid_constant__ CUtensorMap kv_map,
-                        const __grid_constant__ CUtensorMap meta_map, ClusterStepArgs a,
+                        const __grid_constant__ CUtensorMap meta_map, ClusterStepArgs a_in,
                         CsShape shp) {
   constexpr int CPL = D / 32;           // channels per lane
   constexpr int CAPL = kCsGather / C;   // local candidates one CTA may publish
@@ -476,7 +476,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   const int c = static_cast<int>(cluster.block_rank());
   const int h = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int P = a.P, H = a.H;
+  const int P = a_in.P, H = a_in.H;
   const CsLayout lay = cs_layout(D, P, C, shp.max_local, shp.max_slots);
   uint8_t* slot = smem + lay.ring + warp * cs_slot_bytes(D, P);
   float* sc = reinterpret_cast<float*>(smem + lay.scores);
@@ -513,6 +513,31 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   pdl_wait();
   pdl_launch_dependents();
 
+  ClusterStepArgs a = a_in;
+  if (a_in.kv_indptr) {  // batched: request blockIdx.z of a shared page pool
+    const int r = blockIdx.z;
+    const int p0 = __ldcg(a_in.kv_indptr + r);
+    const int m0 = __ldcg(a_in.meta_indptr + r);
+    a.n_pages = __ldcg(a_in.kv_indptr + r + 1) - p0;
+    a.last_len = __ldcg(a_in.last_lens + r);
+    // every CTA of the cluster reads the same values, so all leave together
+    // (no cluster barrier is pending: the arrival above needs no wait)
+    if (p0 < 0 || m0 < 0 || a.n_pages < 1 || a.n_pages > a_in.max_pages || a.last_len < 1 ||
+        a.last_len > P) {
+      if (tid == 0) raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
+      return;
+    }
+    a.kv_indices = a_in.kv_indices + p0;
+    a.meta_indices = a_in.meta_indices + m0;
+    const int kp = a_in.sink ? max(3, a_in.budget) : a_in.budget;
+    a.k_slots = min(kp, a.n_pages);
+    const size_t qo = static_cast<size_t>(r) * H * D;
+    a.q += qo;
+    a.k_new += qo;
+    a.v_new += qo;
+    a.o += qo;
+    if (a.selected_out) a.selected_out += static_cast<size_t>(r) * H * a_in.sel_cols;
+  }
   const int N = a.n_pages, n = N - 1;
   const int k = a.k_slots;
   const bool sparse = N > k && k > 1;
@@ -1344,10 +1369,10 @@ int cluster_step_plan(int H, int D, int P, int max_pages, int max_slots, int max
 
 int launch_cluster_step(const ClusterStepArgs& a, const CUtensorMap& kv_map,
                         const CUtensorMap& meta_map, int D, const ClusterPlan& plan,
-                        cudaStream_t s) {
+                        cudaStream_t s, int num_requests) {
   const int C = plan.cluster;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(C, a.H);
+  cfg.gridDim = dim3(C, a.H, num_requests);
   cfg.blockDim = dim3(kCsThreads);
   cfg.dynamicSmemBytes = plan.smem;
   cfg.stream = s;

@@ -31,6 +31,15 @@ struct ClusterStepArgs {
   int32_t* selected_out;        // optional [H, sel_cols]
   int sel_cols;
   int* err;
+  // Batched steps (kv_indptr != NULL): request blockIdx.z owns pages
+  // kv_indices[kv_indptr[r] .. kv_indptr[r+1]) and metadata pages from
+  // meta_indptr[r]; its last page holds last_lens[r] tokens; q, k_new, v_new,
+  // o and selected_out advance by one request; k_slots follows from budget.
+  const int32_t* kv_indptr;
+  const int32_t* meta_indptr;
+  const int32_t* last_lens;
+  int budget;
+  int max_pages;                // a request with more pages (or none) is skipped
 };
 
 // Sizes the kernel's shared memory is carved for.
@@ -53,8 +62,9 @@ struct ClusterPlan {
 // caller uses the multi-kernel chain).
 int cluster_step_plan(int H, int D, int P, int max_pages, int max_slots, int max_ctas,
                       ClusterPlan* plan);
+// Launches num_requests x H clusters (num_requests > 1 needs a.kv_indptr).
 int launch_cluster_step(const ClusterStepArgs& a, const CUtensorMap& kv_map,
                         const CUtensorMap& meta_map, int D, const ClusterPlan& plan,
-                        cudaStream_t s);
+                        cudaStream_t s, int num_requests = 1);
 
 }  // namespace aoakv

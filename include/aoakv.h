@@ -362,6 +362,29 @@ AOAKV_API int aoakv_decode_step_grid(
     int32_t sink_first_page, int32_t* selected_out, void* workspace,
     size_t workspace_bytes, int32_t max_ctas, void* stream);
 
+/* Batched decode step (config 4's single launch; no reference counterpart:
+ * the reference hard-wires batch 1, decode_attn.cuh:504-509): the step of
+ * aoakv_decode_step for num_requests requests whose pages live in ONE layer
+ * pool, as one launch over (request, head). Request r's KV pages are
+ * kv_indices[kv_indptr[r] .. kv_indptr[r+1]) (the reference's paged_kv_t
+ * indptr convention, decode_page.cuh:79-352), its metadata pages start at
+ * metadata_indices[metadata_indptr[r]], its last page holds
+ * kv_last_page_len[r] tokens (all device arrays, the new token included).
+ * q, k_new, v_new, o are [num_requests, num_heads, head_dim]; selected_out
+ * (optional) is [num_requests, num_heads, B] as for aoakv_decode_step.
+ * max_pages bounds every request's page count (shared memory is sized for
+ * it); a request with no pages, more than max_pages pages or a last page
+ * length outside [1, page_size] is skipped and AOAKV_DEV_ERR_BAD_PAGE is
+ * recorded. Needs head_dim 64/128 and page_size <= 16; no workspace. */
+AOAKV_API int aoakv_decode_step_batched(
+    const void* q, const void* k_new, const void* v_new, void* o, void* kv_data,
+    int32_t kv_capacity_pages, const int32_t* kv_indptr, const int32_t* kv_indices,
+    const int32_t* kv_last_page_len, void* metadata_data, int32_t metadata_capacity_pages,
+    const int32_t* metadata_indptr, const int32_t* metadata_indices, void* v_log_norm,
+    int32_t num_requests, int32_t max_pages, int32_t num_heads, int32_t head_dim,
+    int32_t page_size, int32_t page_budget, int32_t score_mode, int32_t sink_first_page,
+    int32_t* selected_out, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -195,7 +195,7 @@ def test_step_captured_in_cuda_graph(cuda, step_impl):
         g.replay()
         torch.cuda.synchronize()
         assert torch.equal(o, eager)
-    assert int(ws[:512].view(torch.int32).abs().sum()) == 0
+    assert int(ws[: H * 4].view(torch.int32).abs().sum()) == 0  # the decode tickets re-armed
     assert _lib.device_error() == 0
 
 
