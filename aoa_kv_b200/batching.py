@@ -43,3 +43,46 @@ def balance_requests(weights: list[int], n_gpus: int) -> list[list[int]]:
     for lst in out:
         lst.sort()
     return out
+
+
+def decode_step_batched(q, k_new, v_new, o, kv, kv_indptr, kv_indices, kv_last_page_len, meta,
+                        meta_indptr, meta_indices, v_log_norm, max_pages: int, page_budget: int,
+                        score_mode: str = "aoakv", sink_first_page: bool = False,
+                        selected=None, stream=None):
+    """One decode step of every request whose pages live in one layer pool,
+    as ONE launch over (request, head) (aoakv_decode_step_batched).
+
+    kv [cap, 2, P, H, D] and meta [mcap, 2, P, H, D] fp16 and v_log_norm
+    [cap, H] are the layer's pools; request r's KV pages are
+    kv_indices[kv_indptr[r]:kv_indptr[r+1]] (new token's page included, its
+    fill kv_last_page_len[r]) and its metadata pages start at
+    meta_indices[meta_indptr[r]] (all int32 on the device). q, k_new, v_new,
+    o: [R, H, D] fp16; selected (optional): [R, H, B] int32 with B =
+    page_budget (max(3, page_budget) with the sink)."""
+    import torch
+
+    from . import _lib
+    R, H, D = q.shape
+    cap, _, P = kv.shape[0], kv.shape[1], kv.shape[2]
+    for name, t in (("q", q), ("k_new", k_new), ("v_new", v_new), ("o", o), ("kv", kv),
+                    ("meta", meta), ("v_log_norm", v_log_norm)):
+        if not t.is_cuda or t.dtype != torch.float16 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous fp16 CUDA tensor")
+    for name, t in (("kv_indptr", kv_indptr), ("kv_indices", kv_indices),
+                    ("kv_last_page_len", kv_last_page_len), ("meta_indptr", meta_indptr),
+                    ("meta_indices", meta_indices)):
+        if not t.is_cuda or t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous int32 CUDA tensor")
+    if kv_indptr.numel() != R + 1 or meta_indptr.numel() != R + 1 or \
+            kv_last_page_len.numel() != R:
+        raise ValueError("indptr arrays need num_requests + 1 entries, kv_last_page_len one "
+                         "per request")
+    mode = _lib.SCORE_AOAKV if score_mode == "aoakv" else _lib.SCORE_QUEST
+    s = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
+    _lib.call("aoakv_decode_step_batched", q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(),
+              o.data_ptr(), kv.data_ptr(), cap, kv_indptr.data_ptr(), kv_indices.data_ptr(),
+              kv_last_page_len.data_ptr(), meta.data_ptr(), meta.shape[0],
+              meta_indptr.data_ptr(), meta_indices.data_ptr(), v_log_norm.data_ptr(), R,
+              int(max_pages), H, D, P, int(page_budget), mode, int(bool(sink_first_page)),
+              None if selected is None else selected.data_ptr(), s)
+    return o

@@ -1,41 +1,48 @@
 #!/usr/bin/env python
 """Headline benchmark: sparse-decode µs/layer @ 32K context, 1K budget.
 
-Workload (the headline "32K ctx, B=1024" configuration with outlier-key inputs): one
-request, 32 heads MHA, head_dim 128, fp16 paged KV with page_size 16, context
-32768 tokens (N = 2048 pages), budget 1024 tokens (64 pages: 63 selected +
-the last page), AOA-KV value-aware scoring; K ~ N(0,1) * LogNormal(0,1)
-per-channel scale, q, V ~ N(0,1), seed 1; synthetic data.
+Workload (the headline "32K ctx, B=1024" configuration with outlier-key
+inputs): one request, 32 heads MHA, head_dim 128, fp16 paged KV with
+page_size 16, context 32768 tokens (N = 2048 pages, the new token included),
+budget 1024 tokens (64 pages: 63 selected + the last page), AOA-KV
+value-aware scoring; K ~ N(0,1) * LogNormal(0,1) per-channel scale, q, V ~
+N(0,1), seed 1; synthetic data.
 
 A "step" is one decode token through L = 32 layers (each layer has its own
 KV cache, metadata and v_log_norm): per layer the library appends the token
-and runs estimate -> top-k -> sparse decode. The 32 layers touch
-32 x 50.5 MB > L2 (126 MB) per step, so no layer finds its data in L2.
+and runs estimate -> top-k -> sparse decode (one launch per layer). The 32
+layers touch 32 x 50.5 MB > L2 (126 MB) per step, so no layer finds its data
+in L2.
 
-  value     device time per layer-step, whole job: max-over-ranks time of K
-            CUDA-graph replays of the 32-layer step / (K * 32 * n_gpus)
+  value     device time per layer-step of one request on one GPU: the
+            max-over-ranks time of K CUDA-graph replays of the 32-layer step
+            / (K * 32). With --gpus N every GPU serves its own request (N
+            replicas, no collective), so the value is per GPU ("weak").
   e2e       the same through InferenceController.decode_step, with the
             step's q, k, v copied from pinned host memory and its outputs
             copied back inside the timed region, no graph
-  roofline  the step kernel (one fused launch per layer): algorithmic bytes
-            of a layer-step / its average duration inside the timed graph;
-            estimate_roofline: the stand-alone page scorer timed the same way
+  roofline  the step kernel: algorithmic bytes of a layer-step / its
+            average duration inside the timed graph
 
-With --gpus N (torchrun, one process per GPU) every rank serves its own
-request (request sharding, no collective): scaling "weak".
---mode longctx instead splits ONE 128K-context request (budget 4096) by page
-range over the GPUs, with two NCCL all_gathers per layer: scaling "strong".
---mode batched runs 32 requests of 4K-16K tokens (config 4), balanced over
-the GPUs by bytes, no collective: scaling "strong". --mode model times a
-32-layer Llama-2-7B-shaped decode step with this attention (config 3).
+Extra keys of the same line (each its own workload; see their "config"):
+  longctx           config 5: ONE 131072-token request (budget 4096) split
+                    by page range over the job's N GPUs (strong scaling),
+                    two all_gathers per layer; at N = 1 the plain step
+  batched           config 4: 32 requests of 4K-16K tokens balanced over the
+                    GPUs by bytes, one launch per layer per GPU (strong)
+  prefill_metadata  config 5's prefill: KV pages + key max/min + v_log_norm
+                    for 131071 tokens in one pass (N = 1 only)
+  config2           config 2 at 8192 tokens: each kernel alone and the step
+                    as one launch and as the chain (N = 1 only)
+--mode model times config 3 (Llama-2-7B-shaped decode, budget sweep).
 --impl reference times the reference's CPU simulation path (the numpy port
 in oracle/sim.py of filter_util.py + quest_attention.py) on the host cores.
 """
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -48,49 +55,140 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "sparse-decode µs/layer @32K ctx, 1K budget; % of B200 HBM roofline"
-# DRAM bytes (read + write) of one fused step launch at the headline shape,
-# from the ncu capture summarised under profiles/ (dram__bytes_read.sum +
-# dram__bytes_write.sum, one layer, caches flushed)
-STEP_TRAFFIC_BYTES = 52_328_448
 H, D, P = 32, 128, 16
+# DRAM bytes (read + write) of one cluster step launch at the headline shape:
+# dram__bytes_read.sum + dram__bytes_write.sum from the ncu capture
+# summarised in profiles/cluster_step_32k.md (not measured in this run)
+STEP_TRAFFIC_BYTES = None
+STEP_TRAFFIC_SOURCE = "profiles/cluster_step_32k.md (ncu, not measured in this run)"
 
 
 def parse():
-    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap = argparse.ArgumentParser(description=__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--mode", choices=["headline", "longctx", "batched", "model"],
                     default="headline",
-                    help="headline: 32K ctx, 1K budget, one request per GPU; longctx: one "
-                         "128K-context request split by page range over the GPUs; batched: "
-                         "--requests requests of 4K-16K tokens balanced over the GPUs; "
-                         "model: a 32-layer Llama-2-7B-shaped decode step (random weights)")
-    ap.add_argument("--requests", type=int, default=32, help="batched: requests in the batch")
-    ap.add_argument("--streams", type=int, default=8,
-                    help="batched: requests' steps run side by side on this many streams, each "
-                         "step's fused kernel capped to its share of the GPU (1 = one after "
-                         "another on the whole GPU)")
-    ap.add_argument("--layers", type=int, default=None, help="default 32 (headline), 4 (longctx)")
-    ap.add_argument("--ctx", type=int, default=None, help="default 32768 (headline), 131072 (longctx)")
-    ap.add_argument("--budget", type=int, default=None,
-                    help="token budget; default 1024 (headline), 4096 (longctx)")
+                    help="headline (default): the headline line with every extra key; "
+                         "longctx / batched: that key alone; model: config 3")
+    ap.add_argument("--extras", default="longctx,batched,prefill_metadata,config2",
+                    help="comma list of extra keys for the headline line ('' = none)")
+    ap.add_argument("--layers", type=int, default=32, help="headline layers per step")
+    ap.add_argument("--ctx", type=int, default=32768, help="headline context tokens")
+    ap.add_argument("--budget", type=int, default=1024, help="headline token budget")
     ap.add_argument("--method", choices=["aoakv", "quest"], default="aoakv")
     ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--long-ctx", type=int, default=131072)
+    ap.add_argument("--long-budget", type=int, default=4096)
+    ap.add_argument("--extra-layers", type=int, default=4,
+                    help="layers per step of the longctx and batched keys")
+    ap.add_argument("--requests", type=int, default=32, help="batched: requests")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="CPU-baseline sample budget (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--soak-seconds", type=float, default=1.0,
                     help="graph replays before the timed region so the clock sampler sees load")
-    ap.add_argument("--no-graph", action="store_true", help="longctx: launch without a CUDA graph")
-    a = ap.parse_args()
-    long = a.mode == "longctx"
-    a.layers = a.layers or (4 if a.mode != "headline" else 32)
-    a.ctx = a.ctx or (131072 if long else 32768)
-    a.budget = a.budget or (4096 if long else 1024)
-    return a
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------- plumbing
+def dist_env():
+    return (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def init_gpu(world, local):
+    import torch
+    import torch.distributed as dist
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    return dev
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world, dev) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def gather_ints(vals, world, dev):
+    """Every rank's list of ints (same length on every rank), rank order."""
+    import torch
+    t = torch.tensor(vals, device=dev, dtype=torch.int64)
+    if world == 1:
+        return [list(map(int, t.tolist()))]
+    import torch.distributed as dist
+    out = torch.empty(world * t.numel(), device=dev, dtype=torch.int64)
+    dist.all_gather_into_tensor(out, t)
+    return [list(map(int, r)) for r in out.view(world, -1).tolist()]
+
+
+def time_replays(run, steps, warmup, world, dev) -> float:
+    """ms of `steps` calls of run() on the current stream, CUDA events, after
+    `warmup` calls, barrier + synchronize on both sides, max over ranks."""
+    import torch
+    for _ in range(warmup):
+        run()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1), world, dev)
+
+
+def capture(fn, dev):
+    """fn() once eagerly on a side stream (attributes and workspaces outside
+    capture), then a CUDA graph of it."""
+    import torch
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def load_peak():
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        peaks = {}
+    if peaks.get("hbm_gbs"):
+        return float(peaks["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    return 6650.0, "fallback"
+
+
+def roof(bytes_, us, peak, n_gpus=1):
+    ach = bytes_ / (us * 1e-6) / 1e9
+    return {"bound": "hbm", "achieved": round(ach, 1), "peak": round(peak * n_gpus, 1),
+            "unit": "GB/s", "frac": round(ach / (peak * n_gpus), 4), "algorithmic_bytes": bytes_}
 
 
 def lib_md5() -> str:
@@ -104,38 +202,30 @@ def lib_md5() -> str:
         return "unknown"
 
 
-def workload_config(a, n_gpus):
-    n_pages = (a.ctx + P - 1) // P
-    return {
-        "workload": f"1 request/GPU, {a.layers}-layer decode step, ctx {a.ctx}, budget {a.budget}",
-        "context_tokens": a.ctx, "token_budget": a.budget, "page_size": P, "num_heads": H,
-        "head_dim": D, "layers_per_step": a.layers, "score_mode": a.method, "sink_first_page": False,
-        "pages_scored": n_pages - 1, "pages_attended": min(a.budget // P, n_pages),
-        "inputs": "K~N(0,1)*LogNormal(0,1)[h,d], q,V~N(0,1), seed %d" % a.seed,
-        "l2": "inputs larger than L2: %d layers x %.1f MB touched per step" % (
-            a.layers, step_bytes(a) / 1e6),
-        "accumulate": "fp32", "parallelism": f"request-sharded x{n_gpus}, no collective",
-    }
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
-def step_bytes(a) -> int:
-    """Algorithmic bytes of one layer-step: metadata of the
-    N-1 scored pages, their v_log_norm (aoakv), the k attended pages' K and V,
-    and q + o."""
-    n = (a.ctx + P - 1) // P
-    k = min(a.budget // P, n)
-    b = (n - 1) * H * 2 * D * 2 + k * P * H * D * 2 * 2 + 2 * H * D * 2
-    if a.method == "aoakv":
-        b += (n - 1) * H * 2
-    return b
+def step_bytes(ctx, budget, method="aoakv") -> int:
+    """Algorithmic bytes of one layer-step: metadata (key max and min rows)
+    of the N-1 scored pages, their v_log_norm (aoakv), the k attended pages'
+    K and V, and q + o."""
+    from aoa_kv_b200.batching import step_bytes as sb
+    return sb(ctx, budget, H, D, P, method)
 
 
-def estimate_bytes(a) -> int:
+def estimate_bytes(ctx, method="aoakv") -> int:
     """Algorithmic bytes of one estimate launch: metadata + v_log_norm of the
     N-1 scored pages, q, and the fp32 scores written."""
-    n = (a.ctx + P - 1) // P
+    n = (ctx + P - 1) // P
     b = (n - 1) * H * 2 * D * 2 + H * D * 2 + (n - 1) * H * 4
-    if a.method == "aoakv":
+    if method == "aoakv":
         b += (n - 1) * H * 2
     return b
 
@@ -215,6 +305,15 @@ def cpu_threads() -> int:
     return os.cpu_count() or 1
 
 
+def reference_timing_here():
+    """The reference's own filter_util.py step timed beside the port on the
+    machine that has the reference checkout (tests/golden/time_cpu_reference.py)."""
+    try:
+        return json.loads((ROOT / "tests" / "golden" / "cpu_reference_timing.json").read_text())
+    except (OSError, ValueError):
+        return None
+
+
 def cpu_sim_setup(a):
     import numpy as np
     from oracle import sim
@@ -247,46 +346,84 @@ def cpu_sim_steps(a, n_steps, budget_s=None):
     return times
 
 
+def cpu_baseline_entry(times, a):
+    """The port's median step, and the same scaled by the filter_util / port
+    ratio measured where the reference checkout exists (the reference
+    itself cannot run here)."""
+    us = statistics.median(times) * 1e6
+    rt = reference_timing_here()
+    ratio = rt["filter_util_over_port"] if rt else None
+    return us, {
+        "value": round(us * ratio if ratio else us, 1), "unit": "us", "cores": cpu_threads(),
+        "cpu_model": cpu_model(), "kind": "port",
+        "port_measured_us": round(us, 1),
+        "filter_util_over_port": ratio,
+        "filter_util_over_port_measured_on": rt and f"{rt['cpu_model']}, {rt['threads']} threads",
+        "sample": f"{len(times)} single-layer decode steps of the reference simulation restated "
+                  f"in oracle/sim.py (filter_util.py + quest_attention.py decode branch) at ctx "
+                  f"{a.ctx}, budget {a.budget}, {a.method}, fixed=True (pages 0 and N-1 forced); "
+                  f"median" + ("; value = port median x filter_util/port ratio" if ratio else ""),
+    }
+
+
 def run_reference(a):
-    rank = int(os.environ.get("RANK", "0"))
-    n_gpus = int(os.environ.get("WORLD_SIZE", str(a.gpus)))
+    world, rank, _ = dist_env()
     if rank != 0:
         return
     for _ in range(max(0, min(a.warmup, 3))):
         cpu_sim_steps(a, 1)
     times = cpu_sim_steps(a, a.steps)
-    us = statistics.median(times) * 1e6
-    cores = cpu_threads()
+    _, cpu = cpu_baseline_entry(times, a)
+    us = cpu["value"]
+    cfg = workload_config(a, world)
+    cfg["sink_first_page"] = True  # the simulation's fixed=True
+    cfg["parallelism"] = "host cores of rank 0's node (per-replica latency, not divided by N)"
     line = {
-        "metric": METRIC, "value": round(us, 3), "unit": "us", "impl": "reference",
-        "n_gpus": n_gpus, "steps": len(times), "warmup": a.warmup, "ms_per_step": round(us / 1e3, 3),
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": workload_config(a, n_gpus),
-        "cpu_baseline": {"value": round(us, 3), "unit": "us", "cores": cores, "kind": "port",
-                         "sample": f"{len(times)} single-layer decode steps of the simulation "
-                                   f"(oracle/sim.py restating filter_util.py + quest_attention.py), "
-                                   f"ctx {a.ctx}, budget {a.budget}, {a.method}, fixed=True, median"},
-        "e2e": {"value": round(us, 3), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "metric": METRIC, "value": us, "unit": "us", "impl": "reference",
+        "n_gpus": world, "steps": len(times), "warmup": a.warmup,
+        "ms_per_step": round(us / 1e3, 3), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+        "cpu_baseline": cpu,
+        "e2e": {"value": us, "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-# ---------------------------------------------------------------- our arm
-def setup_layers(a, dev):
+# ---------------------------------------------------------------- headline
+def workload_config(a, n_gpus):
+    n_pages = (a.ctx + P - 1) // P
+    return {
+        "workload": f"1 request per GPU, {a.layers}-layer decode step, ctx {a.ctx}, "
+                    f"budget {a.budget}",
+        "context_tokens": a.ctx, "token_budget": a.budget, "page_size": P, "num_heads": H,
+        "head_dim": D, "layers_per_step": a.layers, "score_mode": a.method,
+        "sink_first_page": False, "pages_scored": n_pages - 1,
+        "pages_attended": min(a.budget // P, n_pages),
+        "inputs": "K~N(0,1)*LogNormal(0,1)[h,d], q,V~N(0,1), seed %d" % a.seed,
+        "l2": "inputs larger than L2: %d layers x %.1f MB touched per step" % (
+            a.layers, step_bytes(a.ctx, a.budget, a.method) / 1e6),
+        "accumulate": "fp32",
+        "parallelism": f"{n_gpus} replica(s), one request per GPU, no collective; value is "
+                       f"per GPU (max over ranks), not divided by the GPU count",
+    }
+
+
+def setup_layers(ctx, layers, budget, seed, method, dev, outlier=True):
+    """An InferenceController holding `layers` layers of ctx-1 cached tokens,
+    ready for the decode step of token ctx; returns (ctl, [(q, k, v)])."""
     import torch
 
     import aoa_kv_b200 as ak
-    gen = torch.Generator(device=dev).manual_seed(a.seed)
-    ctl = ak.InferenceController(a.layers, H, D, P, a.budget // P, a.ctx + P, torch.float16, dev,
-                                 method=a.method)
-    S = a.ctx
-    ctl.prepare_metadata(S - 1)
-    ctl.begin_forward(S - 1)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    ctl = ak.InferenceController(layers, H, D, P, budget // P, ctx + P, torch.float16, dev,
+                                 method=method)
+    ctl.prepare_metadata(ctx - 1)
+    ctl.begin_forward(ctx - 1)
     news = []
-    for layer in range(a.layers):
-        scale = torch.exp(torch.randn(H, D, device=dev, generator=gen))
-        K = (torch.randn(S, H, D, device=dev, generator=gen) * scale).half()
-        V = torch.randn(S, H, D, device=dev, generator=gen).half()
+    for layer in range(layers):
+        scale = torch.exp(torch.randn(H, D, device=dev, generator=gen)) if outlier else 1.0
+        K = (torch.randn(ctx, H, D, device=dev, generator=gen) * scale).half()
+        V = torch.randn(ctx, H, D, device=dev, generator=gen).half()
         q = torch.randn(1, H, D, device=dev, generator=gen).half()
         ak.append_kv(K[:-1].contiguous(), V[:-1].contiguous(), ctl, layer)
         news.append((q, K[-1:].contiguous(), V[-1:].contiguous()))
@@ -298,45 +435,29 @@ def setup_layers(a, dev):
     return ctl, news
 
 
-def run_ours(a):
+def run_headline(a):
+    import ctypes
+
     import torch
-    import torch.distributed as dist
 
     import aoa_kv_b200 as ak
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        import datetime
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
+    world, rank, local = dist_env()
+    dev = init_gpu(world, local)
     ak._lib.load()
+    peak, peak_src = load_peak()
 
-    ctl, news = setup_layers(a, dev)
+    ctl, news = setup_layers(a.ctx, a.layers, a.budget, a.seed, a.method, dev)
     outs = [torch.empty(1, H, D, dtype=torch.float16, device=dev) for _ in range(a.layers)]
-    import ctypes
-    nk = ctypes.c_int32(0)
-    ak._lib.call("aoakv_step_launches", H, D, P, len(ctl.kv_cache.indicies),
-                 ctl.step_page_budget(), int(ctl.sink_first_page), 0, ctypes.byref(nk))
-    kernels_per_layer = int(nk.value)
+    nk, ncl = ctypes.c_int32(0), ctypes.c_int32(0)
+    ak._lib.call("aoakv_step_plan_info", ctl.step_plan(0)._h, len(ctl.kv_cache.indicies), 0,
+                 ctypes.byref(nk), ctypes.byref(ncl))
+    kernels_per_layer, cluster = int(nk.value), int(ncl.value)
 
     def one_step():
         for layer, (q, k, v) in enumerate(news):
             ctl.decode_step(q, k, v, layer, out=outs[layer])
 
-    s = torch.cuda.Stream(device=dev)
-    s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        one_step()  # first calls set kernel attributes outside capture
-    torch.cuda.current_stream().wait_stream(s)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        one_step()
-    torch.cuda.synchronize()
+    graph = capture(one_step, dev)
     ak.check_device()
 
     sampler = ClockSampler(gpu_query_id(local)) if rank == 0 else None
@@ -344,35 +465,17 @@ def run_ours(a):
     for _ in range(a.warmup):
         graph.replay()
     torch.cuda.synchronize()
-    # keep the GPU busy so the clock sampler sees it under this load
-    t_end = time.monotonic() + a.soak_seconds
+    t_end = time.monotonic() + a.soak_seconds  # let the clock sampler see the load
     while time.monotonic() < t_end:
         for _ in range(20):
             graph.replay()
         torch.cuda.synchronize()
-
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev0.record()
-    for _ in range(a.steps):
-        graph.replay()
-    ev1.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    ms = time_replays(graph.replay, a.steps, 0, world, dev)
     t_timed_end = time.monotonic()
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
     ak.check_device()
-    us_layer_job = ms * 1e3 / (a.steps * a.layers * world)
-    us_layer_gpu = ms * 1e3 / (a.steps * a.layers)
+    us_layer = ms * 1e3 / (a.steps * a.layers)
 
-    # --- dominant kernel alone: the page-score estimate (fp32 scores)
+    # the page scorer alone (fp32 scores), the same layers
     n = (a.ctx + P - 1) // P
     scores = torch.empty(H, n, dtype=torch.float32, device=dev)
 
@@ -385,24 +488,10 @@ def run_ours(a):
                          meta.shape[0], ctl.kv_indices_with_last.data_ptr(),
                          ctl.kv_cache.pool.capacity, ctl.v_log_norm_layer(layer).data_ptr(), H, D,
                          P, 0, ctl.score_mode, torch.cuda.current_stream().cuda_stream)
-    with torch.cuda.stream(s):
-        est_all()
-    torch.cuda.synchronize()
-    g_est = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_est):
-        est_all()
-    for _ in range(3):
-        g_est.replay()
-    reps = max(5, a.steps // 2)
-    torch.cuda.synchronize()
-    ev0.record()
-    for _ in range(reps):
-        g_est.replay()
-    ev1.record()
-    torch.cuda.synchronize()
-    est_us = ev0.elapsed_time(ev1) * 1e3 / (reps * a.layers)
+    g_est = capture(est_all, dev)
+    est_us = time_replays(g_est.replay, max(5, a.steps // 2), 3, world, dev) * 1e3 / (
+        max(5, a.steps // 2) * a.layers)
 
-    # --- e2e through the public API with host buffers
     e2e = None
     if not a.no_e2e:
         # the step's inputs (every layer's q, k, v) in one pinned host buffer,
@@ -418,92 +507,235 @@ def run_ours(a):
                 ctl.decode_step(dev_qkv[layer, 0], dev_qkv[layer, 1], dev_qkv[layer, 2], layer,
                                 out=o_all[layer])
             host_o.copy_(o_all, non_blocking=True)
-        for _ in range(a.warmup):
-            e2e_step()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        ev0.record()
-        for _ in range(a.steps):
-            e2e_step()
-        ev1.record()
-        torch.cuda.synchronize()
-        ems = ev0.elapsed_time(ev1)
-        if world > 1:
-            t = torch.tensor([ems], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ems = float(t.item())
-        e2e = {"value": round(ems * 1e3 / (a.steps * a.layers * world), 3), "unit": "us",
+        ems = time_replays(e2e_step, a.steps, a.warmup, world, dev)
+        e2e = {"value": round(ems * 1e3 / (a.steps * a.layers), 3), "unit": "us",
                "h2d_bytes_per_step": a.layers * 3 * H * D * 2,
                "d2h_bytes_per_step": a.layers * H * D * 2,
-               "api": "InferenceController.decode_step per layer (ctypes -> aoakv_decode_step); "
-                      "one H2D of the step's q/k/v and one D2H of its outputs; no graph"}
+               "api": "InferenceController.decode_step per layer (ctypes -> "
+                      "aoakv_step_plan_run); one H2D of the step's q/k/v and one D2H of its "
+                      "outputs; no graph; per GPU"}
 
     if sampler:
         sampler.stop()
     clocks = sampler.summary(t_soak, t_timed_end) if sampler else None
 
-    peaks = {}
-    try:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except (OSError, ValueError):
-        pass
-    peak = float(peaks.get("hbm_gbs") or 6650.0)
-    peak_src = "measured" if peaks.get("hbm_gbs") else "fallback"
-    eb = estimate_bytes(a)
-    ach = eb / (est_us * 1e-6) / 1e9
-    sb = step_bytes(a)
-    step_ach = sb / (us_layer_gpu * 1e-6) / 1e9
-
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        times = cpu_sim_steps(a, 50, budget_s=a.cpu_seconds)
-        cpu_us = statistics.median(times) * 1e6
-        cpu = {"value": round(cpu_us, 1), "unit": "us", "cores": cpu_threads(), "kind": "port",
-               "sample": f"{len(times)} single-layer decode steps of the reference simulation "
-                         f"(oracle/sim.py: filter_util.py + quest_attention.py decode branch) at "
-                         f"ctx {a.ctx}, budget {a.budget}, {a.method}, fixed=True; median"}
+        _, cpu = cpu_baseline_entry(cpu_sim_steps(a, 50, budget_s=a.cpu_seconds), a)
 
+    sb = step_bytes(a.ctx, a.budget, a.method)
+    eb = estimate_bytes(a.ctx, a.method)
+    r = roof(sb, us_layer, peak)
+    r.update({"kernel": (f"cluster_step_kernel<{D},{cluster}> (append+estimate+top-k+decode, "
+                         f"one launch)") if kernels_per_layer == 1 else
+              f"step chain of {kernels_per_layer} kernels",
+              "traffic": STEP_TRAFFIC_BYTES, "traffic_source": STEP_TRAFFIC_SOURCE,
+              "avg_launch_us": round(us_layer, 3),
+              "ideal_us": round(sb / (peak * 1e9) * 1e6, 3), "peak_source": peak_src,
+              "timing": "CUDA events around K graph replays of the 32-layer step on the "
+                        "launching stream; avg launch = time / (K * layers), gaps included"})
+    er = roof(eb, est_us, peak)
+    er.update({"kernel": "estimate_attn_score alone (page scorer)",
+               "avg_launch_us": round(est_us, 3)})
+    line = None
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(us_layer_job, 3), "unit": "us", "n_gpus": world,
+            "metric": METRIC, "value": round(us_layer, 3), "unit": "us", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4),
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic", "config": workload_config(a, world),
-            "per_gpu_us_per_layer": round(us_layer_gpu, 3),
-            # the step kernel: one launch per layer (fused) or the chain of
-            # kernels_per_layer launches; avg launch duration = timed graph
-            # time / layers, gaps between launches included
-            "roofline": {"bound": "hbm",
-                         "kernel": "fused_step_kernel (append+estimate+top-k+decode)"
-                         if kernels_per_layer == 1 else
-                         f"step chain of {kernels_per_layer} kernels",
-                         "achieved": round(step_ach, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(step_ach / peak, 4),
-                         "traffic": STEP_TRAFFIC_BYTES if (kernels_per_layer == 1 and
-                                                           a.ctx == 32768 and a.budget == 1024 and
-                                                           a.method == "aoakv") else None,
-                         "algorithmic_bytes": sb, "avg_launch_us": round(us_layer_gpu, 3),
-                         "ideal_us": round(sb / (peak * 1e9) * 1e6, 3),
-                         "peak_source": peak_src},
-            "estimate_roofline": {"kernel": "estimate_attn_score stand-alone (page scorer)",
-                                  "achieved": round(ach, 1), "unit": "GB/s",
-                                  "frac": round(ach / peak, 4), "algorithmic_bytes": eb,
-                                  "avg_launch_us": round(est_us, 3)},
+            "roofline": r, "estimate_roofline": er,
             "e2e": e2e, "gpu_launches": kernels_per_layer * a.layers * a.steps,
             "step_kernels_per_layer": kernels_per_layer, "clocks": clocks,
-            "library_md5": lib_md5(),
-            "cpu_baseline": cpu,
+            "library_md5": lib_md5(), "cpu_baseline": cpu,
         }
-        print(json.dumps(line), flush=True)
     del graph, g_est
+    ctl.clean_states()
+    del ctl, news, outs
+    torch.cuda.empty_cache()
+
+    extras = [x for x in a.extras.split(",") if x]
+    for key in extras:
+        fn = {"longctx": longctx_key, "batched": batched_key,
+              "prefill_metadata": prefill_key, "config2": config2_key}.get(key)
+        if fn is None:
+            raise SystemExit(f"unknown extra key {key!r}")
+        if key in ("prefill_metadata", "config2") and world > 1:
+            continue  # single-GPU workloads: reported at N = 1
+        val = fn(a, world, rank, dev, peak)
+        if line is not None:
+            line[key] = val
+        torch.cuda.empty_cache()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    finish(world)
+
+
+def finish(world):
+    import gc
+
+    import torch
+    gc.collect()  # graphs that hold NCCL calls go before the process group
+    torch.cuda.synchronize()
     if world > 1:
+        import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
 
 
 # ------------------------------------------------ long context, sharded
-LONG_METRIC = "sparse-decode µs/layer @128K ctx, 4K budget, page-range sharded"
+def _prefill(K, V, t0, t1, kv, kv_idx, meta, meta_idx, vlog, stream):
+    """Tokens [t0, t1) of K, V [S, H, D] into pages 0.. of the given tables."""
+    from aoa_kv_b200 import _lib
+    n_tok = t1 - t0
+    if n_tok <= 0:
+        return
+    n_pref = -(-n_tok // P)
+    _lib.call("aoakv_append_kv_cache_prefill", K[t0:t1].data_ptr(), V[t0:t1].data_ptr(), n_tok,
+              kv.data_ptr(), kv_idx.data_ptr(), n_pref, (n_tok - 1) % P + 1, kv.shape[0],
+              meta.data_ptr(), meta_idx.data_ptr(), -(-n_pref // P), (n_pref - 1) % P + 1,
+              meta.shape[0], vlog.data_ptr(), H, D, P, _lib.LAYOUT_NHD, stream)
+
+
+def _pool(n_pages, dev):
+    import torch
+    cap = n_pages + 1
+    mcap = -(-cap // P)
+    kv = torch.empty(cap, 2, P, H, D, dtype=torch.float16, device=dev)
+    meta = torch.empty(mcap, 2, P, H, D, dtype=torch.float16, device=dev)
+    vlog = torch.zeros(cap, H, dtype=torch.float16, device=dev)
+    kv_idx = torch.arange(n_pages, dtype=torch.int32, device=dev)
+    meta_idx = torch.arange(mcap, dtype=torch.int32, device=dev)
+    return kv, meta, vlog, kv_idx, meta_idx
+
+
+def longctx_key(a, world, rank, dev, peak):
+    """Config 5: one request of a.long_ctx tokens (the new one included),
+    budget a.long_budget, q, K, V ~ N(0,1) (seed 4). N = 1: the plain step
+    (StepPlan, one launch per layer), cross-checked against the sharded
+    decoder run on one rank. N > 1: the page range is split over the ranks
+    (aoa_kv_b200.sharded: local top-k, all_gather of candidates, global
+    top-k, partial decode of the owned pages, all_gather of partial states,
+    LSE merge), cross-checked on rank 0 against the plain step over the
+    whole sequence."""
+    import torch
+
+    from aoa_kv_b200 import StepPlan, _lib, sharded
+    S, budget, L = a.long_ctx, a.long_budget, a.extra_layers
+    n_total, last_len = -(-S // P), (S - 1) % P + 1
+    lo, hi = sharded.partition_pages(n_total, world, P)[rank]
+    n_local, owns = hi - lo, rank == world - 1
+    stream = torch.cuda.current_stream().cuda_stream
+    kpages = budget // P
+    layers, news, full0 = [], [], None
+    for layer in range(L):
+        g = torch.Generator(device=dev).manual_seed(4000 + layer)
+        K = torch.randn(S, H, D, device=dev, generator=g).half()
+        V = torch.randn(S, H, D, device=dev, generator=g).half()
+        q = torch.randn(H, D, device=dev, generator=g).half()
+        news.append((q, K[S - 1].clone(), V[S - 1].clone()))
+        kv, meta, vlog, kv_idx, meta_idx = _pool(n_local, dev)
+        _prefill(K, V, lo * P, min(hi * P, S - 1), kv, kv_idx, meta, meta_idx, vlog, stream)
+        layers.append(sharded.ShardLayer(kv=kv, meta=meta, vlog=vlog, kv_idx=kv_idx,
+                                         meta_idx=meta_idx, page_lo=lo, n_local=n_local,
+                                         n_total=n_total, last_len=last_len, owns_last=owns,
+                                         last_phys=n_local - 1 if owns else -1))
+        if layer == 0 and rank == 0 and world > 1:  # the whole sequence, for the check
+            full0 = _pool(n_total, dev)
+            _prefill(K, V, 0, S - 1, full0[0], full0[3], full0[1], full0[4], full0[2], stream)
+        del K, V
+    torch.cuda.synchronize()
+    mode = _lib.SCORE_AOAKV if a.method == "aoakv" else _lib.SCORE_QUEST
+    o = torch.empty(L, H, D, dtype=torch.float16, device=dev)
+    sel = torch.empty(L, H, kpages, dtype=torch.int32, device=dev)
+    # the step's workspace (used only if a plan runs the four-kernel chain)
+    ws = torch.zeros(_lib.size_query("aoakv_step_workspace_size", H, D, n_total, kpages),
+                     dtype=torch.uint8, device=dev)
+    if world == 1:
+        plans = [StepPlan(lay.kv, lay.kv.shape[0], lay.meta, lay.meta.shape[0], lay.vlog, H, D, P,
+                          kpages, mode, max_pages=n_total) for lay in layers]
+
+        def one_step():
+            for i, (lay, (q, k, v)) in enumerate(zip(layers, news)):
+                plans[i].run(q, k, v, o[i], lay.kv_idx, n_total, last_len, lay.meta_idx,
+                             None, ws, ws.numel(), torch.cuda.current_stream().cuda_stream)
+        launches = plans[0].info(n_total)[0] * L
+    else:
+        dec = sharded.ShardedDecoder(torch.distributed.group.WORLD, H, D, P, kpages, a.method)
+
+        def one_step():
+            for i, (lay, (q, k, v)) in enumerate(zip(layers, news)):
+                o[i].copy_(dec.step(lay, q, k, v)[0])
+        launches = None
+    graph = capture(one_step, dev)
+    steps = max(10, a.steps // 2)
+    ms = time_replays(graph.replay, steps, a.warmup, world, dev)
+    _lib.check_device()
+    us = ms * 1e3 / (steps * L)
+
+    # check (layer 0): the other implementation on the same data
+    err, sel_equal = None, None
+    if world == 1:
+        plans[0].run(news[0][0], news[0][1], news[0][2], o[0], layers[0].kv_idx, n_total,
+                     last_len, layers[0].meta_idx, sel[0], ws, ws.numel(), stream)
+        dec = sharded.ShardedDecoder(_SoloGroup(), H, D, P, kpages, a.method)
+        o_x, sel_x = dec.step(layers[0], *news[0])
+        torch.cuda.synchronize()
+        err = float((o[0].float() - o_x.float()).abs().max())
+        mine = torch.sort(sel[0][:, :kpages - 1], dim=1).values
+        sel_equal = bool(torch.equal(mine, torch.sort(sel_x, dim=1).values))
+        sel_global = sel[0][:, :kpages - 1]
+    else:
+        o_s, sel_s = dec.step(layers[0], *news[0])
+        torch.cuda.synchronize()
+        sel_global = sel_s
+        if rank == 0:
+            kv, meta, vlog, kv_idx, meta_idx = full0
+            ref_plan = StepPlan(kv, kv.shape[0], meta, meta.shape[0], vlog, H, D, P, kpages, mode,
+                                max_pages=n_total)
+            o_ref = torch.empty(H, D, dtype=torch.float16, device=dev)
+            sel_ref = torch.empty(H, kpages, dtype=torch.int32, device=dev)
+            ref_plan.run(news[0][0], news[0][1], news[0][2], o_ref, kv_idx, n_total, last_len,
+                         meta_idx, sel_ref, ws, ws.numel(), stream)
+            torch.cuda.synchronize()
+            err = float((o_s.float() - o_ref.float()).abs().max())
+            sel_equal = bool(torch.equal(torch.sort(sel_ref[:, :kpages - 1], dim=1).values,
+                                         torch.sort(sel_s, dim=1).values))
+            del ref_plan
+    # per-GPU algorithmic bytes of a layer-step: this rank's scored pages'
+    # metadata (+ v_log_norm), its attended pages' K and V, q and o
+    n_score = n_local - (1 if owns else 0)
+    in_mine = ((sel_global >= lo) & (sel_global < hi)).sum().item() + (H if owns else 0)
+    row = 2 * D * 2 + (2 if a.method == "aoakv" else 0)
+    mine_bytes = n_score * H * row + in_mine * P * D * 2 * 2 + 2 * H * D * 2
+    got = gather_ints([mine_bytes, in_mine], world, dev)
+    per_gpu, pages_dec = [r[0] for r in got], [r[1] for r in got]
+    del graph
+    torch.cuda.synchronize()
+    if rank != 0:
+        return None
+    total = sum(per_gpu)
+    out = {
+        "metric": "sparse-decode µs/layer @128K ctx, 4K budget (config 5)",
+        "value": round(us, 3), "unit": "us", "n_gpus": world, "scaling": "strong",
+        "steps": steps, "layers_per_step": L,
+        "roofline": roof(total, us, peak, world),
+        "max_gpu_bytes": max(per_gpu), "per_gpu_bytes": per_gpu,
+        "decode_head_pages_per_gpu": pages_dec,
+        "max_abs_err": err, "selection_equal": sel_equal,
+        "checked_against": ("the sharded decoder (estimate, top-k, partial decode, merge) on the "
+                            "same data, layer 0" if world == 1 else
+                            "the one-GPU step over the whole sequence on rank 0, layer 0"),
+        "config": {"workload": f"1 request, ctx {S} (new token included), budget {budget}, "
+                               f"{L}-layer step, q,K,V~N(0,1) seed 4",
+                   "pages": n_total, "pages_per_gpu": n_local,
+                   "parallelism": "1 GPU, one step launch per layer" if world == 1 else
+                   f"page range x{world}; all_gather of candidates ({world}x{H}x"
+                   f"{kpages - 1}x8 B) and partial states ({world}x{H}x{D + 1}x4 B) per layer"},
+    }
+    if launches is not None:
+        out["gpu_launches"] = launches * steps
+    return out
 
 
 class _SoloGroup:
@@ -514,281 +746,267 @@ class _SoloGroup:
         return t.unsqueeze(0)
 
 
-def run_longctx(a):
-    """One request of a.ctx tokens split by page range over the job's GPUs
-    (aoa_kv_b200.sharded): per layer, the last rank appends, every rank
-    scores and proposes its top-(k-1), all_gather, global top-(k-1), partial
-    decode of the owned pages, all_gather, LSE merge. Strong scaling: the
-    total work is one request whatever the GPU count."""
-    import datetime
-
-    import torch
-    import torch.distributed as dist
-
-    from aoa_kv_b200 import _lib, sharded
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-        group = dist.group.WORLD
-    else:
-        group = _SoloGroup()
-    _lib.load()
-    S = a.ctx
-    n_total, last_len = S // P + 1, S % P + 1
-    lo, hi = sharded.partition_pages(n_total, world, P)[rank]
-    n_local = hi - lo
-    owns = rank == world - 1
-    cap = n_local + 1
-    mcap = -(-cap // P)
-    layers, news = [], []
-    for layer in range(a.layers):
-        g_layer = torch.Generator(device=dev).manual_seed(a.seed * 1000 + layer)
-        scale = torch.exp(torch.randn(H, D, device=dev, generator=g_layer))
-        q = torch.randn(H, D, device=dev, generator=g_layer).half()
-        k_new = (torch.randn(H, D, device=dev, generator=g_layer) * scale).half()
-        v_new = torch.randn(H, D, device=dev, generator=g_layer).half()
-        g_rank = torch.Generator(device=dev).manual_seed(a.seed * 100000 + layer * 100 + rank)
-        kv = torch.empty(cap, 2, P, H, D, dtype=torch.float16, device=dev)
-        meta = torch.empty(mcap, 2, P, H, D, dtype=torch.float16, device=dev)
-        vlog = torch.zeros(cap, H, dtype=torch.float16, device=dev)
-        kv_idx = torch.arange(n_local, dtype=torch.int32, device=dev)
-        meta_idx = torch.arange(mcap, dtype=torch.int32, device=dev)
-        t0, t1 = lo * P, min(hi * P, S)
-        if t1 > t0:
-            Kc = (torch.randn(t1 - t0, H, D, device=dev, generator=g_rank) * scale).half()
-            Vc = torch.randn(t1 - t0, H, D, device=dev, generator=g_rank).half()
-            n_pref = -(-(t1 - t0) // P)
-            _lib.call("aoakv_append_kv_cache_prefill", Kc.data_ptr(), Vc.data_ptr(), t1 - t0,
-                      kv.data_ptr(), kv_idx.data_ptr(), n_pref, (t1 - t0 - 1) % P + 1, cap,
-                      meta.data_ptr(), meta_idx.data_ptr(), -(-n_pref // P),
-                      (n_pref - 1) % P + 1, mcap, vlog.data_ptr(), H, D, P, _lib.LAYOUT_NHD,
-                      torch.cuda.current_stream().cuda_stream)
-            del Kc, Vc
-        layers.append(sharded.ShardLayer(kv=kv, meta=meta, vlog=vlog, kv_idx=kv_idx,
-                                         meta_idx=meta_idx, page_lo=lo, n_local=n_local,
-                                         n_total=n_total, last_len=last_len, owns_last=owns,
-                                         last_phys=n_local - 1 if owns else -1))
-        news.append((q, k_new, v_new))
-    torch.cuda.synchronize()
-    dec = sharded.ShardedDecoder(group, H, D, P, a.budget // P, a.method)
-
-    def one_step():
-        for lay, (q, k, v) in zip(layers, news):
-            dec.step(lay, q, k, v)
-
-    s = torch.cuda.Stream(device=dev)
-    s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        one_step()  # workspaces and kernel attributes outside capture
-    torch.cuda.current_stream().wait_stream(s)
-    torch.cuda.synchronize()
-    graph = None
-    if not a.no_graph:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            one_step()
-    def run():
-        if graph is not None:
-            graph.replay()
-        else:
-            one_step()
-
-    for _ in range(a.warmup):
-        run()
-    torch.cuda.synchronize()
-    _lib.check_device()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(a.steps):
-        run()
-    ev1.record()
-    torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    _lib.check_device()
-    us = ms * 1e3 / (a.steps * a.layers)
-    sb = step_bytes(a)
-    peaks = {}
-    try:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except (OSError, ValueError):
-        pass
-    peak = float(peaks.get("hbm_gbs") or 6650.0)
-    ach = sb / (us * 1e-6) / 1e9
-    ks = min(a.budget // P, n_total) - 1
-    if rank == 0:
-        print(json.dumps({
-            "metric": LONG_METRIC, "value": round(us, 3), "unit": "us", "n_gpus": world,
-            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4),
-            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
-            "data": "synthetic",
-            "config": {"workload": f"1 request, {a.layers}-layer decode step, ctx {S}, budget "
-                                   f"{a.budget}, pages split by range over {world} GPU(s)",
-                       "context_tokens": S, "token_budget": a.budget, "page_size": P,
-                       "num_heads": H, "head_dim": D, "layers_per_step": a.layers,
-                       "score_mode": a.method, "pages_per_gpu": n_local,
-                       "exchange_bytes_per_layer_per_gpu": world * H * ks * 8 +
-                       world * H * (D + 1) * 4,
-                       "graph": graph is not None,
-                       "parallelism": f"page-range x{world}, all_gather of candidates and "
-                                      f"partial states (NCCL)" if world > 1 else "1 GPU"},
-            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak * world,
-                         "unit": "GB/s", "frac": round(ach / (peak * world), 4),
-                         "algorithmic_bytes": sb, "avg_layer_us": round(us, 3),
-                         "note": "peak = measured HBM GB/s x GPUs"},
-        }), flush=True)
-    # a graph that holds NCCL calls must be released before the process
-    # group, or the exit waits for ever
-    graph = None
-    import gc
-    gc.collect()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
 # ------------------------------------------------------ batched decode
-BATCH_METRIC = "sparse-decode µs/layer for a batch of 32 requests (4K-16K ctx, 1K budget)"
-
-
-def run_batched(a):
-    """Config 4: a.requests independent requests, context U[4096, 16384]
-    tokens in whole pages (seed 3), budget a.budget, balanced over the job's
-    GPUs by bytes (aoa_kv_b200.batching); each GPU runs its requests' steps
-    (one fused launch per request and layer) in a CUDA graph. No collective
-    on the data path; the total work is fixed: scaling "strong"."""
-    import datetime
-
+def batched_key(a, world, rank, dev, peak):
+    """Config 4: a.requests requests, context U[4096, 16384] tokens in whole
+    pages (seed 3), budget a.budget, balanced over the GPUs by bytes
+    (aoa_kv_b200.batching); each GPU keeps its requests in one pool per
+    layer and runs ONE aoakv_decode_step_batched launch per layer. No
+    collective; fixed total work: strong scaling. Checked on rank 0 against
+    one StepPlan run per request (layer 0)."""
     import numpy as np
     import torch
-    import torch.distributed as dist
 
-    import aoa_kv_b200 as ak
-    from aoa_kv_b200 import batching
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    ak._lib.load()
+    from aoa_kv_b200 import StepPlan, _lib, batching
+    L = a.extra_layers
     g = np.random.default_rng(3)
     ctxs = [int(c) * P for c in g.integers(4096 // P, 16384 // P + 1, size=a.requests)]
     weights = [batching.step_bytes(c, a.budget, H, D, P, a.method) for c in ctxs]
     mine = batching.balance_requests(weights, world)[rank]
-    reqs = []
-    for r in mine:
-        gen = torch.Generator(device=dev).manual_seed(3000 + r)
-        S = ctxs[r]
-        ctl = ak.InferenceController(a.layers, H, D, P, a.budget // P, S + P, torch.float16, dev,
-                                     method=a.method)
-        ctl.prepare_metadata(S - 1)
-        ctl.begin_forward(S - 1)
-        news = []
-        for layer in range(a.layers):
+    R = len(mine)
+    pages = [-(-ctxs[r] // P) for r in mine]
+    n_all = sum(pages)
+    kv_indptr = np.concatenate([[0], np.cumsum(pages)]).astype(np.int32)
+    mp = [-(-n // P) for n in pages]
+    meta_indptr = np.concatenate([[0], np.cumsum(mp)]).astype(np.int32)
+    last = np.array([(ctxs[r] - 1) % P + 1 for r in mine], np.int32)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def dev_i32(x):
+        return torch.from_numpy(np.ascontiguousarray(x, dtype=np.int32)).to(dev)
+    kv_indptr_d, meta_indptr_d, last_d = dev_i32(kv_indptr), dev_i32(meta_indptr), dev_i32(last)
+    kv_tab = torch.arange(n_all, dtype=torch.int32, device=dev)
+    meta_tab = torch.arange(int(meta_indptr[-1]), dtype=torch.int32, device=dev)
+    pools, qkv = [], []
+    for layer in range(L):
+        kv = torch.empty(n_all + 1, 2, P, H, D, dtype=torch.float16, device=dev)
+        meta = torch.empty(int(meta_indptr[-1]) + 1, 2, P, H, D, dtype=torch.float16, device=dev)
+        vlog = torch.zeros(n_all + 1, H, dtype=torch.float16, device=dev)
+        q_l = torch.empty(R, H, D, dtype=torch.float16, device=dev)
+        k_l, v_l = torch.empty_like(q_l), torch.empty_like(q_l)
+        for i, r in enumerate(mine):
+            gen = torch.Generator(device=dev).manual_seed(3000 + 100 * r + layer)
+            S = ctxs[r]
             scale = torch.exp(torch.randn(H, D, device=dev, generator=gen))
             K = (torch.randn(S, H, D, device=dev, generator=gen) * scale).half()
             V = torch.randn(S, H, D, device=dev, generator=gen).half()
-            q = torch.randn(1, H, D, device=dev, generator=gen).half()
-            ak.append_kv(K[:-1].contiguous(), V[:-1].contiguous(), ctl, layer)
-            news.append((q, K[-1:].contiguous(), V[-1:].contiguous(),
-                         torch.empty(1, H, D, dtype=torch.float16, device=dev)))
+            q_l[i] = torch.randn(H, D, device=dev, generator=gen).half()
+            k_l[i], v_l[i] = K[S - 1], V[S - 1]
+            p0, m0 = int(kv_indptr[i]), int(meta_indptr[i])
+            _prefill(K, V, 0, S - 1, kv, kv_tab[p0:], meta, meta_tab[m0:], vlog, stream)
             del K, V
-        ctl.end_forward()
-        ctl.prepare_metadata(1)
-        ctl.begin_forward(1)
-        reqs.append((ctl, news))
+        pools.append((kv, meta, vlog))
+        qkv.append((q_l, k_l, v_l))
     torch.cuda.synchronize()
-
-    n_streams = max(1, min(a.streams, len(reqs)))
-    sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    cap = 0 if n_streams == 1 else max(64, (2 * sms // n_streams) // 2 * 2)
-    lanes = [torch.cuda.Stream(device=dev) for _ in range(n_streams)]
-    order = sorted(range(len(reqs)), key=lambda i: -weights[mine[i]])
-    lane_of = {i: j % n_streams for j, i in enumerate(order)}
+    o = torch.empty(L, R, H, D, dtype=torch.float16, device=dev)
+    max_pages = max(pages) if pages else 1
 
     def one_step():
-        # fork: every lane waits for the issuing stream; join at the end
-        main = torch.cuda.current_stream()
-        for ln in lanes:
-            ln.wait_stream(main)
-        for layer in range(a.layers):
-            for i, (ctl, news) in enumerate(reqs):
-                q, k, v, o = news[layer]
-                with torch.cuda.stream(lanes[lane_of[i]]):
-                    ctl.decode_step(q, k, v, layer, out=o, max_ctas=cap)
-        for ln in lanes:
-            main.wait_stream(ln)
-
-    s = torch.cuda.Stream(device=dev)
-    s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        one_step()
-    torch.cuda.current_stream().wait_stream(s)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        one_step()
-    for _ in range(a.warmup):
-        graph.replay()
-    torch.cuda.synchronize()
-    ak.check_device()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(a.steps):
-        graph.replay()
-    ev1.record()
-    torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    ak.check_device()
-    us = ms * 1e3 / (a.steps * a.layers)
-    total_bytes = sum(weights)
-    peaks = {}
-    try:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except (OSError, ValueError):
-        pass
-    peak = float(peaks.get("hbm_gbs") or 6650.0)
-    ach = total_bytes / (us * 1e-6) / 1e9
-    if rank == 0:
-        print(json.dumps({
-            "metric": BATCH_METRIC.replace("32 requests", f"{a.requests} requests"),
-            "value": round(us, 3), "unit": "us", "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4), "higher_is_better": False,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": f"{a.requests} requests, ctx U[4096,16384] tokens (seed 3), "
-                                   f"budget {a.budget}, {a.layers}-layer step",
-                       "requests_on_rank0": len(mine), "bytes_per_layer_step": total_bytes,
-                       "streams": n_streams, "ctas_per_step": cap or "whole GPU",
-                       "parallelism": f"request-sharded x{world} (greedy byte balance), "
-                                      f"no collective"},
-            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak * world,
-                         "unit": "GB/s", "frac": round(ach / (peak * world), 4),
-                         "note": "peak = measured HBM GB/s x GPUs"},
-        }), flush=True)
+        for layer in range(L):
+            kv, meta, vlog = pools[layer]
+            q_l, k_l, v_l = qkv[layer]
+            batching.decode_step_batched(q_l, k_l, v_l, o[layer], kv, kv_indptr_d, kv_tab, last_d,
+                                         meta, meta_indptr_d, meta_tab, vlog, max_pages,
+                                         a.budget // P, a.method)
+    ms = 0.0
+    steps = max(10, a.steps // 2)
+    graph = None
+    if R:
+        graph = capture(one_step, dev)
+        ms = time_replays(graph.replay, steps, a.warmup, world, dev)
+    else:
+        ms = time_replays(lambda: None, steps, 0, world, dev)
+    _lib.check_device()
+    us = ms * 1e3 / (steps * L)
+    err = None
+    if rank == 0 and R:
+        kv, meta, vlog = pools[0]
+        q_l, k_l, v_l = qkv[0]
+        o_one = torch.empty(H, D, dtype=torch.float16, device=dev)
+        mode = _lib.SCORE_AOAKV if a.method == "aoakv" else _lib.SCORE_QUEST
+        plan = StepPlan(kv, kv.shape[0], meta, meta.shape[0], vlog, H, D, P, a.budget // P, mode,
+                        max_pages=max_pages)
+        err = 0.0
+        for i in range(R):
+            p0, m0 = int(kv_indptr[i]), int(meta_indptr[i])
+            plan.run(q_l[i], k_l[i], v_l[i], o_one, kv_tab[p0:].data_ptr(), pages[i],
+                     int(last[i]), meta_tab[m0:].data_ptr(), None, None, 0, stream)
+            torch.cuda.synchronize()
+            err = max(err, float((o_one.float() - o[0, i].float()).abs().max()))
+        plan.close()
+    mine_bytes = sum(weights[r] for r in mine)
+    got = gather_ints([mine_bytes, R], world, dev)
+    per_gpu, per_req = [x[0] for x in got], [x[1] for x in got]
     del graph
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    torch.cuda.synchronize()
+    if rank != 0:
+        return None
+    total = sum(weights)
+    return {
+        "metric": f"sparse-decode µs/layer for a batch of {a.requests} requests (4K-16K ctx, "
+                  f"{a.budget} budget) (config 4)",
+        "value": round(us, 3), "unit": "us", "n_gpus": world, "scaling": "strong",
+        "steps": steps, "layers_per_step": L,
+        "roofline": roof(total, us, peak, world),
+        "max_gpu_bytes": max(per_gpu), "per_gpu_bytes": per_gpu, "requests_per_gpu": per_req,
+        "max_abs_err": err,
+        "checked_against": "one StepPlan step per request on the same pool (layer 0, rank 0)",
+        "gpu_launches": L * steps,
+        "config": {"workload": f"{a.requests} requests, ctx U[4096,16384] tokens in whole pages "
+                               f"(seed 3), budget {a.budget}, {L}-layer step, outlier K",
+                   "bytes_per_layer_step": total,
+                   "parallelism": f"request-sharded x{world} (greedy byte balance), no "
+                                  f"collective; one batched launch per layer per GPU"},
+    }
+
+
+# ------------------------------------------------- config 5 prefill build
+def prefill_key(a, world, rank, dev, peak):
+    """Config 5's prefill: aoakv_append_kv_cache_prefill of a.long_ctx - 1
+    tokens of one layer in one pass (KV pages, key max/min metadata of every
+    page, v_log_norm of every full page). Bytes: K and V read and written
+    once, the metadata and v_log_norm written."""
+    import torch
+
+    from aoa_kv_b200 import _lib
+    S = a.long_ctx - 1
+    n_pages = -(-S // P)
+    g = torch.Generator(device=dev).manual_seed(4)
+    K = torch.randn(S, H, D, device=dev, generator=g).half()
+    V = torch.randn(S, H, D, device=dev, generator=g).half()
+    kv, meta, vlog, kv_idx, meta_idx = _pool(n_pages, dev)
+
+    def run():
+        _prefill(K, V, 0, S, kv, kv_idx, meta, meta_idx, vlog,
+                 torch.cuda.current_stream().cuda_stream)
+    steps = 10
+    ms = time_replays(run, steps, 3, world, dev)
+    _lib.check_device()
+    us = ms * 1e3 / steps
+    kvb = S * H * D * 2 * 2
+    b = 2 * kvb + n_pages * 2 * H * D * 2 + (S // P) * H * 2
+    return {"metric": f"prefill page build µs for {S} tokens (config 5)", "value": round(us, 1),
+            "unit": "us", "roofline": roof(b, us, peak), "gpu_launches": steps,
+            "config": {"tokens": S, "pages": n_pages,
+                       "bytes": "K,V read + KV pages written + key max/min metadata written + "
+                                "v_log_norm written",
+                       "inputs": "q,K,V~N(0,1) seed 4; 4.4 GB per call > L2"}}
+
+
+# ------------------------------------------------------ config 2, 8192
+def config2_key(a, world, rank, dev, peak):
+    """Config 2 at 8192 tokens, budget 1024 (outlier K, seed 1): each kernel
+    alone over 8 layers (8 x 25 MB > L2) and the step as one launch and as
+    the four-kernel chain, µs per layer."""
+    import torch
+
+    from aoa_kv_b200 import StepPlan, _lib
+    ctx, budget, L = 8192, 1024, 8
+    ctl, news = setup_layers(ctx, L, budget, 1, a.method, dev)
+    n = len(ctl.kv_cache.indicies)
+    kp = budget // P
+    o = torch.empty(L, H, D, dtype=torch.float16, device=dev)
+    scores = torch.empty(L, H, n, dtype=torch.float32, device=dev)
+    sel = torch.empty(L, H, kp - 1, dtype=torch.int32, device=dev)
+    ws_n = _lib.size_query("aoakv_decode_workspace_size", H, D, kp - 1)
+    ws = torch.zeros(ws_n, dtype=torch.uint8, device=dev)
+    sws = ctl._ensure_step_workspace()
+    chain = []
+    for layer in range(L):
+        kv_p, kv_cap, meta_p, meta_cap, vlog_p = ctl._layer_buffers(layer)
+        chain.append(StepPlan(kv_p, kv_cap, meta_p, meta_cap, vlog_p, H, D, P, kp,
+                              ctl.score_mode, chain=True))
+
+    def st():
+        return torch.cuda.current_stream().cuda_stream
+
+    def k_append():
+        for layer, (q, k, v) in enumerate(news):
+            kv_p, kv_cap, meta_p, meta_cap, vlog_p = ctl._layer_buffers(layer)
+            _lib.call("aoakv_append_kv_cache_decode", k.data_ptr(), v.data_ptr(), kv_p,
+                      ctl.kv_indices_with_last.data_ptr(), n, ctl.kv_cache.last_page_len, kv_cap,
+                      meta_p, ctl.metadata_indices.data_ptr(), len(ctl.metadata_cache.indicies),
+                      ctl.metadata_cache.last_page_len, meta_cap, vlog_p, H, D, P, 0, st())
+
+    def k_estimate():
+        for layer, (q, _, _) in enumerate(news):
+            kv_p, kv_cap, meta_p, meta_cap, vlog_p = ctl._layer_buffers(layer)
+            _lib.call("aoakv_estimate_attn_score", q.data_ptr(), scores[layer].data_ptr(), 1, n,
+                      meta_p, ctl.metadata_indices.data_ptr(), len(ctl.metadata_cache.indicies),
+                      ctl.metadata_cache.last_page_len, meta_cap,
+                      ctl.kv_indices_with_last.data_ptr(), kv_cap, vlog_p, H, D, P, 0,
+                      ctl.score_mode, st())
+
+    def k_topk():
+        for layer in range(L):
+            _lib.call("aoakv_topk_filtering", scores[layer].data_ptr(), 1, n,
+                      ctl.kv_indices_with_last.data_ptr(), 0, H, n - 1, kp - 1, None, 0,
+                      sel[layer].data_ptr(), kp - 1, 0, st())
+
+    def k_decode():
+        for layer, (q, _, _) in enumerate(news):
+            kv_p, kv_cap, _, _, _ = ctl._layer_buffers(layer)
+            _lib.call("aoakv_sparse_decode", q.data_ptr(), o[layer].data_ptr(), kv_p, kv_cap,
+                      sel[layer].data_ptr(), kp - 1, kp - 1, ctl.kv_cache.indicies[-1],
+                      ctl.kv_cache.last_page_len, H, D, P, 0, 0.0, ws.data_ptr(), ws_n, st())
+
+    def fused():
+        for layer, (q, k, v) in enumerate(news):
+            ctl.decode_step(q, k, v, layer, out=o[layer])
+
+    def chained():
+        for layer, (q, k, v) in enumerate(news):
+            chain[layer].run(q, k, v, o[layer], ctl.kv_indices_with_last, n,
+                             ctl.kv_cache.last_page_len, ctl.metadata_indices, None, sws,
+                             sws.numel(), st())
+    row = 2 * D * 2 + (2 if a.method == "aoakv" else 0)
+    parts = {
+        "append_decode": (k_append, 2 * H * D * 2 + 2 * H * D * 2 * 2),
+        "estimate": (k_estimate, estimate_bytes(ctx, a.method)),
+        "topk": (k_topk, H * (n - 1) * 4 + H * (kp - 1) * 4),
+        "sparse_decode": (k_decode, kp * P * H * D * 2 * 2 + 2 * H * D * 2 + H * (kp - 1) * 4),
+        "step_one_launch": (fused, step_bytes(ctx, budget, a.method)),
+        "step_chain": (chained, step_bytes(ctx, budget, a.method)),
+    }
+    k_append()  # the token's page holds it before the timings (all idempotent)
+    k_estimate()
+    k_topk()
+    out = {"metric": "µs per layer at 8192 ctx, 1K budget (config 2)",
+           "config": {"workload": f"{L} layers x ctx {ctx}, budget {budget}, outlier K seed 1, "
+                                  f"{a.method}; each launch over its layers in one CUDA graph",
+                      "scored_bytes_per_page": H * row}}
+    launches = 0
+    steps = max(10, a.steps // 2)
+    for name, (fn, b) in parts.items():
+        g = capture(fn, dev)
+        ms = time_replays(g.replay, steps, 3, world, dev)
+        us = ms * 1e3 / (steps * L)
+        out[name] = {"us": round(us, 3), **roof(b, us, peak)}
+        launches += steps * L * (4 if name == "step_chain" else 1)
+        del g
+    _lib.check_device()
+    out["gpu_launches"] = launches
+    for p in chain:
+        p.close()
+    ctl.clean_states()
+    return out
+
+
+def run_single(a, key):
+    world, rank, local = dist_env()
+    dev = init_gpu(world, local)
+    from aoa_kv_b200 import _lib
+    _lib.load()
+    peak, _ = load_peak()
+    fn = longctx_key if key == "longctx" else batched_key
+    val = fn(a, world, rank, dev, peak)
+    if rank == 0:
+        line = dict(val)
+        line.update({"warmup": a.warmup, "higher_is_better": False, "vs_baseline": None,
+                     "dtype": "f16", "data": "synthetic", "ms_per_step":
+                     round(val["value"] * val["layers_per_step"] / 1e3, 4)})
+        print(json.dumps(line), flush=True)
+    finish(world)
 
 
 # ------------------------------------------- Llama-2-7B-shaped decode step
@@ -799,21 +1017,20 @@ def run_model(a):
     """Config 3: one decode token through a 32-layer Llama-2-7B-shaped model
     with random fp16 weights (hidden 4096, 32 heads, head_dim 128, MLP 11008,
     vocab 32000): RMSNorm, q/k/v GEMVs, RoPE (aoakv_apply_rope_in_place),
-    attention through
-    InferenceController.decode_step (layers 0-1 dense, as in the reference's
-    skip layers, llama.py:428-439; the rest with the token budget), o_proj,
-    SwiGLU MLP, final norm, LM head and a device-side argmax, captured in one
-    CUDA graph. The KV caches hold a.ctx synthetic tokens per layer. The
-    GEMVs are torch (cuBLAS); the attention share is timed separately by
-    replaying a graph of only the attention calls."""
+    attention through InferenceController.decode_step (layers 0-1 dense, as
+    in the reference's skip layers, llama.py:428-439; the rest with the token
+    budget), o_proj, SwiGLU MLP, final norm, LM head and a device-side argmax,
+    captured in one CUDA graph; contexts 16384 and 32768 x budgets
+    512/1024/2048/4096 (KV ~ N(0,1), seed 2). The GEMVs are torch (cuBLAS);
+    the attention share is timed by replaying a graph of only the attention
+    calls."""
     import torch
 
     import aoa_kv_b200 as ak
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(dev)
+    dev = init_gpu(1, int(os.environ.get("LOCAL_RANK", "0")))
     ak._lib.load()
     L, HID, FF, VOCAB = 32, 4096, 11008, 32000
-    gen = torch.Generator(device=dev).manual_seed(a.seed)
+    gen = torch.Generator(device=dev).manual_seed(2)
 
     def w(*shape):
         return (torch.randn(*shape, device=dev, generator=gen) * 0.02).half()
@@ -826,118 +1043,96 @@ def run_model(a):
     norm_f = torch.ones(HID, device=dev, dtype=torch.float16)
     weight_bytes = sum(t.numel() * 2 for lw in layers for t in lw.values()) + \
         (emb.numel() + lm_head.numel() + norm_f.numel()) * 2
-
-    S = a.ctx
-    ctl = ak.InferenceController(L, H, D, P, a.budget // P, S + P, torch.float16, dev,
-                                 method=a.method)
-    ctl.prepare_metadata(S - 1)
-    ctl.begin_forward(S - 1)
-    for layer in range(L):
-        scale = torch.exp(torch.randn(H, D, device=dev, generator=gen))
-        K = (torch.randn(S - 1, H, D, device=dev, generator=gen) * scale).half()
-        V = torch.randn(S - 1, H, D, device=dev, generator=gen).half()
-        ak.append_kv(K, V, ctl, layer)
-        del K, V
-    ctl.end_forward()
-    ctl.prepare_metadata(1)
-    ctl.begin_forward(1)
-    dense_budget = ctl.kv_cache.pool.capacity  # layers 0-1: every page
-    sparse_budget = a.budget // P
-
+    peak, _ = load_peak()
 
     def rmsnorm(x, g):
         xf = x.float()
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5)).half() * g
 
-    token = torch.zeros(1, dtype=torch.long, device=dev)
-    q_buf = torch.empty(L, 1, H, D, dtype=torch.float16, device=dev)
-    k_buf = torch.empty_like(q_buf)
-    v_buf = torch.empty_like(q_buf)
-    o_buf = torch.empty_like(q_buf)
-    for layer in (0, 1):  # size the step workspace for the dense layers outside capture
-        ctl.set_page_budget(dense_budget)
-        ctl._ensure_step_workspace()
-    ctl.set_page_budget(sparse_budget)
-
-    def attention(layer):
-        ctl.set_page_budget(dense_budget if layer < 2 else sparse_budget)
-        ctl.decode_step(q_buf[layer], k_buf[layer], v_buf[layer], layer, out=o_buf[layer])
-
-    def token_step():
-        x = emb[token]  # [1, HID]
-        for layer, lw in enumerate(layers):
-            h = rmsnorm(x, lw["ln1"])
-            q_buf[layer].copy_((h @ lw["wq"]).view(1, H, D))
-            k_buf[layer].copy_((h @ lw["wk"]).view(1, H, D))
-            v_buf[layer].copy_((h @ lw["wv"]).view(1, H, D))
-            # RoPE at the new token's position (this library's kernel)
-            ak.apply_rope_in_place(q_buf[layer], k_buf[layer], S - 1)
-            attention(layer)
-            x = x + o_buf[layer].view(1, HID) @ lw["wo"]
-            h = rmsnorm(x, lw["ln2"])
-            x = x + (torch.nn.functional.silu(h @ lw["wg"]) * (h @ lw["wu"])) @ lw["wd"]
-        logits = rmsnorm(x, norm_f) @ lm_head
-        token.copy_(logits.argmax(dim=-1))
-
-    def attention_only():
+    results = []
+    for S in (16384, 32768):
+        ctl = ak.InferenceController(L, H, D, P, 4096 // P, S + P, torch.float16, dev,
+                                     method=a.method)
+        ctl.prepare_metadata(S - 1)
+        ctl.begin_forward(S - 1)
         for layer in range(L):
-            attention(layer)
+            K = torch.randn(S - 1, H, D, device=dev, generator=gen).half()
+            V = torch.randn(S - 1, H, D, device=dev, generator=gen).half()
+            ak.append_kv(K, V, ctl, layer)
+            del K, V
+        ctl.end_forward()
+        ctl.prepare_metadata(1)
+        ctl.begin_forward(1)
+        dense_budget = ctl.kv_cache.pool.capacity  # layers 0-1: every page
+        token = torch.zeros(1, dtype=torch.long, device=dev)
+        q_buf = torch.empty(L, 1, H, D, dtype=torch.float16, device=dev)
+        k_buf, v_buf, o_buf = (torch.empty_like(q_buf) for _ in range(3))
+        for budget in (512, 1024, 2048, 4096):
+            sparse_budget = budget // P
+            ctl.set_page_budget(dense_budget)
+            ctl._ensure_step_workspace()
+            ctl.set_page_budget(sparse_budget)
 
-    s = torch.cuda.Stream(device=dev)
-    s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        token_step()
-        attention_only()
-    torch.cuda.current_stream().wait_stream(s)
-    torch.cuda.synchronize()
-    g_tok, g_att = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_tok):
-        token_step()
-    with torch.cuda.graph(g_att):
-        attention_only()
+            def attention(layer):
+                ctl.set_page_budget(dense_budget if layer < 2 else sparse_budget)
+                ctl.decode_step(q_buf[layer], k_buf[layer], v_buf[layer], layer,
+                                out=o_buf[layer])
 
-    def timed(graph):
-        for _ in range(a.warmup):
-            graph.replay()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(a.steps):
-            graph.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / a.steps
+            def token_step():
+                x = emb[token]  # [1, HID]
+                for layer, lw in enumerate(layers):
+                    h = rmsnorm(x, lw["ln1"])
+                    q_buf[layer].copy_((h @ lw["wq"]).view(1, H, D))
+                    k_buf[layer].copy_((h @ lw["wk"]).view(1, H, D))
+                    v_buf[layer].copy_((h @ lw["wv"]).view(1, H, D))
+                    ak.apply_rope_in_place(q_buf[layer], k_buf[layer], S - 1)
+                    attention(layer)
+                    x = x + o_buf[layer].view(1, HID) @ lw["wo"]
+                    h = rmsnorm(x, lw["ln2"])
+                    x = x + (torch.nn.functional.silu(h @ lw["wg"]) * (h @ lw["wu"])) @ lw["wd"]
+                logits = rmsnorm(x, norm_f) @ lm_head
+                token.copy_(logits.argmax(dim=-1))
 
-    ms_tok = timed(g_tok)
-    ms_att = timed(g_att)
-    ak.check_device()
+            def attention_only():
+                for layer in range(L):
+                    attention(layer)
+            g_tok, g_att = capture(token_step, dev), capture(attention_only, dev)
+            ms_tok = time_replays(g_tok.replay, a.steps, a.warmup, 1, dev) / a.steps
+            ms_att = time_replays(g_att.replay, a.steps, a.warmup, 1, dev) / a.steps
+            ak.check_device()
+            att_bytes = 2 * step_bytes(S, S) + (L - 2) * step_bytes(S, budget)
+            results.append({"context": S, "budget": budget, "ms_per_token": round(ms_tok, 4),
+                            "attention_ms_per_token": round(ms_att, 4),
+                            "attention_share": round(ms_att / ms_tok, 4),
+                            "attention_roofline": roof(att_bytes, ms_att * 1e3, peak)})
+            del g_tok, g_att
+        ctl.clean_states()
+        del ctl
+        torch.cuda.empty_cache()
+    head = next(r for r in results if r["context"] == 32768 and r["budget"] == 1024)
     print(json.dumps({
-        "metric": MODEL_METRIC, "value": round(ms_tok, 4), "unit": "ms", "n_gpus": 1,
-        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_tok, 4),
+        "metric": MODEL_METRIC, "value": head["ms_per_token"], "unit": "ms", "n_gpus": 1,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": head["ms_per_token"],
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic",
-        "config": {"workload": f"Llama-2-7B-shaped decode, random weights, ctx {S}, "
-                               f"budget {a.budget}, layers 0-1 dense",
-                   "weight_bytes": weight_bytes, "context_tokens": S, "token_budget": a.budget},
-        "attention_ms_per_token": round(ms_att, 4),
-        "attention_share": round(ms_att / ms_tok, 4),
-        "weights_ideal_ms": round(weight_bytes / (6452.2e9) * 1e3, 4),
+        "config": {"workload": "Llama-2-7B-shaped decode, random weights, KV~N(0,1) seed 2, "
+                               "layers 0-1 dense; value at ctx 32768, budget 1024",
+                   "weight_bytes": weight_bytes},
+        "sweep": results,
+        "weights_ideal_ms": round(weight_bytes / (peak * 1e9) * 1e3, 4),
     }), flush=True)
-    del g_tok, g_att
 
 
 def main():
     a = parse()
     if a.impl == "reference":
         run_reference(a)
-    elif a.mode == "longctx":
-        run_longctx(a)
-    elif a.mode == "batched":
-        run_batched(a)
+    elif a.mode in ("longctx", "batched"):
+        run_single(a, a.mode)
     elif a.mode == "model":
         run_model(a)
     else:
-        run_ours(a)
+        run_headline(a)
 
 
 if __name__ == "__main__":

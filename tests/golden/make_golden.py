@@ -1,7 +1,8 @@
 """Writes the golden vectors in tests/golden/*.npz from the reference's OWN code.
 
-Run where the reference checkout exists (its path in AOAKV_REFERENCE, or the
-built-in default):  python tests/golden/make_golden.py
+Run where the reference checkout exists, giving its root as the first
+argument or in AOAKV_REFERENCE:
+    python tests/golden/make_golden.py <reference checkout>
 
 Semantics A (``sim_*.npz``): the reference simulation — the real
 filtering/filter_util.py functions (imported, not copied) driven by the decode
@@ -38,8 +39,8 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
 from gen import digest, gen_qkv  # noqa: E402
 
-REF = Path(os.environ.get("AOAKV_REFERENCE", "/root/reference"))
-TESTS = REF / "kernels" / "aoa_kv" / "quest" / "tests"
+REF: Path  # the reference checkout's root, set by main()
+TESTS: Path  # its kernels/aoa_kv/quest/tests
 
 SIM_CASES = [
     # name, seed, H, S, D, P, token_budget, method, fixed, dist
@@ -137,6 +138,14 @@ def save(name, meta, **arrays):
 
 
 def main():
+    global REF, TESTS
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("AOAKV_REFERENCE")
+    if not root:
+        sys.exit("usage: make_golden.py <reference checkout> (or set AOAKV_REFERENCE)")
+    REF = Path(root).resolve()
+    TESTS = REF / "kernels" / "aoa_kv" / "quest" / "tests"
+    if not (REF / "filtering" / "filter_util.py").is_file():
+        sys.exit(f"{REF}: no filtering/filter_util.py (not the reference checkout)")
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     fu = load_filter_util()
     for name, seed, H, S, D, P, budget, method, fixed, dist in SIM_CASES:
