@@ -85,16 +85,22 @@ __host__ __device__ inline int cs_slot_bytes(int D, int P) {
   const int b = score > dec ? score : dec;
   return (b + 1023) / 1024 * 1024;
 }
-__host__ __device__ inline int cs_capl(int C) { return kCsGather / C; }
+// Local candidates one CTA may publish: its share of the gathered lists,
+// but no more than twice the attended slots (at least kCsMaxCand), so a
+// small cluster does not spend shared memory on lists it cannot fill.
+__host__ __device__ inline int cs_capl(int C, int max_slots) {
+  const int want = 2 * max_slots > kCsMaxCand ? 2 * max_slots : kCsMaxCand;
+  return kCsGather / C < want ? kCsGather / C : want;
+}
 __host__ __device__ inline int cs_max_items(int C, int max_slots) {
-  const int a = cs_capl(C) + 2, b = (max_slots + C - 1) / C;
+  const int a = cs_capl(C, max_slots) + 2, b = (max_slots + C - 1) / C;
   return a > b ? a : b;
 }
 
 __host__ __device__ inline CsLayout cs_layout(int D, int P, int C, int max_local,
                                               int max_slots) {
   CsLayout L;
-  const int capl = cs_capl(C);
+  const int capl = cs_capl(C, max_slots);
   const int capx = capl > kCsMaxCand ? capl : kCsMaxCand;
   int off = 0;
   L.ring = off;  // one TMA slot per warp: metadata pages, then K/V pages
@@ -458,7 +464,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
                         const __grid_constant__ CUtensorMap meta_map, ClusterStepArgs a_in,
                         CsShape shp) {
   constexpr int CPL = D / 32;           // channels per lane
-  constexpr int CAPL = kCsGather / C;   // local candidates one CTA may publish
+  const int CAPL = cs_capl(C, shp.max_slots);  // local candidates one CTA may publish
   using Vec = typename LaneVec<CPL>::T;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
