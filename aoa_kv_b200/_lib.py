@@ -68,6 +68,10 @@ SIGNATURES = {
     "aoakv_decode_step_batched": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_p, _c_p, _c_p, _c_p,
                                   _c_i32, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                                   _c_i32, _c_i32, _c_i32, _c_p, _c_p],
+    "aoakv_shard_propose": [_c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_p],
+    "aoakv_shard_finish": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_p,
+                           _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_p],
+    "aoakv_merge_packed_states": [_c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p],
     "aoakv_decode_step_grid": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p,
                                _c_p, _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                                _c_i32, _c_p, _c_p, _c_size, _c_i32, _c_p],

@@ -39,6 +39,29 @@ __global__ void merge_states_kernel(const float* o_parts, const float* lse_parts
   }
 }
 
+// The same merge over states packed as the sharded step exchanges them:
+// states[g, h] = {o[D], lse}.
+__global__ void merge_packed_kernel(const float* states, int G, int H, int D, __half* o) {
+  const int h = blockIdx.x;
+  const size_t row = static_cast<size_t>(D) + 1;
+  float m = -INFINITY;
+  for (int g = 0; g < G; ++g) m = fmaxf(m, states[(static_cast<size_t>(g) * H + h) * row + D]);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f, sum = 0.f;
+    if (m != -INFINITY) {
+      for (int g = 0; g < G; ++g) {
+        const float* st = states + (static_cast<size_t>(g) * H + h) * row;
+        const float l = st[D];
+        if (l == -INFINITY) continue;
+        const float w = expf(l - m);
+        sum += w;
+        acc += w * st[d];
+      }
+    }
+    o[static_cast<size_t>(h) * D + d] = __float2half_rn(sum > 0.f ? acc / sum : 0.f);
+  }
+}
+
 __global__ void map_pages_kernel(const int32_t* ids, int64_t count, int32_t lo, int32_t n_local,
                                  const int32_t* local, int32_t* out) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
@@ -80,5 +103,19 @@ extern "C" int aoakv_merge_states(const float* o_parts, const float* lse_parts,
   merge_states_kernel<<<num_heads, threads, 0, static_cast<cudaStream_t>(stream)>>>(
       o_parts, lse_parts, num_parts, num_heads, head_dim, static_cast<__half*>(o), lse_out);
   AOAKV_CUDA_TRY(cudaGetLastError(), "merge_states launch");
+  return AOAKV_OK;
+}
+
+extern "C" int aoakv_merge_packed_states(const float* states, int32_t num_parts,
+                                         int32_t num_heads, int32_t head_dim, void* o,
+                                         void* stream) {
+  AOAKV_NVTX("aoakv_merge_packed_states");
+  AOAKV_CHECK_ARG(states && o, "merge_packed_states: NULL pointer argument");
+  AOAKV_CHECK_ARG(num_parts >= 1 && num_heads >= 1 && head_dim >= 1 && head_dim <= 1024,
+                  "merge_packed_states: bad sizes");
+  const int threads = head_dim < 128 ? ((head_dim + 31) / 32) * 32 : 128;
+  merge_packed_kernel<<<num_heads, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      states, num_parts, num_heads, head_dim, static_cast<__half*>(o));
+  AOAKV_CUDA_TRY(cudaGetLastError(), "merge_packed_states launch");
   return AOAKV_OK;
 }

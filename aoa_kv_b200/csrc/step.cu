@@ -351,6 +351,133 @@ extern "C" int aoakv_step_plan_destroy(aoakv_step_plan plan) {
   return AOAKV_OK;
 }
 
+// ---------------------------------------------------- page-range sharding
+namespace aoakv {
+namespace {
+
+constexpr int kShardMaxProp = 1024;  // entries per (rank, head): k - 1
+
+// Arguments shared by both shard passes; fills the whole-sequence k.
+int shard_args(const aoakv_step_plan_s* p, ClusterStepArgs* a, const void* q,
+               const int32_t* kv_indices, int n_local, int n_total, int page_lo,
+               const int32_t* meta_indices, int* k_out) {
+  AOAKV_CHECK_ARG(p != nullptr, "shard: plan is NULL");
+  if (!p->cluster_ok)
+    return set_error(AOAKV_ERR_UNSUPPORTED,
+                     "shard: the plan runs the four-kernel chain (needs head_dim 64/128, "
+                     "page_size <= 16 and a page count that fits the cluster kernel)");
+  AOAKV_CHECK_ARG(q && kv_indices && meta_indices, "shard: NULL pointer argument");
+  AOAKV_CHECK_ARG(n_local >= 1 && page_lo >= 0 && page_lo % p->P == 0 &&
+                      page_lo + n_local <= n_total,
+                  "shard: local pages must be [page_lo, page_lo + num_local_pages) of the "
+                  "sequence with page_lo a multiple of page_size");
+  int k_pages, k;
+  step_budget(n_total, p->budget, p->sink, &k_pages, &k);
+  AOAKV_CHECK_ARG(k <= p->cp.shape.max_slots,
+                  "shard: the plan's max_pages is below the pages attended per head");
+  *a = {};
+  a->q = static_cast<const __half*>(q);
+  a->kv = static_cast<__half*>(p->kv);
+  a->kv_indices = kv_indices;
+  a->kv_cap = p->kv_cap;
+  a->meta = static_cast<__half*>(p->meta);
+  a->meta_indices = meta_indices;
+  a->meta_cap = p->meta_cap;
+  a->vlog = static_cast<__half*>(p->vlog);
+  a->H = p->H;
+  a->P = p->P;
+  a->k_slots = k;
+  a->mode = p->mode;
+  a->two_rsqrt_d = 2.f / std::sqrt(static_cast<float>(p->D));
+  a->scale_log2 = (1.f / std::sqrt(static_cast<float>(p->D))) * 1.4426950408889634f;
+  a->err = dev_error_ptr();
+  a->page_lo = page_lo;
+  a->last_len = 1;
+  *k_out = k;
+  return AOAKV_OK;
+}
+
+}  // namespace
+}  // namespace aoakv
+
+extern "C" int aoakv_shard_propose(aoakv_step_plan plan, const void* q,
+                                   const int32_t* kv_indices, int32_t num_local_pages,
+                                   int32_t num_total_pages, int32_t page_lo,
+                                   const int32_t* metadata_indices, void* cand_out,
+                                   void* stream) {
+  AOAKV_NVTX("aoakv_shard_propose");
+  ClusterStepArgs a;
+  int k = 0;
+  int rc = shard_args(plan, &a, q, kv_indices, num_local_pages, num_total_pages, page_lo,
+                      metadata_indices, &k);
+  if (rc) return rc;
+  AOAKV_CHECK_ARG(cand_out != nullptr, "shard_propose: cand_out is NULL");
+  AOAKV_CHECK_ARG(num_total_pages > k && k > 1,
+                  "shard_propose: nothing to select (every page, or only the last, is "
+                  "attended); call aoakv_shard_finish with no candidates");
+  AOAKV_CHECK_ARG(k - 1 <= kShardMaxProp, "shard_propose: page budget above 1025 pages");
+  const bool owns_last = page_lo + num_local_pages == num_total_pages;
+  // one page past the local ones stands for another GPU's last page: the
+  // kernel scores pages [0, n_pages - 1) and never reads that entry
+  a.n_pages = num_local_pages + (owns_last ? 0 : 1);
+  AOAKV_CHECK_ARG(a.n_pages <= plan->max_pages,
+                  "shard_propose: more local pages than the plan's max_pages - 1");
+  a.sink = plan->sink && page_lo == 0;
+  a.shard = kShardPropose;
+  a.n_prop = k - 1;
+  a.cand_out = static_cast<uint2*>(cand_out);
+  return launch_cluster_step(a, plan->kv_sw, plan->meta_map, plan->D, plan->cp,
+                             static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int aoakv_shard_finish(aoakv_step_plan plan, const void* q, const void* k_new,
+                                  const void* v_new, const int32_t* kv_indices,
+                                  int32_t num_local_pages, int32_t num_total_pages,
+                                  int32_t page_lo, int32_t kv_last_page_len,
+                                  const int32_t* metadata_indices, const void* cand_all,
+                                  int32_t world, int32_t rank, float* state_out,
+                                  int32_t* selected_out, void* stream) {
+  AOAKV_NVTX("aoakv_shard_finish");
+  ClusterStepArgs a;
+  int k = 0;
+  int rc = shard_args(plan, &a, q, kv_indices, num_local_pages, num_total_pages, page_lo,
+                      metadata_indices, &k);
+  if (rc) return rc;
+  AOAKV_CHECK_ARG(state_out != nullptr, "shard_finish: state_out is NULL");
+  const bool owns_last = page_lo + num_local_pages == num_total_pages;
+  const bool sparse = num_total_pages > k && k > 1;
+  if (owns_last) {
+    AOAKV_CHECK_ARG(k_new && v_new, "shard_finish: the last page's owner needs k_new, v_new");
+    AOAKV_CHECK_ARG(kv_last_page_len >= 1 && kv_last_page_len <= plan->P,
+                    "shard_finish: kv_last_page_len must be in [1, page_size]");
+  }
+  if (sparse) {
+    AOAKV_CHECK_ARG(cand_all != nullptr, "shard_finish: cand_all is NULL");
+    AOAKV_CHECK_ARG(world >= 1 && world <= kShardMaxWorld && rank >= 0 && rank < world,
+                    "shard_finish: world must be in [1, 8] and rank in [0, world)");
+    AOAKV_CHECK_ARG(k - 1 <= kShardMaxProp && world * (k - 1) <= 2048,
+                    "shard_finish: world * (k - 1) candidates above 2048");
+  }
+  AOAKV_CHECK_ARG(num_local_pages <= plan->max_pages,
+                  "shard_finish: more local pages than the plan's max_pages");
+  a.k_new = static_cast<const __half*>(k_new);
+  a.v_new = static_cast<const __half*>(v_new);
+  a.n_pages = num_local_pages;
+  a.last_len = owns_last ? kv_last_page_len : 1;
+  a.shard = kShardFinish;
+  a.n_prop = sparse ? k - 1 : 0;
+  a.dense = num_total_pages <= k;
+  a.cand_in = static_cast<const uint2*>(cand_all);
+  a.world = sparse ? world : 1;
+  a.rank = sparse ? rank : 0;
+  a.owns_last = owns_last;
+  a.state_out = state_out;
+  a.selected_out = sparse ? selected_out : nullptr;
+  a.sel_cols = k - 1;
+  return launch_cluster_step(a, plan->kv_sw, plan->meta_map, plan->D, plan->cp,
+                             static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int aoakv_step_launches(int32_t num_heads, int32_t head_dim, int32_t page_size,
                                    int32_t num_kv_pages, int32_t page_budget,
                                    int32_t sink_first_page, int32_t want_selected,

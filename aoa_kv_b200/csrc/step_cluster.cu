@@ -546,7 +546,10 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   }
   const int N = a.n_pages, n = N - 1;
   const int k = a.k_slots;
-  const bool sparse = N > k && k > 1;
+  const int shard = a.shard;
+  // propose scores and ranks every local page (even when they are <= k);
+  // finish scores nothing
+  const bool sparse = shard == kShardPropose ? n >= 1 : (shard == kShardNone && N > k && k > 1);
   const bool aoa = a.mode == AOAKV_SCORE_AOAKV;
   const int n_st = sparse ? (n + P - 1) / P : 0;  // metadata pages holding scored pages
   const int st_lo = (c * n_st) / C, st_hi = ((c + 1) * n_st) / C;
@@ -557,10 +560,12 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   // slots [s_lo, s_hi), so the last page falls to CTA C-1
   const int T = sparse ? k : (N <= k ? N : 1);
   const int s_lo = (c * T) / C, s_hi = ((c + 1) * T) / C;
-  const int w_last = c == C - 1 ? (T - 1 - s_lo) % kCsWarps : -1;
-  // ids of the last page (attended by CTA C-1, which also appends to it)
-  const int last_pid = __ldcg(a.kv_indices + N - 1);
-  const int app_mpid = c == C - 1 ? __ldcg(a.meta_indices + (N - 1) / P) : 0;
+  // ids of the last page (attended by CTA C-1, which also appends to it);
+  // a propose pass, or a finish pass on a GPU without it, has none
+  const bool has_last = shard == kShardNone || (shard == kShardFinish && a.owns_last);
+  const int w_last = (c == C - 1 && has_last) ? (shard ? 0 : (T - 1 - s_lo) % kCsWarps) : -1;
+  const int last_pid = has_last ? __ldcg(a.kv_indices + N - 1) : -1;
+  const int app_mpid = (c == C - 1 && has_last) ? __ldcg(a.meta_indices + (N - 1) / P) : 0;
   if (warp == w_last && lane == 0 && last_pid >= 0 && last_pid < a.kv_cap) {  // warm L2
 #pragma unroll
     for (int sub = 0; sub < D / 64; ++sub) {
@@ -730,6 +735,68 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       tma_prefetch_l2_3d(&kv_map, 64 * sub, h, pid * 2 * P + P);
     }
   };
+  int n_out = 0;  // propose: entries of this head's cand_out written, best first
+  if (shard == kShardFinish) {
+    // This GPU's list holds its best pages, best first: rank each entry
+    // against the other GPUs' lists; the winners are a prefix of the list.
+    const int np = a.n_prop, G = a.world, me = a.rank;
+    const int n_mine = N - (a.owns_last ? 1 : 0);  // local pages besides the last
+    int w = 0;
+    if (np > 0) {
+      for (int g = tid; g < G * np; g += kCsThreads) {
+        const int gg = g / np, i = g - gg * np;
+        const uint2 e = __ldcg(a.cand_in + (static_cast<size_t>(gg) * H + h) * np + i);
+        gkey[g] = e.x;
+        gpos[g] = e.y;
+      }
+      __syncthreads();
+      // global rank of entry i of list g: i plus, in every other list, the
+      // entries that beat it (a prefix: binary search)
+      auto rank_of = [&](int g, int i) -> int {
+        const uint32_t mk = gkey[g * np + i], mp = gpos[g * np + i];
+        int r = i;
+        for (int gg = 0; gg < G; ++gg) {
+          if (gg == g) continue;
+          int lo = gg * np, hi = lo + np;
+          while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (cs_beats(gkey[mid], gpos[mid], mk, mp)) lo = mid + 1;
+            else hi = mid;
+          }
+          r += lo - gg * np;
+        }
+        return r;
+      };
+      bool win = false;
+      if (tid < np) win = gpos[me * np + tid] != 0xffffffffu && rank_of(me, tid) < np;
+      w = __syncthreads_count(win);
+      if (sel_row)  // every list's winners, by rank (lists c, c + C, ... here)
+        for (int g = c; g < G; g += C)
+          for (int i = tid; i < np; i += kCsThreads)
+            if (gpos[g * np + i] != 0xffffffffu) {
+              const int r = rank_of(g, i);
+              if (r < np) sel_row[r] = static_cast<int>(gpos[g * np + i]);
+            }
+    }
+    // attended here: the winners (or every local page when dense), then
+    // the last page on its owner; CTA c takes slots [lo_s, hi_s)
+    const int Tl = (np > 0 ? w : (a.dense ? n_mine : 0)) + (a.owns_last ? 1 : 0);
+    const int lo_s = (c * Tl) / C, hi_s = ((c + 1) * Tl) / C;
+    for (int j = lo_s + tid; j < hi_s; j += kCsThreads) {
+      int pid = -1;
+      if (a.owns_last && j == Tl - 1) {
+        pid = last_pid;
+      } else if (np > 0) {
+        const int li = static_cast<int>(gpos[me * np + j]) - a.page_lo;
+        if (li >= 0 && li < n_mine) pid = __ldcg(a.kv_indices + li);  // else BAD_PAGE below
+      } else {
+        pid = __ldcg(a.kv_indices + j);
+      }
+      items[j - lo_s] = pid;
+    }
+    n_items = hi_s - lo_s;
+    last_item = (a.owns_last && c == C - 1) ? Tl - 1 - lo_s : -1;
+  }
   if (sparse) {
     const int K = (k - 1) - r_lo;  // pages to choose among the ranked ones (>= 1)
     const int rk0 = min(nloc, max(0, r_lo - pos_lo));  // first ranked local index
@@ -801,7 +868,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     // release never waits for them: K/V of the first candidates into the
     // ring, a few more warmed in L2.
     cluster_arrive_release();
-    if (m_c <= CAPL) {
+    if (m_c <= CAPL && shard == kShardNone) {
       n_spec = min(kCsWarps, n_special + m_c);
       if (warp < n_spec) {
         const int pid = warp < n_special
@@ -843,6 +910,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     fast = fast_s != 0;
     if (fast) {
       const int M = peer_off[C];  // K <= M <= kCsGather
+      n_out = r_lo + min(K, M);
       for (int g = tid; g < M; g += kCsThreads) {  // every list, keys and pages apart
         int cc = 0;
         while (cc < C - 1 && g >= peer_off[cc + 1]) ++cc;
@@ -881,6 +949,9 @@ __global__ void __launch_bounds__(kCsThreads, 1)
           if (cc != c) r += lo[cc] - peer_off[cc];
         win = r < K;
         if (win && sel_row) sel_row[r + r_lo] = static_cast<int>(lst[tid].z);
+        if (win && shard == kShardPropose)
+          a.cand_out[static_cast<size_t>(h) * a.n_prop + r + r_lo] =
+              make_uint2(lst[tid].x, static_cast<uint32_t>(a.page_lo) + lst[tid].y);
       }
       const int w_c = __syncthreads_count(win);  // the winners are lst[0, w_c)
       n_items = n_special + w_c;
@@ -1054,27 +1125,55 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         if (lane == C - 1) peer_off[C] = x;
       }
       __syncthreads();
-      // the page ids of this CTA's decode slots, from the owners' lists
-      for (int sl = s_lo + tid; sl < min(s_hi, T - 1); sl += kCsThreads) {
-        int pid = -1;
-        if (sl < peer_off[C]) {
-          int cc = 0;
-          while (cc < C - 1 && sl >= peer_off[cc + 1]) ++cc;
-          const int pos = cluster.map_shared_rank(sel, cc)[sl - peer_off[cc]];
-          if (pos >= 0 && pos < N) pid = __ldcg(a.kv_indices + pos);
+      if (shard == kShardPropose) {
+        // the selected pages of every CTA with their keys (the sink page
+        // above all), each CTA ranking its own by (key, page)
+        const int own = peer_off[c + 1] - peer_off[c], total = peer_off[C];
+        for (int j = tid; j < own; j += kCsThreads) {
+          const int pos = sel[j];
+          const uint32_t key =
+              (a.sink && pos == 0) ? 0xffffffffu : float_to_key(sc[pos - pos_lo]);
+          cand2[j] = make_uint2(key, static_cast<uint32_t>(pos));
         }
-        items[sl - s_lo] = pid;
-        if (sel_row) sel_row[sl] = pid;
+        __syncthreads();
+        cluster.sync();  // keyed lists published
+        for (int g = tid; g < total; g += kCsThreads) {
+          int cc = 0;
+          while (cc < C - 1 && g >= peer_off[cc + 1]) ++cc;
+          candall[g] = cluster.map_shared_rank(cand2, cc)[g - peer_off[cc]];
+        }
+        __syncthreads();
+        for (int j = tid; j < own; j += kCsThreads) {
+          const uint2 me = cand2[j];
+          int r = 0;
+          for (int g = 0; g < total; ++g) r += cs_beats(candall[g].x, candall[g].y, me.x, me.y);
+          a.cand_out[static_cast<size_t>(h) * a.n_prop + r] =
+              make_uint2(me.x, static_cast<uint32_t>(a.page_lo) + me.y);
+        }
+        n_out = total;
+      } else {
+        // the page ids of this CTA's decode slots, from the owners' lists
+        for (int sl = s_lo + tid; sl < min(s_hi, T - 1); sl += kCsThreads) {
+          int pid = -1;
+          if (sl < peer_off[C]) {
+            int cc = 0;
+            while (cc < C - 1 && sl >= peer_off[cc + 1]) ++cc;
+            const int pos = cluster.map_shared_rank(sel, cc)[sl - peer_off[cc]];
+            if (pos >= 0 && pos < N) pid = __ldcg(a.kv_indices + pos);
+          }
+          items[sl - s_lo] = pid;
+          if (sel_row) sel_row[sl] = pid;
+        }
       }
     }
-  } else {
+  } else if (shard == kShardNone) {
     for (int sl = s_lo + tid; sl < min(s_hi, T - 1); sl += kCsThreads) {  // every page
       const int pid = __ldcg(a.kv_indices + sl);
       items[sl - s_lo] = pid;
       if (sel_row) sel_row[sl] = pid;
     }
   }
-  if (!sparse || !fast) {
+  if (shard == kShardNone && (!sparse || !fast)) {
     n_items = s_hi - s_lo;
     if (c == C - 1) {
       last_item = T - 1 - s_lo;
@@ -1084,12 +1183,21 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       }
     }
   }
-  if (sel_row && c == C - 1)
+  if (sel_row && c == C - 1 && shard == kShardNone)
     for (int i = T + tid; i < a.sel_cols; i += kCsThreads) sel_row[i] = -1;
+  if (shard == kShardPropose && c == 0) {  // the sink page first; unused entries last
+    uint2* out = a.cand_out + static_cast<size_t>(h) * a.n_prop;
+    if (sink_owner && tid == 0) out[0] = make_uint2(0xffffffffu, static_cast<uint32_t>(a.page_lo));
+    for (int i = n_out + tid; i < a.n_prop; i += kCsThreads) out[i] = make_uint2(0u, 0xffffffffu);
+  }
   __syncthreads();
   // no shared memory of a peer is read after this point (the values read are
   // consumed), so the arrival need not order anything
   cluster_arrive_relaxed();
+  if (shard == kShardPropose) {  // no decode: wait until no peer reads this CTA
+    cluster_wait_acquire();
+    return;
+  }
 
   // ------------------------------------------------------------- 3 decode
   // q as column 0 of the B operand of S^T = K q^T (lanes 0..3: channels
@@ -1275,7 +1383,13 @@ __global__ void __launch_bounds__(kCsThreads, 1)
           OO += f * xo[cc * (D + 2) + tid];
         }
       }
-      a.o[static_cast<size_t>(h) * D + tid] = __float2half_rn(LL > 0.f ? OO / LL : 0.f);
+      if (shard == kShardFinish) {  // this GPU's partial state
+        float* so = a.state_out + static_cast<size_t>(h) * (D + 1);
+        so[tid] = LL > 0.f ? OO / LL : 0.f;
+        if (tid == 0) so[D] = LL > 0.f ? (MM + log2f(LL)) * 0.6931471805599453f : -INFINITY;
+      } else {
+        a.o[static_cast<size_t>(h) * D + tid] = __float2half_rn(LL > 0.f ? OO / LL : 0.f);
+      }
     }
   }
   cluster_wait_acquire();  // every peer is past its last read of this CTA's memory

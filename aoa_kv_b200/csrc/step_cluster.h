@@ -40,7 +40,31 @@ struct ClusterStepArgs {
   const int32_t* last_lens;
   int budget;
   int max_pages;                // a request with more pages (or none) is skipped
+  // One sequence split over GPUs by page range (shard != kShardNone). The
+  // local pages are global pages page_lo, page_lo + 1, ...; k_slots is the
+  // whole sequence's k and n_prop = k - 1 entries travel per (rank, head).
+  //   propose: score the local pages (all n_pages - 1 of them; n_pages
+  //            counts one page past the local ones when another GPU owns the
+  //            last page), keep the local top-n_prop and write them to
+  //            cand_out[h, 0..n_prop) as {order key, global page id}, best
+  //            first, unused entries {0, 0xffffffff}. No append, no decode.
+  //   finish:  rank this GPU's list in cand_in[world, H, n_prop] against
+  //            the others, decode the winners it holds (plus the last page,
+  //            appending the new token, when owns_last) and write the
+  //            partial state state_out[h] = {o[D] normalised, lse (natural
+  //            log)}; n_prop == 0: every local page (dense) or only the last.
+  int shard;
+  int page_lo;
+  int n_prop;
+  uint2* cand_out;
+  const uint2* cand_in;
+  int world, rank;
+  int owns_last, dense;
+  float* state_out;
 };
+
+enum { kShardNone = 0, kShardPropose = 1, kShardFinish = 2 };
+constexpr int kShardMaxWorld = 8;
 
 // Sizes the kernel's shared memory is carved for.
 struct CsShape {

@@ -331,6 +331,52 @@ AOAKV_API int aoakv_step_plan_info(aoakv_step_plan plan, int32_t num_kv_pages,
                                    int32_t* cluster_out);
 AOAKV_API int aoakv_step_plan_destroy(aoakv_step_plan plan);
 
+/* One sequence split over GPUs by page range (config 5's 128K-token decode;
+ * the reference runs it on one GPU only). GPU g holds global pages
+ * [page_lo, page_lo + num_local_pages) through its own layer pools and page
+ * tables (page_lo a multiple of page_size, so metadata pages are never
+ * split); the GPU holding page num_total_pages - 1 owns the last page. Per
+ * layer and token every GPU runs, with its own plan (created with max_pages
+ * >= num_local_pages + 1 and the whole sequence's page_budget):
+ *   1 aoakv_shard_propose: scores its pages and writes its best k-1
+ *     (k = min(budget, num_total_pages), the budget rule of
+ *     aoakv_decode_step) to cand_out [num_heads, k-1] as {uint32 order key,
+ *     uint32 global page id}, best first (ties: lower page), unused entries
+ *     {0, 0xffffffff}. Only when num_total_pages > k > 1.
+ *   2 an all_gather of cand_out into cand_all [world, num_heads, k-1]
+ *     (rank order);
+ *   3 aoakv_shard_finish: ranks its entries against the other GPUs', decodes
+ *     the winners it holds and, on the owner, the last page after appending
+ *     k_new, v_new to it (the append and metadata update of
+ *     aoakv_append_kv_cache_decode); writes its partial state
+ *     state_out [num_heads, head_dim + 1] fp32 = {o normalised over its
+ *     tokens, lse = ln(sum exp(scaled scores))}, {0, -inf} for no tokens.
+ *     cand_all may be NULL when no selection runs (every page attended, or
+ *     only the last). selected_out (optional, [num_heads, k-1]) receives the
+ *     whole selection's global page ids, best first;
+ *   4 an all_gather of state_out into states [world, num_heads, head_dim+1];
+ *   5 aoakv_merge_packed_states: the log-sum-exp merge into o [num_heads,
+ *     head_dim] fp16 (the same output on every GPU).
+ * The global selection equals the one-GPU step's: each GPU's k-1 best
+ * contain its share of the global k-1 best. Limits: world <= 8,
+ * world * (k-1) <= 2048. The plan must run the cluster kernel
+ * (AOAKV_ERR_UNSUPPORTED otherwise). */
+AOAKV_API int aoakv_shard_propose(aoakv_step_plan plan, const void* q,
+                                  const int32_t* kv_indices, int32_t num_local_pages,
+                                  int32_t num_total_pages, int32_t page_lo,
+                                  const int32_t* metadata_indices, void* cand_out,
+                                  void* stream);
+AOAKV_API int aoakv_shard_finish(aoakv_step_plan plan, const void* q, const void* k_new,
+                                 const void* v_new, const int32_t* kv_indices,
+                                 int32_t num_local_pages, int32_t num_total_pages,
+                                 int32_t page_lo, int32_t kv_last_page_len,
+                                 const int32_t* metadata_indices, const void* cand_all,
+                                 int32_t world, int32_t rank, float* state_out,
+                                 int32_t* selected_out, void* stream);
+AOAKV_API int aoakv_merge_packed_states(const float* states, int32_t num_parts,
+                                        int32_t num_heads, int32_t head_dim, void* o,
+                                        void* stream);
+
 /* aoakv_step_plan_info for a problem without a plan (the default plan). */
 AOAKV_API int aoakv_step_launches(int32_t num_heads, int32_t head_dim, int32_t page_size,
                                   int32_t num_kv_pages, int32_t page_budget,

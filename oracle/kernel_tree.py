@@ -144,6 +144,16 @@ def apply_rope(x: np.ndarray, past_kv_len: int, rope_scale: float = 1.0,
 BITONIC_MAX_K = 256
 
 
+def score_keys(scores: np.ndarray) -> np.ndarray:
+    """The selection's order-preserving uint32 key of each fp32 score (as
+    uint64): larger score, larger key; -0 == +0; NaN 0, below -inf."""
+    f = np.ascontiguousarray(scores, dtype=np.float32)
+    u = f.view(np.uint32).astype(np.uint64)
+    u = np.where(u == 0x80000000, 0, u)  # -0 == +0
+    key = np.where(u & 0x80000000, ~u & 0xFFFFFFFF, u | 0x80000000)  # order-preserving
+    return np.where(np.isnan(f), 0, key)  # NaN below -inf
+
+
 def topk_positions(scores: np.ndarray, k: int, sink: bool = False) -> np.ndarray:
     """The library's exact selection rule (the reference's RAFT radix select,
     decode_select_k.cuh:25-61, leaves ties and order unspecified): the k
@@ -152,10 +162,7 @@ def topk_positions(scores: np.ndarray, k: int, sink: bool = False) -> np.ndarray
     order as the library writes it: descending score (ties: lower position
     first) for k <= 256, ascending position above. [H, k]."""
     f = np.ascontiguousarray(scores, dtype=np.float32)
-    u = f.view(np.uint32).astype(np.uint64)
-    u = np.where(u == 0x80000000, 0, u)  # -0 == +0
-    key = np.where(u & 0x80000000, ~u & 0xFFFFFFFF, u | 0x80000000)  # order-preserving
-    key = np.where(np.isnan(f), 0, key)  # NaN below -inf
+    key = score_keys(f)
     if sink:
         key[:, 0] = 0xFFFFFFFF
     n = f.shape[-1]

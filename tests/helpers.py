@@ -21,9 +21,11 @@ def golden_names(prefix: str) -> list[str]:
 
 def selection_mismatch(sel_a: np.ndarray, sel_b: np.ndarray, scores: np.ndarray,
                        rtol: float = 1e-3) -> list[tuple[int, int, float, float]]:
-    """Pages selected by one side only whose score is NOT within rtol
-    (relative to the k-th largest score of the row) of the selection
-    threshold. An empty list means the selections agree up to near-ties.
+    """Pages selected by one side only whose score is NOT within rtol of the
+    selection threshold (the k-th largest score of the row), relative to
+    that threshold (plus 1e-5 absolute, the fp32 summation-order noise of a
+    score near zero). An empty list means the selections agree up to
+    near-ties.
 
     sel_a, sel_b: [H, k] page ids; scores: [H, N] indexed by page id.
     Returns (head, page, score, threshold) for each genuine mismatch."""
@@ -34,9 +36,8 @@ def selection_mismatch(sel_a: np.ndarray, sel_b: np.ndarray, scores: np.ndarray,
             continue
         k = len(a)
         row = scores[h].astype(np.float64)
-        finite = row[np.isfinite(row) & (np.abs(row) < 1e30)]
         thr = np.sort(row)[::-1][k - 1] if k <= len(row) else row.min()
-        tol = rtol * max(abs(thr), np.abs(finite).max() if finite.size else 1.0, 1e-6)
+        tol = rtol * abs(thr) + 1e-5
         for p in a ^ b:
             if abs(row[p] - thr) > tol:
                 bad.append((h, p, float(row[p]), float(thr)))

@@ -1,8 +1,10 @@
 """GPU parity of the page-range sharded step (aoa_kv_b200.sharded with
-CudaShardOps: estimate, top-k, partial decode and merge kernels) against the
-unsharded kernel-tree oracle. The ranks are emulated as threads on one GPU
-that exchange tensors through an in-process all_gather, so the test needs a
-single GPU; bench.py --mode longctx runs the same code over NCCL."""
+CudaShardOps: the propose and finish passes of the cluster step kernel and
+the packed-state merge) against the unsharded kernel-tree oracle. The ranks
+are emulated as threads on one GPU that exchange tensors through an
+in-process all_gather (the host waits for each pass, so no kernel waits on
+another), so the test needs a single GPU; bench.py runs the same code over
+NCCL."""
 import threading
 
 import numpy as np
@@ -59,7 +61,7 @@ def run_sharded(world, q, K, V, S, H, D, P, budget, mode, sink):
                 meta_idx=lay.meta_idx, page_lo=lo, n_local=n_local, n_total=n_total,
                 last_len=last_len, owns_last=owns,
                 last_phys=int(lay.kv_idx_np[n_local - 1]) if owns else -1)
-            dec = sharded.ShardedDecoder(group, H, D, P, budget, mode, sink)
+            dec = sharded.ShardedDecoder(group, H, D, P, budget, mode, sink, rank=r)
             o, sel = dec.step(layer, torch.from_numpy(q).cuda(), torch.from_numpy(K[S]).cuda(),
                               torch.from_numpy(V[S]).cuda())
             torch.cuda.synchronize()
@@ -78,15 +80,21 @@ def run_sharded(world, q, K, V, S, H, D, P, budget, mode, sink):
     return results
 
 
-@pytest.mark.parametrize("world,S,budget,mode,sink", [
-    (2, 8192 + 5, 64, "aoakv", False),
-    (4, 8192 + 5, 64, "quest", True),
-    (3, 32768, 300, "aoakv", False),   # k-1 = 299 > 256: radix-path order
-    (2, 700, 100, "aoakv", False),     # every page attended
+@pytest.mark.parametrize("world,S,budget,mode,sink,ties", [
+    (2, 8192 + 5, 64, "aoakv", False, False),
+    (4, 8192 + 5, 64, "quest", True, False),
+    (3, 32768, 300, "aoakv", False, False),   # k-1 = 299 proposals per rank
+    (8, 32768, 256, "quest", False, False),   # 8 x 255 candidates per head
+    (4, 1000, 40, "aoakv", False, False),     # shards shorter than k-1: padded lists
+    (2, 8192 + 5, 64, "quest", False, True),  # equal scores: the lowest pages win
+    (2, 700, 100, "aoakv", False, False),     # every page attended
+    (2, 700, 1, "aoakv", False, False),       # only the last page
 ])
-def test_sharded_step_matches_oracle(cuda, world, S, budget, mode, sink):
+def test_sharded_step_matches_oracle(cuda, world, S, budget, mode, sink, ties):
     H, D, P = 32, 128, 16
     q, K, V = gen_qkv(S + world, H, S + 1, D, "outlier")
+    if ties:  # every page gets the same quest score
+        K[:] = np.float16(0.5)
     results = run_sharded(world, q, K, V, S, H, D, P, budget, mode, sink)
     n_total, last_len = S // P + 1, S % P + 1
     c = kt.LayerCache(n_total + 1, H, D, P)
@@ -104,6 +112,8 @@ def test_sharded_step_matches_oracle(cuda, world, S, budget, mode, sink):
                 scores[:, 0] = np.inf
             g = [sorted(row.tolist()) for row in sel]
             w = [sorted(row.tolist()) for row in want_sel[:, :-1]]
+            if ties:
+                assert g == [list(range(k - 1))] * H, f"rank {r}"
             assert not selection_mismatch(np.array(g), np.array(w), scores), f"rank {r}"
             if g == w:
                 assert np.abs(o - want_o).max() < 2e-3, f"rank {r}"

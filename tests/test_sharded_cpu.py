@@ -22,7 +22,10 @@ from oracle import kernel_tree as kt
 
 
 class NumpyShardOps:
-    """The shard operations on CPU tensors, computed with the oracle."""
+    """The shard operations on CPU tensors, computed with the oracle: the
+    proposals as the propose kernel writes them ({order key, global id},
+    best first, unused entries {0, -1}), the finish pass's ranking, append
+    and partial decode, and the log-sum-exp merge."""
 
     def __init__(self, H, D, P):
         self.H, self.D, self.P = H, D, P
@@ -32,41 +35,64 @@ class NumpyShardOps:
         c.kv, c.meta, c.vlog = layer.kv.numpy(), layer.meta.numpy(), layer.vlog.numpy()
         return c
 
-    def append_decode(self, layer, k_new, v_new):
-        kt.append_decode(self._cache(layer), layer.kv_idx.numpy(), layer.meta_idx.numpy(),
-                         layer.n_local, layer.last_len, k_new.numpy(), v_new.numpy())
+    def propose(self, q, layer, ks, sink_here):
+        n_score = layer.n_local - (1 if layer.owns_last else 0)
+        out = np.zeros((self.H, ks, 2), np.int64)
+        out[:, :, 1] = sharded.SENTINEL_ID
+        if n_score > 0:
+            sc = kt.estimate(q.numpy(), self._cache(layer), layer.meta_idx.numpy(),
+                             layer.kv_idx.numpy(), n_score + 1, mode=self.mode)
+            key = kt.score_keys(sc)
+            if sink_here:
+                key[:, 0] = 0xFFFFFFFF
+            m = min(ks, n_score)
+            pos = kt.topk_positions(sc, m, sink_here)
+            if m > 256:  # the oracle lists large k by position: best first here
+                kk = np.take_along_axis(key, pos, axis=1)
+                order = np.lexsort((pos, -kk.astype(np.int64)), axis=1)
+                pos = np.take_along_axis(pos, order, axis=1)
+            out[:, :m, 0] = np.take_along_axis(key, pos, axis=1)
+            out[:, :m, 1] = pos + layer.page_lo
+        return torch.from_numpy(out.astype(np.uint32).view(np.int32))
 
-    def local_topk(self, q, layer, n_score, ks, mode, sink):
+    def finish(self, q, k_new, v_new, layer, cand_all, ks, rank, want_selected):
         c = self._cache(layer)
-        sc = kt.estimate(q.numpy(), c, layer.meta_idx.numpy(), layer.kv_idx.numpy(),
-                         n_score + 1, mode)
-        pos = kt.topk_positions(sc, ks, sink)
-        vals = np.take_along_axis(sc, pos, axis=1).astype(np.float32)
-        return torch.from_numpy(vals), torch.from_numpy((pos + layer.page_lo).astype(np.int32))
+        if layer.owns_last:
+            kt.append_decode(c, layer.kv_idx.numpy(), layer.meta_idx.numpy(), layer.n_local,
+                             layer.last_len, k_new.numpy(), v_new.numpy())
+        n_mine = layer.n_local - (1 if layer.owns_last else 0)
+        sel = None
+        if cand_all is not None:
+            ca = cand_all.numpy().view(np.uint32).astype(np.int64)  # [G, H, ks, 2]
+            G = ca.shape[0]
+            sel = np.zeros((self.H, ks), np.int32)
+            local = []
+            for h in range(self.H):
+                ent = ca[:, h].reshape(G * ks, 2)
+                ent = ent[ent[:, 1] != 0xFFFFFFFF]
+                order = np.lexsort((ent[:, 1], -ent[:, 0]))[:ks]
+                win = ent[order, 1]
+                sel[h] = win
+                rel = win - layer.page_lo
+                local.append([int(layer.kv_idx[r]) for r in rel if 0 <= r < n_mine])
+            sel = torch.from_numpy(sel)
+        else:
+            k_all = ks == 0 and layer.n_total <= self._k(layer.n_total)
+            local = [[int(p) for p in layer.kv_idx[:n_mine]] if k_all else []] * self.H
+        return torch.from_numpy(self._partial(q, layer, local)), sel if want_selected else None
 
-    def select(self, cand_v, cand_i, ks, sink):
-        pos = kt.topk_positions(cand_v.numpy(), ks, sink)
-        return torch.from_numpy(np.take_along_axis(cand_i.numpy(), pos, axis=1).astype(np.int32))
+    def _k(self, n_total):
+        kp = max(3, self.budget) if self.sink else self.budget
+        return min(kp, n_total)
 
-    @staticmethod
-    def to_local(sel, layer):
-        rel = sel.long() - layer.page_lo
-        mine = (rel >= 0) & (rel < layer.n_local)
-        phys = layer.kv_idx[rel.clamp(0, layer.n_local - 1)]
-        return torch.where(mine, phys, torch.full_like(phys, -1)).to(torch.int32)
-
-    def all_local_pages(self, layer, n_score):
-        return layer.kv_idx[:n_score].to(torch.int32).unsqueeze(0).expand(self.H, n_score)
-
-    def decode_partial(self, q, layer, local):
+    def _partial(self, q, layer, local):
         kv = layer.kv.numpy()
         qf = q.numpy().astype(np.float32)
-        o = np.zeros((self.H, self.D), np.float32)
-        lse = np.full((self.H,), -np.inf, np.float32)
+        st = np.zeros((self.H, self.D + 1), np.float32)
+        st[:, self.D] = -np.inf
         for h in range(self.H):
-            pages = [] if local is None else [int(p) for p in local[h] if int(p) >= 0]
-            ks = [kv[p, 0, :, h] for p in pages]
-            vs = [kv[p, 1, :, h] for p in pages]
+            ks = [kv[p, 0, :, h] for p in local[h]]
+            vs = [kv[p, 1, :, h] for p in local[h]]
             if layer.owns_last:
                 ks.append(kv[layer.last_phys, 0, :layer.last_len, h])
                 vs.append(kv[layer.last_phys, 1, :layer.last_len, h])
@@ -77,12 +103,13 @@ class NumpyShardOps:
             w = (K @ qf[h]) / math.sqrt(self.D)
             m = w.max()
             e = np.exp(w - m)
-            o[h] = (e / e.sum()) @ V
-            lse[h] = m + math.log(e.sum())
-        return torch.from_numpy(o), torch.from_numpy(lse)
+            st[h, :self.D] = (e / e.sum()) @ V
+            st[h, self.D] = m + math.log(e.sum())
+        return st
 
-    def merge(self, o_parts, lse_parts):
-        op, lp = o_parts.numpy(), lse_parts.numpy()
+    def merge(self, states):
+        s = states.numpy()
+        op, lp = s[..., :self.D], s[..., self.D]
         m = lp.max(axis=0)
         w = np.where(np.isfinite(lp), np.exp(lp - m[None]), 0.0)
         o = (w[..., None] * op).sum(axis=0) / w.sum(axis=0)[:, None]
@@ -133,8 +160,10 @@ def _worker(rank, world, port, out_dir, case):
         H, D, P, S = case["H"], case["D"], case["P"], case["S"]
         q, K, V = make_sequence(case["seed"], H, D, S, case["ties"])
         layer = build_shard(rank, world, q, K, V, H, D, P, S, case["seed"] + 100)
+        ops = NumpyShardOps(H, D, P)
+        ops.mode, ops.budget, ops.sink = case["mode"], case["budget"], case["sink"]
         dec = sharded.ShardedDecoder(dist.group.WORLD, H, D, P, case["budget"], case["mode"],
-                                     case["sink"], ops=NumpyShardOps(H, D, P))
+                                     case["sink"], ops=ops)
         o, sel = dec.step(layer, torch.from_numpy(q), torch.from_numpy(K[S]),
                           torch.from_numpy(V[S]))
         np.savez(os.path.join(out_dir, f"r{rank}.npz"), o=o.float().numpy(),
@@ -201,11 +230,26 @@ def test_partition_pages_whole_metadata_pages():
         sharded.partition_pages(20, 8, 16)
 
 
-def test_shard_too_small_for_budget_raises():
-    layer = sharded.ShardLayer(kv=torch.zeros(1), meta=torch.zeros(1), vlog=torch.zeros(1),
-                               kv_idx=torch.zeros(4, dtype=torch.int32),
-                               meta_idx=torch.zeros(1, dtype=torch.int32), page_lo=0, n_local=4,
+def test_short_shard_pads_its_proposals():
+    """A rank with fewer pages than k-1 proposes them all and pads the rest
+    with {0, -1}, which never win."""
+    H, D, P = 2, 16, 4
+    g = np.random.default_rng(0)
+    c = kt.LayerCache(8, H, D, P)
+    idx = np.arange(5, dtype=np.int32)
+    midx = np.arange(2, dtype=np.int32)
+    kt.append_prefill(c, idx, midx, 4, P, g.standard_normal((16, H, D)).astype(np.float16),
+                      g.standard_normal((16, H, D)).astype(np.float16))
+    layer = sharded.ShardLayer(kv=torch.from_numpy(c.kv), meta=torch.from_numpy(c.meta),
+                               vlog=torch.from_numpy(c.vlog), kv_idx=torch.from_numpy(idx[:4]),
+                               meta_idx=torch.from_numpy(midx), page_lo=0, n_local=4,
                                n_total=100, last_len=1, owns_last=False)
-    dec = sharded.ShardedDecoder(None, 2, 16, 4, 20, ops=NumpyShardOps(2, 16, 4))
-    with pytest.raises(ValueError, match="fewer than"):
-        dec.step(layer, torch.zeros(2, 16), torch.zeros(2, 16), torch.zeros(2, 16))
+    ops = NumpyShardOps(H, D, P)
+    ops.mode = "aoakv"
+    cand = ops.propose(torch.from_numpy(g.standard_normal((H, D)).astype(np.float16)), layer, 9,
+                       False).numpy()
+    assert cand.shape == (H, 9, 2)
+    assert sorted(cand[0, :4, 1].tolist()) == [0, 1, 2, 3]
+    assert (cand[:, 4:, 1] == -1).all() and (cand[:, 4:, 0] == 0).all()
+    keys = cand[:, :4, 0].view(np.uint32)
+    assert (np.diff(keys.astype(np.int64), axis=1) <= 0).all()  # best first
