@@ -26,6 +26,7 @@ _c_ip = ctypes.POINTER(ctypes.c_int32)
 _c_sizep = ctypes.POINTER(ctypes.c_size_t)
 _c_pp = ctypes.POINTER(ctypes.c_void_p)
 PLAN_CHAIN = 1
+PLAN_SHARD = 2
 
 # name -> argtypes (restype is int unless listed in _RESTYPE)
 SIGNATURES = {

@@ -113,7 +113,8 @@ int plan_init(aoakv_step_plan_s* p, void* kv, int kv_cap, void* meta, int meta_c
   AOAKV_CHECK_ARG(max_pages >= 0 && max_pages <= kv_cap,
                   "step plan: max_pages must be in [0, kv_capacity_pages]");
   AOAKV_CHECK_ARG(max_ctas >= 0, "step plan: max_ctas must be >= 0");
-  AOAKV_CHECK_ARG((flags & ~AOAKV_PLAN_CHAIN) == 0, "step plan: unknown flag");
+  AOAKV_CHECK_ARG((flags & ~(AOAKV_PLAN_CHAIN | AOAKV_PLAN_SHARD)) == 0,
+                  "step plan: unknown flag");
   AOAKV_CUDA_TRY(cudaGetDevice(&p->device), "step plan: cudaGetDevice");
   p->H = H;
   p->D = D;
@@ -130,7 +131,8 @@ int plan_init(aoakv_step_plan_s* p, void* kv, int kv_cap, void* meta, int meta_c
   int k_pages, k;
   step_budget(p->max_pages, budget, p->sink, &k_pages, &k);
   p->cluster_ok = !(flags & AOAKV_PLAN_CHAIN) &&
-                  cluster_step_plan(H, D, P, p->max_pages, k_pages, max_ctas, &p->cp);
+                  cluster_step_plan(H, D, P, p->max_pages, k_pages, max_ctas, &p->cp,
+                                    (flags & AOAKV_PLAN_SHARD) != 0);
   if (p->cluster_ok) {
     rc = make_kv_tmap_sw128(&p->kv_sw, kv, H, D, P, kv_cap);
     if (rc) return rc;
@@ -374,7 +376,7 @@ int shard_args(const aoakv_step_plan_s* p, ClusterStepArgs* a, const void* q,
   int k_pages, k;
   step_budget(n_total, p->budget, p->sink, &k_pages, &k);
   AOAKV_CHECK_ARG(k <= p->cp.shape.max_slots,
-                  "shard: the plan's max_pages is below the pages attended per head");
+                  "shard: plan made without AOAKV_PLAN_SHARD, or with a smaller budget");
   *a = {};
   a->q = static_cast<const __half*>(q);
   a->kv = static_cast<__half*>(p->kv);

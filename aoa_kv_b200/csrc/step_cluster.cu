@@ -1425,11 +1425,11 @@ std::atomic<int> g_cluster_pdl{-1};
 }  // namespace
 
 int cluster_step_plan(int H, int D, int P, int max_pages, int max_slots, int max_ctas,
-                      ClusterPlan* plan) {
+                      ClusterPlan* plan, bool slots_beyond_pages) {
   if ((D != 64 && D != 128) || P < 1 || P > kCsMaxPage || H < 1 || H > 65535 || max_pages < 1 ||
       max_slots < 1)
     return 0;
-  if (max_slots > max_pages) max_slots = max_pages;
+  if (max_slots > max_pages && !slots_beyond_pages) max_slots = max_pages;
   const int ctas = max_ctas > 0 ? max_ctas : num_sms();
   int C = 8;
   while (C > 1 && H * C > ctas) C >>= 1;

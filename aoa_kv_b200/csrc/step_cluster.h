@@ -84,8 +84,10 @@ struct ClusterPlan {
 // D, page size P, up to max_pages pages of which up to max_slots are
 // attended, at most max_ctas CTAs when max_ctas > 0); 0 otherwise (the
 // caller uses the multi-kernel chain).
+// slots_beyond_pages keeps max_slots above max_pages (a page-range shard
+// attends up to the whole sequence's k pages, some held by other GPUs).
 int cluster_step_plan(int H, int D, int P, int max_pages, int max_slots, int max_ctas,
-                      ClusterPlan* plan);
+                      ClusterPlan* plan, bool slots_beyond_pages = false);
 // Launches num_requests x H clusters (num_requests > 1 needs a.kv_indptr).
 int launch_cluster_step(const ClusterStepArgs& a, const CUtensorMap& kv_map,
                         const CUtensorMap& meta_map, int D, const ClusterPlan& plan,

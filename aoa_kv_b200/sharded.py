@@ -171,7 +171,7 @@ class CudaShardOps:
                 raise ValueError("the layer pool needs one page more than the local pages")
             plan = StepPlan(layer.kv, cap, layer.meta, layer.meta.shape[0], layer.vlog, self.H,
                             self.D, self.P, self.page_budget, self.mode, self.sink,
-                            max_pages=layer.n_local + 1)
+                            max_pages=layer.n_local + 1, shard=True)
             self._plans[key] = plan
         return plan
 

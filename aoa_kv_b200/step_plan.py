@@ -16,17 +16,19 @@ from . import _lib
 class StepPlan:
     """One layer's step plan. Buffers are raw device pointers (ints) or
     tensors; ``chain=True`` forces the four-kernel chain instead of the one
-    cluster launch."""
+    cluster launch; ``shard=True`` plans a page-range shard of a longer
+    sequence (aoakv_shard_propose / aoakv_shard_finish)."""
 
     def __init__(self, kv, kv_cap, meta, meta_cap, vlog, num_heads, head_dim, page_size,
                  page_budget, score_mode, sink_first_page=False, max_pages=0, max_ctas=0,
-                 chain=False):
+                 chain=False, shard=False):
         self._h = ctypes.c_void_p()
         self._lib = _lib.load()
         _lib.call("aoakv_step_plan_create", ctypes.byref(self._h), _addr(kv), int(kv_cap),
                   _addr(meta), int(meta_cap), _addr(vlog), int(num_heads), int(head_dim),
                   int(page_size), int(page_budget), int(score_mode), int(bool(sink_first_page)),
-                  int(max_pages), int(max_ctas), _lib.PLAN_CHAIN if chain else 0)
+                  int(max_pages), int(max_ctas),
+                  (_lib.PLAN_CHAIN if chain else 0) | (_lib.PLAN_SHARD if shard else 0))
         self.page_budget = int(page_budget)
         self.max_ctas = int(max_ctas)
 

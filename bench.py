@@ -666,7 +666,7 @@ def longctx_key(a, world, rank, dev, peak):
         def one_step():
             for i, (lay, (q, k, v)) in enumerate(zip(layers, news)):
                 o[i].copy_(dec.step(lay, q, k, v)[0])
-        launches = None
+        launches = 3 * L
     graph = capture(one_step, dev)
     steps = max(10, a.steps // 2)
     ms = time_replays(graph.replay, steps, a.warmup, world, dev)
@@ -723,15 +723,16 @@ def longctx_key(a, world, rank, dev, peak):
         "max_gpu_bytes": max(per_gpu), "per_gpu_bytes": per_gpu,
         "decode_head_pages_per_gpu": pages_dec,
         "max_abs_err": err, "selection_equal": sel_equal,
-        "checked_against": ("the sharded decoder (estimate, top-k, partial decode, merge) on the "
-                            "same data, layer 0" if world == 1 else
+        "checked_against": ("the sharded decoder run as one rank (propose and finish passes, "
+                            "packed merge) on the same data, layer 0" if world == 1 else
                             "the one-GPU step over the whole sequence on rank 0, layer 0"),
         "config": {"workload": f"1 request, ctx {S} (new token included), budget {budget}, "
                                f"{L}-layer step, q,K,V~N(0,1) seed 4",
                    "pages": n_total, "pages_per_gpu": n_local,
                    "parallelism": "1 GPU, one step launch per layer" if world == 1 else
-                   f"page range x{world}; all_gather of candidates ({world}x{H}x"
-                   f"{kpages - 1}x8 B) and partial states ({world}x{H}x{D + 1}x4 B) per layer"},
+                   f"page range x{world}; per layer: propose launch, all_gather of candidates "
+                   f"({world}x{H}x{kpages - 1}x8 B), finish launch, all_gather of partial "
+                   f"states ({world}x{H}x{D + 1}x4 B), merge launch; NCCL, one CUDA graph"},
     }
     if launches is not None:
         out["gpu_launches"] = launches * steps

@@ -303,11 +303,14 @@ AOAKV_API int aoakv_step_workspace_size(int32_t num_heads, int32_t head_dim,
  *              shared memory is sized for it.
  *   max_ctas   0 = the whole GPU, else at most this many CTAs per step (so
  *              several requests' steps can share the GPU).
- *   flags      AOAKV_PLAN_CHAIN forces the four-kernel chain.
+ *   flags      AOAKV_PLAN_CHAIN forces the four-kernel chain;
+ *              AOAKV_PLAN_SHARD sizes the plan for aoakv_shard_* (a page
+ *              range of a longer sequence: up to page_budget attended
+ *              pages even when max_pages is smaller).
  * aoakv_step_plan_run runs one step (arguments as aoakv_decode_step) on the
  * device the plan was created on; it does not synchronise, allocate or
  * re-plan. Plans are immutable: one plan may serve several streams. */
-enum { AOAKV_PLAN_CHAIN = 1 };
+enum { AOAKV_PLAN_CHAIN = 1, AOAKV_PLAN_SHARD = 2 };
 typedef struct aoakv_step_plan_s* aoakv_step_plan;
 
 AOAKV_API int aoakv_step_plan_create(aoakv_step_plan* plan_out, void* kv_data,
@@ -336,8 +339,9 @@ AOAKV_API int aoakv_step_plan_destroy(aoakv_step_plan plan);
  * [page_lo, page_lo + num_local_pages) through its own layer pools and page
  * tables (page_lo a multiple of page_size, so metadata pages are never
  * split); the GPU holding page num_total_pages - 1 owns the last page. Per
- * layer and token every GPU runs, with its own plan (created with max_pages
- * >= num_local_pages + 1 and the whole sequence's page_budget):
+ * layer and token every GPU runs, with its own plan (created with
+ * AOAKV_PLAN_SHARD, max_pages >= num_local_pages + 1 and the whole
+ * sequence's page_budget):
  *   1 aoakv_shard_propose: scores its pages and writes its best k-1
  *     (k = min(budget, num_total_pages), the budget rule of
  *     aoakv_decode_step) to cand_out [num_heads, k-1] as {uint32 order key,
