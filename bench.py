@@ -59,7 +59,7 @@ H, D, P = 32, 128, 16
 # DRAM bytes (read + write) of one cluster step launch at the headline shape:
 # dram__bytes_read.sum + dram__bytes_write.sum from the ncu capture
 # summarised in profiles/cluster_step_32k.md (not measured in this run)
-STEP_TRAFFIC_BYTES = None
+STEP_TRAFFIC_BYTES = 57_103_000
 STEP_TRAFFIC_SOURCE = "profiles/cluster_step_32k.md (ncu, not measured in this run)"
 
 
@@ -70,10 +70,12 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--mode", choices=["headline", "longctx", "batched", "model"],
+    ap.add_argument("--mode", choices=["headline", "longctx", "batched", "model", "kernels"],
                     default="headline",
                     help="headline (default): the headline line with every extra key; "
-                         "longctx / batched: that key alone; model: config 3")
+                         "longctx / batched: that key alone; model: config 3; kernels: each "
+                         "kernel of one headline layer alone, L2 flushed before every launch "
+                         "(the workload of the per-kernel ncu summaries)")
     ap.add_argument("--extras", default="longctx,batched,prefill_metadata,config2",
                     help="comma list of extra keys for the headline line ('' = none)")
     ap.add_argument("--layers", type=int, default=32, help="headline layers per step")
@@ -1124,6 +1126,101 @@ def run_model(a):
     }), flush=True)
 
 
+# ----------------------------------------------- each kernel, one layer
+def run_kernels(a):
+    """One layer of the headline shape (ctx a.ctx, budget a.budget, outlier K,
+    seed a.seed). Each kernel of the step runs alone, 5 times, with L2
+    flushed (a 256 MB write) before every launch and CUDA events around the
+    launch itself: the prefill append (once, in the setup, untimed), the
+    decode append, the page scorer, the top-k, the sparse decode, the
+    one-launch step and the four-kernel chain. Prints one JSON line: per
+    kernel its mean launch time, algorithmic bytes and GB/s."""
+    import torch
+
+    from aoa_kv_b200 import StepPlan, _lib
+    dev = init_gpu(1, int(os.environ.get("LOCAL_RANK", "0")))
+    _lib.load()
+    peak, peak_src = load_peak()
+    ctl, news = setup_layers(a.ctx, 1, a.budget, a.seed, a.method, dev)
+    n = len(ctl.kv_cache.indicies)
+    kp = a.budget // P
+    q, k, v = news[0]
+    kv_p, kv_cap, meta_p, meta_cap, vlog_p = ctl._layer_buffers(0)
+    scores = torch.empty(H, n, dtype=torch.float32, device=dev)
+    sel = torch.empty(H, kp - 1, dtype=torch.int32, device=dev)
+    o = torch.empty(H, D, dtype=torch.float16, device=dev)
+    ws_n = _lib.size_query("aoakv_decode_workspace_size", H, D, kp - 1)
+    ws = torch.zeros(ws_n, dtype=torch.uint8, device=dev)
+    sws = ctl._ensure_step_workspace()
+    chain = StepPlan(kv_p, kv_cap, meta_p, meta_cap, vlog_p, H, D, P, kp, ctl.score_mode,
+                     chain=True)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def st():
+        return torch.cuda.current_stream().cuda_stream
+
+    def append():
+        _lib.call("aoakv_append_kv_cache_decode", k.data_ptr(), v.data_ptr(), kv_p,
+                  ctl.kv_indices_with_last.data_ptr(), n, ctl.kv_cache.last_page_len, kv_cap,
+                  meta_p, ctl.metadata_indices.data_ptr(), len(ctl.metadata_cache.indicies),
+                  ctl.metadata_cache.last_page_len, meta_cap, vlog_p, H, D, P, 0, st())
+
+    def estimate():
+        _lib.call("aoakv_estimate_attn_score", q.data_ptr(), scores.data_ptr(), 1, n, meta_p,
+                  ctl.metadata_indices.data_ptr(), len(ctl.metadata_cache.indicies),
+                  ctl.metadata_cache.last_page_len, meta_cap,
+                  ctl.kv_indices_with_last.data_ptr(), kv_cap, vlog_p, H, D, P, 0,
+                  ctl.score_mode, st())
+
+    def topk():
+        _lib.call("aoakv_topk_filtering", scores.data_ptr(), 1, n,
+                  ctl.kv_indices_with_last.data_ptr(), 0, H, n - 1, kp - 1, None, 0,
+                  sel.data_ptr(), kp - 1, 0, st())
+
+    def decode():
+        _lib.call("aoakv_sparse_decode", q.data_ptr(), o.data_ptr(), kv_p, kv_cap,
+                  sel.data_ptr(), kp - 1, kp - 1, ctl.kv_cache.indicies[-1],
+                  ctl.kv_cache.last_page_len, H, D, P, 0, 0.0, ws.data_ptr(), ws_n, st())
+
+    def step():
+        ctl.decode_step(q, k, v, 0, out=o)
+
+    def chained():
+        chain.run(q, k, v, o, ctl.kv_indices_with_last, n, ctl.kv_cache.last_page_len,
+                  ctl.metadata_indices, None, sws, sws.numel(), st())
+    sb = step_bytes(a.ctx, a.budget, a.method)
+    cases = [
+        ("append_decode", append, 2 * H * D * 2 * 2 + 2 * H * D * 2 * 2),
+        ("estimate", estimate, estimate_bytes(a.ctx, a.method)),
+        ("topk", topk, H * (n - 1) * 4 + H * (kp - 1) * 4),
+        ("sparse_decode", decode, kp * P * H * D * 2 * 2 + 2 * H * D * 2 + H * (kp - 1) * 4),
+        ("step_one_launch", step, sb),
+        ("step_chain", chained, sb),
+    ]
+    out = {"metric": "per-kernel µs, one headline layer, L2 flushed before each launch",
+           "config": {"workload": f"1 layer, ctx {a.ctx}, budget {a.budget}, {a.method}, "
+                                  f"outlier K seed {a.seed}",
+                      "timing": "CUDA events around each launch; mean of 5"},
+           "peak_gbs": peak, "peak_source": peak_src, "kernels": {}}
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for name, fn, b in cases:
+        fn()  # attributes, tensor maps; every call leaves the same state
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(5):
+            flush.fill_(1)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3)
+        us = statistics.mean(ts)
+        out["kernels"][name] = {"us": round(us, 3), **roof(b, us, peak)}
+    _lib.check_device()
+    chain.close()
+    print(json.dumps(out), flush=True)
+
+
 def main():
     a = parse()
     if a.impl == "reference":
@@ -1132,6 +1229,8 @@ def main():
         run_single(a, a.mode)
     elif a.mode == "model":
         run_model(a)
+    elif a.mode == "kernels":
+        run_kernels(a)
     else:
         run_headline(a)
 
