@@ -92,6 +92,17 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// The dynamic shared memory base advanced to the next multiple of Align
+// bytes. Offsetting the __shared__ array itself (instead of rounding the
+// address as an integer) keeps the pointer's state space visible to the
+// compiler, so accesses through it stay shared-memory instructions rather
+// than generic ones.
+template <uint32_t Align>
+__device__ __forceinline__ uint8_t* align_smem(uint8_t* base) {
+  const uint32_t a = smem_addr(base);
+  return base + (((a + Align - 1u) & ~(Align - 1u)) - a);
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)),
                "r"(count));

@@ -14,8 +14,7 @@ template <int D>
 __global__ void __launch_bounds__(kDecThreads)
     sparse_decode_kernel(const __grid_constant__ CUtensorMap tmap, DecodeArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
+  uint8_t* smem = align_smem<128>(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   int* tok = reinterpret_cast<int*>(smem + 64);
   int* flag = tok + kDecMaxChunk;

@@ -31,8 +31,7 @@ __global__ void __launch_bounds__(1024) estimate_hs_kernel(EstimateArgs a) {
 template <int D>
 __global__ void __launch_bounds__(1024) estimate_tma_kernel(EstimateArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* stages = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
+  uint8_t* stages = align_smem<128>(smem_raw);
   __shared__ uint64_t bars[kEstStages];
   __shared__ int ids_s[2 * kEstMaxRange];
   if (threadIdx.x == 0) {

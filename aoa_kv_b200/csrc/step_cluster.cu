@@ -467,8 +467,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   const int CAPL = cs_capl(C, shp.max_slots);  // local candidates one CTA may publish
   using Vec = typename LaneVec<CPL>::T;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* smem = align_smem<1024>(smem_raw);
   __shared__ uint64_t bars[kCsWarps];
   __shared__ uint64_t merge_bar;  // CTA 0: the other CTAs' partial states are in
   __shared__ CsXchg xs;
@@ -476,7 +475,8 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   __shared__ int peer_cnt[C], peer_off[C + 1];
   __shared__ float gsh[2];
   __shared__ uint32_t kmin_s, kmax_s;     // key range of this CTA's ranked scores
-  __shared__ int cnt_s, fast_s, nw_s;
+  __shared__ int cnt_s;
+  __shared__ int peer_m[C], peer_ovf[C];  // every CTA's candidate count and overflow flag
 
   cg::cluster_group cluster = cg::this_cluster();
   const int c = static_cast<int>(cluster.block_rank());
@@ -859,10 +859,17 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         if (i < m_c && sub == 0) lst[r] = me;
       }
     }
+    // Peers read the first K entries of this list (K * C <= kCsGather, else
+    // the cluster takes the fallback): slots past the candidates hold an
+    // entry that beats nothing and never wins.
+    const bool gatherable = K * C <= kCsGather;
     if (tid == 0) {
       xs.m = m_c;
-      xs.ovf = m_c > CAPL;
+      xs.ovf = m_c > CAPL || !gatherable;
     }
+    if (gatherable && m_c < K)
+      for (int j = m_c + tid; j < K; j += kCsThreads)
+        lst[j] = make_uint4(0u, 0xffffffffu, 0xffffffffu, 0u);
     __syncthreads();
     // Publish (release) first, then start the likely winners' loads, so the
     // release never waits for them: K/V of the first candidates into the
@@ -885,50 +892,60 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       }
     }
     cluster_wait_acquire();  // local candidate lists published
-    if (warp == 0) {
-      int v = 0, ov = 0;
-      if (lane < C) {
-        const CsXchg* px = cluster.map_shared_rank(&xs, lane);
-        v = px->m;
-        ov = px->ovf;
-      }
-      int x = v;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-      }
-      if (lane < C) peer_off[lane] = x - v;
-      if (lane == C - 1) peer_off[C] = x;
-      const unsigned any = __ballot_sync(0xffffffffu, ov != 0);
-      if (lane == 0) {
-        fast_s = any == 0u;
-        nw_s = 0;
-      }
+    // One round of distributed shared memory: every CTA's count, overflow
+    // flag and first K entries (a winner ranks below K in its own list).
+    if (tid < C) {
+      const CsXchg* px = cluster.map_shared_rank(&xs, tid);
+      peer_m[tid] = px->m;
+      peer_ovf[tid] = px->ovf;
     }
-    __syncthreads();
-    fast = fast_s != 0;
-    if (fast) {
-      const int M = peer_off[C];  // K <= M <= kCsGather
-      n_out = r_lo + min(K, M);
-      for (int g = tid; g < M; g += kCsThreads) {  // every list, keys and pages apart
-        int cc = 0;
-        while (cc < C - 1 && g >= peer_off[cc + 1]) ++cc;
-        const uint4 e = cluster.map_shared_rank(lst, cc)[g - peer_off[cc]];
+    if (gatherable)
+      for (int g = tid; g < C * K; g += kCsThreads) {
+        const int cc = g / K;
+        const uint4 e = cluster.map_shared_rank(lst, cc)[g - cc * K];
         gkey[g] = e.x;
         gpos[g] = e.y;
       }
-      __syncthreads();
+    __syncthreads();
+#pragma unroll
+    for (int cc = 0; cc < C; ++cc) fast = fast && peer_ovf[cc] == 0;
+    if (fast) {
+      int M = 0;
+#pragma unroll
+      for (int cc = 0; cc < C; ++cc) M += min(peer_m[cc], K);
+      n_out = r_lo + min(K, M);
+      const int mine = min(m_c, K);
+      // rank of own entry i: i plus the entries of the other lists that beat
+      // it. Few entries: tpc threads count them in parallel; many: one
+      // thread binary-searches each list.
+      int k2 = 1;
+      while (k2 < K) k2 <<= 1;
+      const int tpc = k2 >= kCsThreads ? 1 : (kCsThreads / k2 > 32 ? 32 : kCsThreads / k2);
+      const bool count = (C - 1) * K <= 64 * tpc;
       bool win = false;
-      if (tid < m_c) {
-        const uint32_t mk = gkey[peer_off[c] + tid], mpos = gpos[peer_off[c] + tid];
-        // the entries of every other list that beat mine: binary searches
-        // of all lists in lockstep (independent loads in flight)
-        int lo[C], hi[C];
+      int i = tid, r = 0;
+      if (count) {
+        i = tid / tpc;
+        const int sub = tid - i * tpc;
+        if (i < mine) {
+          const uint32_t mk = gkey[c * K + i], mpos = gpos[c * K + i];
+#pragma unroll
+          for (int cc = 0; cc < C; ++cc) {
+            if (cc == c) continue;
+            for (int g = cc * K + sub; g < (cc + 1) * K; g += tpc)
+              r += cs_beats(gkey[g], gpos[g], mk, mpos);
+          }
+        }
+        for (int off = tpc >> 1; off > 0; off >>= 1) r += __shfl_xor_sync(0xffffffffu, r, off);
+        r += i;
+        win = i < mine && sub == 0 && r < K;
+      } else if (i < mine) {
+        const uint32_t mk = gkey[c * K + i], mpos = gpos[c * K + i];
+        int lo[C], hi[C];  // binary searches of all lists in lockstep
 #pragma unroll
         for (int cc = 0; cc < C; ++cc) {
-          lo[cc] = cc == c ? 0 : peer_off[cc];
-          hi[cc] = cc == c ? 0 : peer_off[cc + 1];
+          lo[cc] = cc * K;
+          hi[cc] = cc == c ? cc * K : cc * K + min(peer_m[cc], K);
         }
         bool more = true;
         while (more) {
@@ -943,16 +960,16 @@ __global__ void __launch_bounds__(kCsThreads, 1)
             }
           }
         }
-        int r = tid;  // rank within its own list
+        r = i;
 #pragma unroll
         for (int cc = 0; cc < C; ++cc)
-          if (cc != c) r += lo[cc] - peer_off[cc];
+          if (cc != c) r += lo[cc] - cc * K;
         win = r < K;
-        if (win && sel_row) sel_row[r + r_lo] = static_cast<int>(lst[tid].z);
-        if (win && shard == kShardPropose)
-          a.cand_out[static_cast<size_t>(h) * a.n_prop + r + r_lo] =
-              make_uint2(lst[tid].x, static_cast<uint32_t>(a.page_lo) + lst[tid].y);
       }
+      if (win && sel_row) sel_row[r + r_lo] = static_cast<int>(lst[i].z);
+      if (win && shard == kShardPropose)
+        a.cand_out[static_cast<size_t>(h) * a.n_prop + r + r_lo] =
+            make_uint2(lst[i].x, static_cast<uint32_t>(a.page_lo) + lst[i].y);
       const int w_c = __syncthreads_count(win);  // the winners are lst[0, w_c)
       n_items = n_special + w_c;
       for (int j = tid; j < n_items; j += kCsThreads)
