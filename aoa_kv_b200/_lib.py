@@ -73,6 +73,13 @@ SIGNATURES = {
     "aoakv_shard_finish": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_p,
                            _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_p],
     "aoakv_merge_packed_states": [_c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p],
+    "aoakv_shard_mailbox_create": [_c_pp, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p],
+    "aoakv_shard_mailbox_connect": [_c_p, _c_p],
+    "aoakv_shard_mailbox_destroy": [_c_p],
+    "aoakv_shard_propose_p2p": [_c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p],
+    "aoakv_shard_finish_p2p": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32,
+                               _c_i32, _c_p, _c_p, _c_p],
+    "aoakv_shard_merge_p2p": [_c_p, _c_i32, _c_p, _c_p],
     "aoakv_decode_step_grid": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p,
                                _c_p, _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                                _c_i32, _c_p, _c_p, _c_size, _c_i32, _c_p],

@@ -151,6 +151,26 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar,
   return false;
 }
 
+// Flags in another GPU's memory (peer pointers over NVLink): a release add
+// and a bounded acquire wait, both at system scope. The wait returns false
+// and records AOAKV_DEV_ERR_TIMEOUT after about a second.
+__device__ __forceinline__ void flag_add_release_sys(uint32_t* f, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t flag_load_acquire_sys(const uint32_t* f) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool flag_wait_sys(const uint32_t* f, uint32_t target, int* err) {
+  for (uint32_t i = 0; i < (1u << 24); ++i) {
+    if (static_cast<int32_t>(flag_load_acquire_sys(f) - target) >= 0) return true;
+    if (i > 64) __nanosleep(64);
+  }
+  raise_dev_error(err, AOAKV_DEV_ERR_TIMEOUT);
+  return false;
+}
+
 // 3-D tiled TMA load global -> shared, completion counted on `bar`.
 // Coordinates are element indices (c0 innermost).
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map,

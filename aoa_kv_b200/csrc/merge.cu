@@ -14,6 +14,7 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "step_cluster.h"
 
 namespace aoakv {
 namespace {
@@ -59,6 +60,52 @@ __global__ void merge_packed_kernel(const float* states, int G, int H, int D, __
       }
     }
     o[static_cast<size_t>(h) * D + d] = __float2half_rn(sum > 0.f ? acc / sum : 0.f);
+  }
+}
+
+// The merge of a sharded step whose states arrive in this GPU's mailbox
+// (peer stores): waits until every GPU delivered this step's state of every
+// head (fs), merges head blockIdx.x, and the last head to finish closes the
+// step's exchanges (ep).
+__global__ void merge_mailbox_kernel(ShardMail m, int world, int rank, int H, int D,
+                                     int proposals, __half* o, int* err) {
+  const int h = blockIdx.x;
+  uint32_t* ep = reinterpret_cast<uint32_t*>(m.base[rank] + m.ep_off);
+  if (threadIdx.x == 0) {
+    const uint32_t target = (__ldcg(ep + 1) + 1u) * static_cast<uint32_t>(H);
+    const uint32_t* fs = reinterpret_cast<const uint32_t*>(m.base[rank] + m.fs_off);
+    for (int g = 0; g < world; ++g) flag_wait_sys(fs + g, target, err);
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+  }
+  __syncthreads();
+  const float* states = reinterpret_cast<const float*>(m.base[rank] + m.state_off);
+  const size_t row = static_cast<size_t>(D) + 1;
+  float mx = -INFINITY;
+  for (int g = 0; g < world; ++g)
+    mx = fmaxf(mx, __ldcg(states + (static_cast<size_t>(g) * H + h) * row + D));
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f, sum = 0.f;
+    if (mx != -INFINITY) {
+      for (int g = 0; g < world; ++g) {
+        const float* st = states + (static_cast<size_t>(g) * H + h) * row;
+        const float l = __ldcg(st + D);
+        if (l == -INFINITY) continue;
+        const float w = expf(l - mx);
+        sum += w;
+        acc += w * __ldcg(st + d);
+      }
+    }
+    o[static_cast<size_t>(h) * D + d] = __float2half_rn(sum > 0.f ? acc / sum : 0.f);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(ep + 2, 1u) == static_cast<uint32_t>(H) - 1u) {  // every head read ep
+      ep[2] = 0u;
+      if (proposals) ep[0] += 1u;
+      ep[1] += 1u;
+      __threadfence();
+    }
   }
 }
 
@@ -119,3 +166,14 @@ extern "C" int aoakv_merge_packed_states(const float* states, int32_t num_parts,
   AOAKV_CUDA_TRY(cudaGetLastError(), "merge_packed_states launch");
   return AOAKV_OK;
 }
+
+namespace aoakv {
+int launch_merge_mailbox(const ShardMail& m, int world, int rank, int H, int D, int proposals,
+                         void* o, cudaStream_t s) {
+  const int threads = D < 128 ? ((D + 31) / 32) * 32 : 128;
+  merge_mailbox_kernel<<<H, threads, 0, s>>>(m, world, rank, H, D, proposals,
+                                             static_cast<__half*>(o), dev_error_ptr());
+  AOAKV_CUDA_TRY(cudaGetLastError(), "merge (mailbox) launch");
+  return AOAKV_OK;
+}
+}  // namespace aoakv

@@ -359,6 +359,10 @@ namespace {
 
 constexpr int kShardMaxProp = 1024;  // entries per (rank, head): k - 1
 
+// A selection runs (proposals travel) when the sequence has more pages than
+// k and k > 1.
+bool num_total_ok(int n_total, int k) { return n_total > k && k > 1; }
+
 // Arguments shared by both shard passes; fills the whole-sequence k.
 int shard_args(const aoakv_step_plan_s* p, ClusterStepArgs* a, const void* q,
                const int32_t* kv_indices, int n_local, int n_total, int page_lo,
@@ -402,34 +406,128 @@ int shard_args(const aoakv_step_plan_s* p, ClusterStepArgs* a, const void* q,
 }  // namespace
 }  // namespace aoakv
 
+// The mailboxes of the peer-store exchange (aoakv_shard_mailbox_*).
+struct aoakv_shard_mailbox_s {
+  int device, world, rank, H, D, max_prop;
+  aoakv::ShardMail mail;
+  uint8_t* local;
+  size_t bytes;
+  bool connected;
+  bool opened[aoakv::kShardMaxWorld];
+};
+
+namespace aoakv {
+namespace {
+
+int shard_propose(const aoakv_step_plan_s* plan, const aoakv_shard_mailbox_s* mb,
+                  const void* q, const int32_t* kv_indices, int n_local, int n_total,
+                  int page_lo, const int32_t* meta_indices, void* cand_out, void* stream) {
+  ClusterStepArgs a;
+  int k = 0;
+  int rc = shard_args(plan, &a, q, kv_indices, n_local, n_total, page_lo, meta_indices, &k);
+  if (rc) return rc;
+  AOAKV_CHECK_ARG(num_total_ok(n_total, k), "shard_propose: nothing to select (every page, "
+                  "or only the last, is attended); run the finish pass with no candidates");
+  AOAKV_CHECK_ARG(k - 1 <= kShardMaxProp, "shard_propose: page budget above 1025 pages");
+  const bool owns_last = page_lo + n_local == n_total;
+  // one page past the local ones stands for another GPU's last page: the
+  // kernel scores pages [0, n_pages - 1) and never reads that entry
+  a.n_pages = n_local + (owns_last ? 0 : 1);
+  AOAKV_CHECK_ARG(a.n_pages <= plan->max_pages,
+                  "shard_propose: more local pages than the plan's max_pages - 1");
+  a.sink = plan->sink && page_lo == 0;
+  a.shard = kShardPropose;
+  a.n_prop = k - 1;
+  if (mb) {
+    AOAKV_CHECK_ARG(mb->connected && mb->H == plan->H && mb->D == plan->D &&
+                        k - 1 <= mb->max_prop,
+                    "shard_propose: mailbox not connected, or made for other sizes");
+    a.p2p = 1;
+    a.mail = mb->mail;
+    a.world = mb->world;
+    a.rank = mb->rank;
+    a.cand_out = reinterpret_cast<uint2*>(mb->local + mb->mail.cand_off) +
+                 static_cast<size_t>(mb->rank) * plan->H * (k - 1);
+  } else {
+    AOAKV_CHECK_ARG(cand_out != nullptr, "shard_propose: cand_out is NULL");
+    a.cand_out = static_cast<uint2*>(cand_out);
+  }
+  return launch_cluster_step(a, plan->kv_sw, plan->meta_map, plan->D, plan->cp,
+                             static_cast<cudaStream_t>(stream));
+}
+
+int shard_finish(const aoakv_step_plan_s* plan, const aoakv_shard_mailbox_s* mb, const void* q,
+                 const void* k_new, const void* v_new, const int32_t* kv_indices, int n_local,
+                 int n_total, int page_lo, int last_len, const int32_t* meta_indices,
+                 const void* cand_all, int world, int rank, float* state_out,
+                 int32_t* selected_out, void* stream) {
+  ClusterStepArgs a;
+  int k = 0;
+  int rc = shard_args(plan, &a, q, kv_indices, n_local, n_total, page_lo, meta_indices, &k);
+  if (rc) return rc;
+  const bool owns_last = page_lo + n_local == n_total;
+  const bool sparse = num_total_ok(n_total, k);
+  if (mb) {
+    AOAKV_CHECK_ARG(mb->connected && mb->H == plan->H && mb->D == plan->D &&
+                        (!sparse || k - 1 <= mb->max_prop),
+                    "shard_finish: mailbox not connected, or made for other sizes");
+    world = mb->world;
+    rank = mb->rank;
+    cand_all = mb->local + mb->mail.cand_off;
+    a.p2p = 1;
+    a.mail = mb->mail;
+  } else {
+    AOAKV_CHECK_ARG(state_out != nullptr, "shard_finish: state_out is NULL");
+    if (!sparse) {  // no lists: world and rank are not used
+      world = 1;
+      rank = 0;
+    }
+  }
+  if (owns_last) {
+    AOAKV_CHECK_ARG(k_new && v_new, "shard_finish: the last page's owner needs k_new, v_new");
+    AOAKV_CHECK_ARG(last_len >= 1 && last_len <= plan->P,
+                    "shard_finish: kv_last_page_len must be in [1, page_size]");
+  }
+  AOAKV_CHECK_ARG(world >= 1 && world <= kShardMaxWorld && rank >= 0 && rank < world,
+                  "shard_finish: world must be in [1, 8] and rank in [0, world)");
+  if (sparse) {
+    AOAKV_CHECK_ARG(cand_all != nullptr, "shard_finish: cand_all is NULL");
+    AOAKV_CHECK_ARG(k - 1 <= kShardMaxProp && world * (k - 1) <= 2048,
+                    "shard_finish: world * (k - 1) candidates above 2048");
+  }
+  AOAKV_CHECK_ARG(n_local <= plan->max_pages,
+                  "shard_finish: more local pages than the plan's max_pages");
+  a.k_new = static_cast<const __half*>(k_new);
+  a.v_new = static_cast<const __half*>(v_new);
+  a.n_pages = n_local;
+  a.last_len = owns_last ? last_len : 1;
+  a.shard = kShardFinish;
+  a.n_prop = sparse ? k - 1 : 0;
+  a.dense = n_total <= k;
+  a.cand_in = static_cast<const uint2*>(cand_all);
+  a.world = world;
+  a.rank = rank;
+  a.owns_last = owns_last;
+  a.state_out = state_out;
+  a.selected_out = sparse ? selected_out : nullptr;
+  a.sel_cols = k - 1;
+  return launch_cluster_step(a, plan->kv_sw, plan->meta_map, plan->D, plan->cp,
+                             static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+int launch_merge_mailbox(const ShardMail& m, int world, int rank, int H, int D, int proposals,
+                         void* o, cudaStream_t s);
+}  // namespace aoakv
+
 extern "C" int aoakv_shard_propose(aoakv_step_plan plan, const void* q,
                                    const int32_t* kv_indices, int32_t num_local_pages,
                                    int32_t num_total_pages, int32_t page_lo,
                                    const int32_t* metadata_indices, void* cand_out,
                                    void* stream) {
   AOAKV_NVTX("aoakv_shard_propose");
-  ClusterStepArgs a;
-  int k = 0;
-  int rc = shard_args(plan, &a, q, kv_indices, num_local_pages, num_total_pages, page_lo,
-                      metadata_indices, &k);
-  if (rc) return rc;
-  AOAKV_CHECK_ARG(cand_out != nullptr, "shard_propose: cand_out is NULL");
-  AOAKV_CHECK_ARG(num_total_pages > k && k > 1,
-                  "shard_propose: nothing to select (every page, or only the last, is "
-                  "attended); call aoakv_shard_finish with no candidates");
-  AOAKV_CHECK_ARG(k - 1 <= kShardMaxProp, "shard_propose: page budget above 1025 pages");
-  const bool owns_last = page_lo + num_local_pages == num_total_pages;
-  // one page past the local ones stands for another GPU's last page: the
-  // kernel scores pages [0, n_pages - 1) and never reads that entry
-  a.n_pages = num_local_pages + (owns_last ? 0 : 1);
-  AOAKV_CHECK_ARG(a.n_pages <= plan->max_pages,
-                  "shard_propose: more local pages than the plan's max_pages - 1");
-  a.sink = plan->sink && page_lo == 0;
-  a.shard = kShardPropose;
-  a.n_prop = k - 1;
-  a.cand_out = static_cast<uint2*>(cand_out);
-  return launch_cluster_step(a, plan->kv_sw, plan->meta_map, plan->D, plan->cp,
-                             static_cast<cudaStream_t>(stream));
+  return shard_propose(plan, nullptr, q, kv_indices, num_local_pages, num_total_pages, page_lo,
+                       metadata_indices, cand_out, stream);
 }
 
 extern "C" int aoakv_shard_finish(aoakv_step_plan plan, const void* q, const void* k_new,
@@ -440,44 +538,130 @@ extern "C" int aoakv_shard_finish(aoakv_step_plan plan, const void* q, const voi
                                   int32_t world, int32_t rank, float* state_out,
                                   int32_t* selected_out, void* stream) {
   AOAKV_NVTX("aoakv_shard_finish");
-  ClusterStepArgs a;
-  int k = 0;
-  int rc = shard_args(plan, &a, q, kv_indices, num_local_pages, num_total_pages, page_lo,
-                      metadata_indices, &k);
-  if (rc) return rc;
-  AOAKV_CHECK_ARG(state_out != nullptr, "shard_finish: state_out is NULL");
-  const bool owns_last = page_lo + num_local_pages == num_total_pages;
-  const bool sparse = num_total_pages > k && k > 1;
-  if (owns_last) {
-    AOAKV_CHECK_ARG(k_new && v_new, "shard_finish: the last page's owner needs k_new, v_new");
-    AOAKV_CHECK_ARG(kv_last_page_len >= 1 && kv_last_page_len <= plan->P,
-                    "shard_finish: kv_last_page_len must be in [1, page_size]");
+  return shard_finish(plan, nullptr, q, k_new, v_new, kv_indices, num_local_pages,
+                      num_total_pages, page_lo, kv_last_page_len, metadata_indices, cand_all,
+                      world, rank, state_out, selected_out, stream);
+}
+
+// ------------------------------------------ peer-store exchange (mailboxes)
+namespace {
+size_t mb_up(size_t x) { return (x + 255) / 256 * 256; }
+}  // namespace
+
+extern "C" int aoakv_shard_mailbox_create(aoakv_shard_mailbox* mb_out, int32_t world,
+                                          int32_t rank, int32_t num_heads, int32_t head_dim,
+                                          int32_t max_proposals, void* ipc_handle_out) {
+  AOAKV_NVTX("aoakv_shard_mailbox_create");
+  AOAKV_CHECK_ARG(mb_out && ipc_handle_out, "shard_mailbox_create: NULL pointer argument");
+  AOAKV_CHECK_ARG(world >= 1 && world <= kShardMaxWorld && rank >= 0 && rank < world &&
+                      num_heads >= 1 && (head_dim == 64 || head_dim == 128) &&
+                      max_proposals >= 1 && max_proposals <= kShardMaxProp,
+                  "shard_mailbox_create: bad sizes");
+  *mb_out = nullptr;
+  aoakv_shard_mailbox_s* mb = new (std::nothrow) aoakv_shard_mailbox_s();
+  AOAKV_CHECK_ARG(mb != nullptr, "shard_mailbox_create: out of host memory");
+  mb->world = world;
+  mb->rank = rank;
+  mb->H = num_heads;
+  mb->D = head_dim;
+  mb->max_prop = max_proposals;
+  ShardMail& m = mb->mail;
+  size_t off = 0;
+  m.cand_off = 0;
+  off = mb_up(static_cast<size_t>(world) * num_heads * max_proposals * 8);
+  m.state_off = static_cast<uint32_t>(off);
+  off += mb_up(static_cast<size_t>(world) * num_heads * (head_dim + 1) * 4);
+  m.fc_off = static_cast<uint32_t>(off);
+  off += 256;
+  m.fs_off = static_cast<uint32_t>(off);
+  off += 256;
+  m.ep_off = static_cast<uint32_t>(off);
+  off += 256;
+  mb->bytes = off;
+  cudaError_t e = cudaGetDevice(&mb->device);
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&mb->local), mb->bytes);
+  if (e == cudaSuccess) e = cudaMemset(mb->local, 0, mb->bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, mb->local);
+  if (e != cudaSuccess) {
+    if (mb->local) cudaFree(mb->local);
+    delete mb;
+    AOAKV_CUDA_TRY(e, "shard_mailbox_create");
   }
-  if (sparse) {
-    AOAKV_CHECK_ARG(cand_all != nullptr, "shard_finish: cand_all is NULL");
-    AOAKV_CHECK_ARG(world >= 1 && world <= kShardMaxWorld && rank >= 0 && rank < world,
-                    "shard_finish: world must be in [1, 8] and rank in [0, world)");
-    AOAKV_CHECK_ARG(k - 1 <= kShardMaxProp && world * (k - 1) <= 2048,
-                    "shard_finish: world * (k - 1) candidates above 2048");
+  std::memcpy(ipc_handle_out, &h, sizeof(h));
+  m.base[rank] = mb->local;
+  *mb_out = mb;
+  return AOAKV_OK;
+}
+
+extern "C" int aoakv_shard_mailbox_connect(aoakv_shard_mailbox mb, const void* ipc_handles) {
+  AOAKV_NVTX("aoakv_shard_mailbox_connect");
+  AOAKV_CHECK_ARG(mb && ipc_handles, "shard_mailbox_connect: NULL pointer argument");
+  AOAKV_CHECK_ARG(!mb->connected, "shard_mailbox_connect: already connected");
+  const uint8_t* hs = static_cast<const uint8_t*>(ipc_handles);
+  for (int g = 0; g < mb->world; ++g) {
+    if (g == mb->rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, hs + static_cast<size_t>(g) * sizeof(h), sizeof(h));
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int j = 0; j < g; ++j)
+        if (mb->opened[j]) {
+          cudaIpcCloseMemHandle(mb->mail.base[j]);
+          mb->opened[j] = false;
+        }
+      AOAKV_CUDA_TRY(e, "shard_mailbox_connect: cudaIpcOpenMemHandle");
+    }
+    mb->mail.base[g] = static_cast<uint8_t*>(p);
+    mb->opened[g] = true;
   }
-  AOAKV_CHECK_ARG(num_local_pages <= plan->max_pages,
-                  "shard_finish: more local pages than the plan's max_pages");
-  a.k_new = static_cast<const __half*>(k_new);
-  a.v_new = static_cast<const __half*>(v_new);
-  a.n_pages = num_local_pages;
-  a.last_len = owns_last ? kv_last_page_len : 1;
-  a.shard = kShardFinish;
-  a.n_prop = sparse ? k - 1 : 0;
-  a.dense = num_total_pages <= k;
-  a.cand_in = static_cast<const uint2*>(cand_all);
-  a.world = sparse ? world : 1;
-  a.rank = sparse ? rank : 0;
-  a.owns_last = owns_last;
-  a.state_out = state_out;
-  a.selected_out = sparse ? selected_out : nullptr;
-  a.sel_cols = k - 1;
-  return launch_cluster_step(a, plan->kv_sw, plan->meta_map, plan->D, plan->cp,
-                             static_cast<cudaStream_t>(stream));
+  mb->connected = true;
+  return AOAKV_OK;
+}
+
+extern "C" int aoakv_shard_mailbox_destroy(aoakv_shard_mailbox mb) {
+  if (!mb) return AOAKV_OK;
+  for (int g = 0; g < mb->world; ++g)
+    if (mb->opened[g]) cudaIpcCloseMemHandle(mb->mail.base[g]);
+  if (mb->local) cudaFree(mb->local);
+  delete mb;
+  return AOAKV_OK;
+}
+
+extern "C" int aoakv_shard_propose_p2p(aoakv_step_plan plan, aoakv_shard_mailbox mb,
+                                       const void* q, const int32_t* kv_indices,
+                                       int32_t num_local_pages, int32_t num_total_pages,
+                                       int32_t page_lo, const int32_t* metadata_indices,
+                                       void* stream) {
+  AOAKV_NVTX("aoakv_shard_propose_p2p");
+  AOAKV_CHECK_ARG(mb != nullptr, "shard_propose_p2p: mailbox is NULL");
+  return shard_propose(plan, mb, q, kv_indices, num_local_pages, num_total_pages, page_lo,
+                       metadata_indices, nullptr, stream);
+}
+
+extern "C" int aoakv_shard_finish_p2p(aoakv_step_plan plan, aoakv_shard_mailbox mb,
+                                      const void* q, const void* k_new, const void* v_new,
+                                      const int32_t* kv_indices, int32_t num_local_pages,
+                                      int32_t num_total_pages, int32_t page_lo,
+                                      int32_t kv_last_page_len,
+                                      const int32_t* metadata_indices, int32_t* selected_out,
+                                      void* stream) {
+  AOAKV_NVTX("aoakv_shard_finish_p2p");
+  AOAKV_CHECK_ARG(mb != nullptr, "shard_finish_p2p: mailbox is NULL");
+  return shard_finish(plan, mb, q, k_new, v_new, kv_indices, num_local_pages, num_total_pages,
+                      page_lo, kv_last_page_len, metadata_indices, nullptr, 0, 0, nullptr,
+                      selected_out, stream);
+}
+
+extern "C" int aoakv_shard_merge_p2p(aoakv_shard_mailbox mb, int32_t with_proposals, void* o,
+                                     void* stream) {
+  AOAKV_NVTX("aoakv_shard_merge_p2p");
+  AOAKV_CHECK_ARG(mb && o, "shard_merge_p2p: NULL pointer argument");
+  AOAKV_CHECK_ARG(mb->connected, "shard_merge_p2p: mailbox not connected");
+  return launch_merge_mailbox(mb->mail, mb->world, mb->rank, mb->H, mb->D,
+                              with_proposals != 0, o, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int aoakv_step_launches(int32_t num_heads, int32_t head_dim, int32_t page_size,

@@ -743,6 +743,18 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     const int n_mine = N - (a.owns_last ? 1 : 0);  // local pages besides the last
     int w = 0;
     if (np > 0) {
+      if (a.p2p) {  // every GPU's proposals of this step are in this GPU's mailbox
+        if (tid == 0) {
+          const uint32_t* ep =
+              reinterpret_cast<const uint32_t*>(a.mail.base[me] + a.mail.ep_off);
+          const uint32_t target = (__ldcg(ep) + 1u) * static_cast<uint32_t>(H);
+          const uint32_t* fc =
+              reinterpret_cast<const uint32_t*>(a.mail.base[me] + a.mail.fc_off);
+          for (int g = 0; g < G; ++g) flag_wait_sys(fc + g, target, a.err);
+          asm volatile("fence.acq_rel.sys;" ::: "memory");
+        }
+        __syncthreads();
+      }
       for (int g = tid; g < G * np; g += kCsThreads) {
         const int gg = g / np, i = g - gg * np;
         const uint2 e = __ldcg(a.cand_in + (static_cast<size_t>(gg) * H + h) * np + i);
@@ -1208,13 +1220,33 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     for (int i = n_out + tid; i < a.n_prop; i += kCsThreads) out[i] = make_uint2(0u, 0xffffffffu);
   }
   __syncthreads();
+  if (shard == kShardPropose) {
+    // No decode. The barrier also makes every CTA's entries of cand_out
+    // visible to CTA 0, which (with mailboxes) forwards the head's list to
+    // every other GPU and raises fc there.
+    cluster_arrive_release();
+    cluster_wait_acquire();
+    if (a.p2p && c == 0) {
+      const int np = a.n_prop;
+      const uint2* src = a.cand_out + static_cast<size_t>(h) * np;
+      for (int g = 0; g < a.world; ++g) {
+        if (g == a.rank) continue;
+        uint2* dst = reinterpret_cast<uint2*>(a.mail.base[g] + a.mail.cand_off) +
+                     (static_cast<size_t>(a.rank) * H + h) * np;
+        for (int i = tid; i < np; i += kCsThreads) dst[i] = __ldcg(src + i);
+      }
+      __threadfence_system();
+      __syncthreads();
+      if (tid == 0)
+        for (int g = 0; g < a.world; ++g)
+          flag_add_release_sys(
+              reinterpret_cast<uint32_t*>(a.mail.base[g] + a.mail.fc_off) + a.rank, 1u);
+    }
+    return;
+  }
   // no shared memory of a peer is read after this point (the values read are
   // consumed), so the arrival need not order anything
   cluster_arrive_relaxed();
-  if (shard == kShardPropose) {  // no decode: wait until no peer reads this CTA
-    cluster_wait_acquire();
-    return;
-  }
 
   // ------------------------------------------------------------- 3 decode
   // q as column 0 of the B operand of S^T = K q^T (lanes 0..3: channels
@@ -1401,12 +1433,31 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         }
       }
       if (shard == kShardFinish) {  // this GPU's partial state
-        float* so = a.state_out + static_cast<size_t>(h) * (D + 1);
-        so[tid] = LL > 0.f ? OO / LL : 0.f;
-        if (tid == 0) so[D] = LL > 0.f ? (MM + log2f(LL)) * 0.6931471805599453f : -INFINITY;
+        const float ov = LL > 0.f ? OO / LL : 0.f;
+        const float lse = LL > 0.f ? (MM + log2f(LL)) * 0.6931471805599453f : -INFINITY;
+        const size_t at = static_cast<size_t>(h) * (D + 1);
+        if (!a.p2p) {
+          a.state_out[at + tid] = ov;
+          if (tid == 0) a.state_out[at + D] = lse;
+        } else {  // into every GPU's mailbox, this GPU's row
+          for (int g = 0; g < a.world; ++g) {
+            float* so = reinterpret_cast<float*>(a.mail.base[g] + a.mail.state_off) +
+                        static_cast<size_t>(a.rank) * H * (D + 1) + at;
+            so[tid] = ov;
+            if (tid == 0) so[D] = lse;
+          }
+        }
       } else {
         a.o[static_cast<size_t>(h) * D + tid] = __float2half_rn(LL > 0.f ? OO / LL : 0.f);
       }
+    }
+    if (shard == kShardFinish && a.p2p) {  // the head's state delivered: raise fs everywhere
+      __threadfence_system();
+      __syncthreads();
+      if (tid == 0)
+        for (int g = 0; g < a.world; ++g)
+          flag_add_release_sys(
+              reinterpret_cast<uint32_t*>(a.mail.base[g] + a.mail.fs_off) + a.rank, 1u);
     }
   }
   cluster_wait_acquire();  // every peer is past its last read of this CTA's memory

@@ -10,6 +10,22 @@
 
 namespace aoakv {
 
+constexpr int kShardMaxWorld = 8;
+
+// The exchange buffers of a page-range sharded sequence when the GPUs write
+// into each other's memory (aoakv_shard_mailbox_*): every rank's mailbox,
+// peers' mapped over NVLink, all with the same layout. Per mailbox:
+//   cand  [world, H, n_prop] {key, global page}: proposals, rank-major
+//   state [world, H, D + 1] fp32: partial states, rank-major
+//   fc[8], fs[8]: per sender, heads delivered (proposals / states), summed
+//                 over the steps
+//   ep[3]: proposal exchanges done, state exchanges done, heads merged in
+//          the current step (written by this GPU's merge only)
+struct ShardMail {
+  uint8_t* base[kShardMaxWorld];
+  uint32_t cand_off, state_off, fc_off, fs_off, ep_off;
+};
+
 struct ClusterStepArgs {
   const __half* q;              // [H, D]
   const __half* k_new;          // [H, D] the new token
@@ -61,10 +77,15 @@ struct ClusterStepArgs {
   int world, rank;
   int owns_last, dense;
   float* state_out;
+  // p2p != 0: the exchanges go through `mail` instead of the caller:
+  // propose forwards each head's list to every other GPU's mailbox and
+  // raises fc there; finish first waits for every GPU's fc, reads cand_in
+  // from its own mailbox and writes its state into every mailbox (fs).
+  int p2p;
+  ShardMail mail;
 };
 
 enum { kShardNone = 0, kShardPropose = 1, kShardFinish = 2 };
-constexpr int kShardMaxWorld = 8;
 
 // Sizes the kernel's shared memory is carved for.
 struct CsShape {

@@ -20,15 +20,24 @@ the same result comes from two kernel passes around two exchanges:
 5. the log-sum-exp merge (FlashInfer VariableLengthMergeStates' math,
    decode_attn.cuh:1035-1043) gives every GPU the same output.
 
-The data path crosses no GPU boundary except through these two all_gathers
-(NCCL over NVLink on GPUs, gloo in the CPU tests), both capturable in a CUDA
-graph with the three launches. The kernels are reached through an
-operations object: ``CudaShardOps`` calls libaoakv.so; tests pass another
-implementation of the same three operations to exercise this host logic on
-CPU ranks.
+The two exchanges run one of two ways:
+  exchange="nccl"  two all_gathers per layer through the process group
+                   (NCCL over NVLink on GPUs, gloo in the CPU tests);
+  exchange="p2p"   no collective: every GPU owns a mailbox in its memory,
+                   mapped into the other GPUs' address space (CUDA IPC), and
+                   the propose and finish kernels store their lists and
+                   partial states straight into every mailbox over NVLink
+                   and raise a per-rank flag there; the next pass on each GPU
+                   waits for all flags (bounded) — the exchange is fused into
+                   the kernels before it.
+Both are capturable in a CUDA graph with the three launches. The kernels
+are reached through an operations object: ``CudaShardOps`` calls
+libaoakv.so; tests pass another implementation of the same operations to
+exercise this host logic on CPU ranks.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -109,9 +118,11 @@ class ShardedDecoder:
 
     def __init__(self, group, num_heads: int, head_dim: int, page_size: int, page_budget: int,
                  score_mode: str = "aoakv", sink_first_page: bool = False, ops=None,
-                 rank: int | None = None):
+                 rank: int | None = None, exchange: str = "nccl", device=None):
         if score_mode not in ("aoakv", "quest"):
             raise ValueError("score_mode must be 'aoakv' or 'quest'")
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange must be 'nccl' or 'p2p'")
         self.group = group
         self.H, self.D, self.P = num_heads, head_dim, page_size
         self.page_budget = page_budget
@@ -120,6 +131,13 @@ class ShardedDecoder:
         self.rank = _group_rank(group) if rank is None else rank
         self.ops = ops if ops is not None else CudaShardOps(num_heads, head_dim, page_size,
                                                             page_budget, score_mode, self.sink)
+        self.exchange = exchange
+        self.mailbox = None
+        if exchange == "p2p":  # collective: every rank constructs its decoder together
+            kp = max(3, page_budget) if self.sink else page_budget
+            self.mailbox = ShardMailbox(group, self.rank, num_heads, head_dim, max(1, kp - 1),
+                                        device if device is not None else
+                                        torch.device("cuda", torch.cuda.current_device()))
 
     def budget(self, n_total: int) -> int:
         """Pages attended per head, the last page included
@@ -134,6 +152,13 @@ class ShardedDecoder:
         ops = self.ops
         k = self.budget(layer.n_total)
         sel = None
+        if self.mailbox is not None:
+            sparse = layer.n_total > k and k > 1
+            if sparse:
+                ops.propose_p2p(q, layer, self.mailbox)
+            sel = ops.finish_p2p(q, k_new, v_new, layer, self.mailbox, k - 1 if sparse else 0,
+                                 want_selected)
+            return ops.merge_p2p(self.mailbox, sparse, q.device), sel
         if layer.n_total > k and k > 1:
             ks = k - 1
             cand = ops.propose(q, layer, ks, self.sink and layer.page_lo == 0)  # [H, ks, 2]
@@ -144,6 +169,33 @@ class ShardedDecoder:
             state, _ = ops.finish(q, k_new, v_new, layer, None, 0, self.rank, False)
         states = _gather(state, self.group)  # [G, H, D + 1]
         return ops.merge(states), sel
+
+
+class ShardMailbox:
+    """This rank's mailbox of the peer-store exchange (aoakv_shard_mailbox_*):
+    created on every rank of ``group`` together; the 64-byte IPC handles are
+    all-gathered through the group and every rank maps the others'."""
+
+    def __init__(self, group, rank: int, num_heads: int, head_dim: int, max_proposals: int,
+                 device):
+        world = int(getattr(group, "world", 1)) if hasattr(group, "all_gather_stack") \
+            else dist.get_world_size(group)
+        self._lib = _lib.load()
+        self._h = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        _lib.call("aoakv_shard_mailbox_create", ctypes.byref(self._h), world, rank, num_heads,
+                  head_dim, max_proposals, handle)
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device)
+        every = _gather(mine, group).cpu().numpy().tobytes()  # [world, 64], rank order
+        _lib.call("aoakv_shard_mailbox_connect", self._h,
+                  (ctypes.c_uint8 * len(every)).from_buffer_copy(every))
+        self.world = world
+
+    def close(self):
+        """Only after every rank finished its last pass (a barrier)."""
+        if self._h:
+            self._lib.aoakv_shard_mailbox_destroy(self._h)
+            self._h = ctypes.c_void_p()
 
 
 class CudaShardOps:
@@ -195,6 +247,27 @@ class CudaShardOps:
                   None if cand_all is None else cand_all.contiguous().data_ptr(), world, rank,
                   state.data_ptr(), None if sel is None else sel.data_ptr(), self._stream(q))
         return state, sel
+
+    def propose_p2p(self, q, layer: ShardLayer, mailbox: ShardMailbox):
+        _lib.call("aoakv_shard_propose_p2p", self._plan(layer)._h, mailbox._h, q.data_ptr(),
+                  layer.kv_idx.data_ptr(), layer.n_local, layer.n_total, layer.page_lo,
+                  layer.meta_idx.data_ptr(), self._stream(q))
+
+    def finish_p2p(self, q, k_new, v_new, layer: ShardLayer, mailbox: ShardMailbox, ks: int,
+                   want_selected: bool):
+        sel = torch.empty(self.H, ks, dtype=torch.int32, device=q.device) \
+            if (want_selected and ks) else None
+        _lib.call("aoakv_shard_finish_p2p", self._plan(layer)._h, mailbox._h, q.data_ptr(),
+                  k_new.data_ptr(), v_new.data_ptr(), layer.kv_idx.data_ptr(), layer.n_local,
+                  layer.n_total, layer.page_lo, layer.last_len, layer.meta_idx.data_ptr(),
+                  None if sel is None else sel.data_ptr(), self._stream(q))
+        return sel
+
+    def merge_p2p(self, mailbox: ShardMailbox, with_proposals: bool, device):
+        o = torch.empty(self.H, self.D, dtype=torch.float16, device=device)
+        _lib.call("aoakv_shard_merge_p2p", mailbox._h, int(bool(with_proposals)), o.data_ptr(),
+                  torch.cuda.current_stream(device).cuda_stream)
+        return o
 
     def merge(self, states):
         G, H, Dp1 = states.shape

@@ -381,6 +381,46 @@ AOAKV_API int aoakv_merge_packed_states(const float* states, int32_t num_parts,
                                         int32_t num_heads, int32_t head_dim, void* o,
                                         void* stream);
 
+/* The same three passes with the two exchanges done by the kernels
+ * themselves (no collective library): each GPU owns a mailbox in its own
+ * memory, mapped into every other GPU's address space (CUDA IPC, NVLink
+ * peer access), and the propose pass stores each head's list straight into
+ * every other GPU's mailbox and raises a per-rank flag there (a release add
+ * at system scope); the finish pass waits for every GPU's flag (bounded:
+ * AOAKV_DEV_ERR_TIMEOUT after about a second, never a hang), ranks, decodes
+ * and stores its partial state into every mailbox the same way; the merge
+ * waits for every GPU's states and writes o. Per layer and token:
+ *   aoakv_shard_propose_p2p (only when a selection runs, as above),
+ *   aoakv_shard_finish_p2p, aoakv_shard_merge_p2p(with_proposals = whether
+ *   the propose pass ran).
+ * Every GPU must run the same passes in the same order. One mailbox serves
+ * all layers of a sequence (each pass completes its exchange before the
+ * next layer's can start on another GPU).
+ * Setup, once per process group: aoakv_shard_mailbox_create allocates and
+ * zero-fills this GPU's mailbox (it synchronises the device) and writes its
+ * 64-byte IPC handle; the caller all-gathers the handles (rank order) and
+ * passes them to aoakv_shard_mailbox_connect. Destroy only after every GPU
+ * has finished its last pass (a host barrier). max_proposals bounds k-1. */
+typedef struct aoakv_shard_mailbox_s* aoakv_shard_mailbox;
+AOAKV_API int aoakv_shard_mailbox_create(aoakv_shard_mailbox* mb_out, int32_t world,
+                                         int32_t rank, int32_t num_heads, int32_t head_dim,
+                                         int32_t max_proposals, void* ipc_handle_out);
+AOAKV_API int aoakv_shard_mailbox_connect(aoakv_shard_mailbox mb, const void* ipc_handles);
+AOAKV_API int aoakv_shard_mailbox_destroy(aoakv_shard_mailbox mb);
+AOAKV_API int aoakv_shard_propose_p2p(aoakv_step_plan plan, aoakv_shard_mailbox mb,
+                                      const void* q, const int32_t* kv_indices,
+                                      int32_t num_local_pages, int32_t num_total_pages,
+                                      int32_t page_lo, const int32_t* metadata_indices,
+                                      void* stream);
+AOAKV_API int aoakv_shard_finish_p2p(aoakv_step_plan plan, aoakv_shard_mailbox mb,
+                                     const void* q, const void* k_new, const void* v_new,
+                                     const int32_t* kv_indices, int32_t num_local_pages,
+                                     int32_t num_total_pages, int32_t page_lo,
+                                     int32_t kv_last_page_len, const int32_t* metadata_indices,
+                                     int32_t* selected_out, void* stream);
+AOAKV_API int aoakv_shard_merge_p2p(aoakv_shard_mailbox mb, int32_t with_proposals, void* o,
+                                    void* stream);
+
 /* aoakv_step_plan_info for a problem without a plan (the default plan). */
 AOAKV_API int aoakv_step_launches(int32_t num_heads, int32_t head_dim, int32_t page_size,
                                   int32_t num_kv_pages, int32_t page_budget,

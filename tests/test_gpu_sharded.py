@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from aoa_kv_b200 import sharded
+from aoa_kv_b200 import _lib, sharded
 from gen import gen_qkv
 from gpu_util import GpuLayer
 from helpers import selection_mismatch
@@ -122,3 +122,49 @@ def test_sharded_step_matches_oracle(cuda, world, S, budget, mode, sink, ties):
                 assert np.abs(o - o_ref).max() < 2e-3, f"rank {r}"
         else:
             assert np.abs(o - want_o).max() < 2e-3, f"rank {r}"
+
+
+class SoloGroup:
+    """The all_gather of a one-rank job."""
+    world = 1
+
+    @staticmethod
+    def all_gather_stack(t):
+        return t.unsqueeze(0)
+
+
+def test_sharded_p2p_one_rank_matches_oracle(cuda):
+    """The peer-store exchange with one rank (its own mailbox): two layers of
+    different lengths, one attended densely and one with a selection,
+    interleaved for three tokens, so the per-exchange counters advance
+    unevenly; every output and selection matches the oracle."""
+    H, D, P = 32, 128, 16
+    cases = []
+    for S, budget in ((700, 64), (8192 + 5, 64)):
+        q, K, V = gen_qkv(S + 11, H, S + 1, D, "outlier")
+        n_total, last_len = S // P + 1, S % P + 1
+        lay = GpuLayer(n_total + 2, H, D, P, seed=5)
+        lay.fill(K[:S], V[:S])
+        layer = sharded.ShardLayer(
+            kv=lay.kv, meta=lay.meta, vlog=lay.vlog, kv_idx=lay.kv_idx[:n_total].contiguous(),
+            meta_idx=lay.meta_idx, page_lo=0, n_local=n_total, n_total=n_total,
+            last_len=last_len, owns_last=True, last_phys=int(lay.kv_idx_np[n_total - 1]))
+        c = kt.LayerCache(n_total + 1, H, D, P)
+        idx = np.arange(n_total + 1, dtype=np.int32)
+        midx = np.arange(c.mcap, dtype=np.int32)
+        kt.append_prefill(c, idx, midx, -(-S // P), (S - 1) % P + 1, K[:S], V[:S])
+        want_o, want_sel = kt.step(q, K[S], V[S], c, idx, midx, n_total, last_len, budget,
+                                   "aoakv", False)
+        cases.append((layer, q, K[S], V[S], want_o, want_sel, n_total > budget))
+    dec = sharded.ShardedDecoder(SoloGroup(), H, D, P, 64, "aoakv", exchange="p2p")
+    for _ in range(3):
+        for layer, q, kn, vn, want_o, want_sel, sparse in cases:
+            o, sel = dec.step(layer, torch.from_numpy(q).cuda(), torch.from_numpy(kn).cuda(),
+                              torch.from_numpy(vn).cuda())
+            torch.cuda.synchronize()
+            assert np.abs(o.float().cpu().numpy() - want_o).max() < 2e-3
+            if sparse:
+                assert [sorted(r) for r in sel.cpu().numpy().tolist()] == \
+                    [sorted(r) for r in want_sel[:, :-1].tolist()]
+    assert _lib.device_error() == 0
+    dec.mailbox.close()
