@@ -66,6 +66,7 @@ SIGNATURES = {
                             _c_size, _c_p],
     "aoakv_step_plan_info": [_c_p, _c_i32, _c_i32, _c_ip, _c_ip],
     "aoakv_step_plan_destroy": [_c_p],
+    "aoakv_step_plan_set_rope": [_c_p, _c_f, _c_f],
     "aoakv_decode_step_batched": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_p, _c_p, _c_p, _c_p,
                                   _c_i32, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                                   _c_i32, _c_i32, _c_i32, _c_p, _c_p],

@@ -161,6 +161,7 @@ class InferenceController:
         self._step_ws_key = None
         self._layer_ptrs: dict = {}
         self._plans: dict = {}  # layer -> StepPlan (aoakv_step_plan_*)
+        self._rope = None  # (rope_scale, rope_theta) when RoPE is fused into decode_step
 
     @property
     def score_mode(self) -> int:
@@ -262,6 +263,15 @@ class InferenceController:
             self._layer_ptrs[layer_idx] = t
         return t
 
+    def fuse_rope(self, rope_scale: float = 1.0, rope_theta: float = 1e4):
+        """From now on decode_step takes q and k unrotated and applies RoPE
+        at the new token's position inside the step (the reference's
+        apply_rope_in_place before append_kv, fused); q and k are left
+        rotated in place. rope_scale <= 0 turns it off."""
+        self._rope = (float(rope_scale), float(rope_theta)) if rope_scale > 0 else None
+        for plan in self._plans.values():
+            plan.set_rope(*(self._rope or (0.0, 1.0)))
+
     def step_plan(self, layer_idx: int, max_ctas: int = 0):
         """The layer's StepPlan for the current budget (created on first use,
         re-created only when the budget or the CTA cap changes)."""
@@ -275,6 +285,8 @@ class InferenceController:
             plan = StepPlan(kv_p, kv_cap, meta_p, meta_cap, vlog_p, self.num_heads,
                             self.head_dim, self.page_size, budget, self.score_mode,
                             self.sink_first_page, max_ctas=max_ctas)
+            if self._rope:
+                plan.set_rope(*self._rope)
             self._plans[layer_idx] = plan
         return plan
 

@@ -151,6 +151,22 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar,
   return false;
 }
 
+// Rotate-half RoPE of one channel pair: x0 is channel j < D/2, x1 channel
+// j + D/2, at position pos; angle pos * rcp_scale * 2^(log2_rcp_theta *
+// 2j/D) in fp32, accurate sincosf, each product and sum rounded once (no
+// fused multiply-add), results rounded to fp16. The stand-alone RoPE kernel
+// and the fused step share it, so both give the same bits.
+__device__ __forceinline__ void rope_pair(float x0, float x1, int j, int D, float pos,
+                                          float rcp_scale, float log2_rcp_theta, __half* o0,
+                                          __half* o1) {
+  const float f = __fmul_rn(rcp_scale, exp2f(__fmul_rn(log2_rcp_theta,
+                                                        __fdiv_rn(2.f * j, static_cast<float>(D)))));
+  float s, c;
+  sincosf(__fmul_rn(pos, f), &s, &c);
+  *o0 = __float2half_rn(__fadd_rn(__fmul_rn(x0, c), -__fmul_rn(x1, s)));
+  *o1 = __float2half_rn(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s)));
+}
+
 // Flags in another GPU's memory (peer pointers over NVLink): a release add
 // and a bounded acquire wait, both at system scope. The wait returns false
 // and records AOAKV_DEV_ERR_TIMEOUT after about a second.

@@ -30,14 +30,9 @@ __global__ void rope_kernel(__half* q, __half* k, int seq_len, int past_kv_len, 
   const int t = static_cast<int>((row % rows) / H);
   const float pos = static_cast<float>(past_kv_len + t);
   const int half = D / 2;
-  for (int j = lane; j < half; j += 32) {
-    const float f = rcp_scale * exp2f(log2_rcp_theta * (2.f * j / D));
-    float s, c;
-    sincosf(pos * f, &s, &c);
-    const float x0 = __half2float(x[j]), x1 = __half2float(x[j + half]);
-    x[j] = __float2half_rn(x0 * c - x1 * s);
-    x[j + half] = __float2half_rn(x1 * c + x0 * s);
-  }
+  for (int j = lane; j < half; j += 32)
+    rope_pair(__half2float(x[j]), __half2float(x[j + half]), j, D, pos, rcp_scale,
+              log2_rcp_theta, &x[j], &x[j + half]);
 }
 
 }  // namespace

@@ -42,6 +42,8 @@ struct aoakv_step_plan_s {
   CUtensorMap kv_sw;             // cluster: K/V tiles, 128-byte swizzle
   CUtensorMap meta_map;          // cluster: metadata tiles
   CUtensorMap kv_plain;          // chain: the decode kernel's K/V boxes
+  bool rope;                     // RoPE fused into the step (aoakv_step_plan_set_rope)
+  float rope_scale, rope_theta;
 };
 
 namespace aoakv {
@@ -170,6 +172,12 @@ int run_cluster(const aoakv_step_plan_s* p, const void* q, const void* k_new, co
   a.selected_out = selected_out;
   a.sel_cols = k_pages;
   a.err = dev_error_ptr();
+  if (p->rope) {
+    a.rope = 1;
+    a.rope_pos = (N - 1) * p->P + last_len - 1;
+    a.rope_rcp_scale = 1.f / p->rope_scale;
+    a.rope_log2_rcp_theta = std::log2(1.f / p->rope_theta);
+  }
   return launch_cluster_step(a, p->kv_sw, p->meta_map, p->D, p->cp, s);
 }
 
@@ -188,6 +196,12 @@ int run_chain(const aoakv_step_plan_s* p, const void* q, const void* k_new, cons
                          std::to_string(lay.total));
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const int n_meta = (N + P - 1) / P;
+  if (p->rope) {  // q and k_new rotated in place at the new token's position first
+    const int rc0 = aoakv_apply_rope_in_place(const_cast<void*>(q), const_cast<void*>(k_new), 1,
+                                              (N - 1) * P + last_len - 1, H, D, p->rope_scale,
+                                              p->rope_theta, s);
+    if (rc0) return rc0;
+  }
   int rc = aoakv_append_kv_cache_decode(k_new, v_new, p->kv, kv_indices, N, last_len, p->kv_cap,
                                         p->meta, meta_indices, n_meta, (N - 1) % P + 1,
                                         p->meta_cap, p->vlog, H, D, P, AOAKV_LAYOUT_NHD, s);
@@ -345,6 +359,17 @@ extern "C" int aoakv_step_plan_info(aoakv_step_plan plan, int32_t num_kv_pages,
   AOAKV_CHECK_ARG(num_kv_pages >= 1, "step plan: num_kv_pages must be >= 1");
   if (kernels_out) *kernels_out = plan_kernels(plan, num_kv_pages, want_selected != 0);
   if (cluster_out) *cluster_out = plan->cluster_ok ? plan->cp.cluster : 0;
+  return AOAKV_OK;
+}
+
+extern "C" int aoakv_step_plan_set_rope(aoakv_step_plan plan, float rope_scale,
+                                        float rope_theta) {
+  AOAKV_CHECK_ARG(plan != nullptr, "step_plan_set_rope: plan is NULL");
+  AOAKV_CHECK_ARG(rope_scale <= 0.f || rope_theta > 0.f,
+                  "step_plan_set_rope: rope_theta must be > 0");
+  plan->rope = rope_scale > 0.f;
+  plan->rope_scale = rope_scale;
+  plan->rope_theta = rope_theta;
   return AOAKV_OK;
 }
 

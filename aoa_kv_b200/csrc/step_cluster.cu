@@ -458,6 +458,26 @@ struct LaneVec<2> {
   using T = uint32_t;
 };
 
+// RoPE of the lane's CPL channels of one row held as floats (channel
+// lane * CPL + t); the partner of a channel (j <-> j + D/2) sits 16 lanes
+// away. The values come back rounded to fp16, as the stand-alone kernel
+// stores them. Every lane of the warp takes part.
+template <int CPL>
+__device__ __forceinline__ void cs_rope_lane(float v[CPL], int lane, int D, float pos,
+                                             float rcp_scale, float log2_rcp_theta) {
+  float p[CPL];
+#pragma unroll
+  for (int t = 0; t < CPL; ++t) p[t] = __shfl_xor_sync(0xffffffffu, v[t], 16);
+  const bool lo = lane < 16;
+#pragma unroll
+  for (int t = 0; t < CPL; ++t) {
+    __half o0, o1;
+    rope_pair(lo ? v[t] : p[t], lo ? p[t] : v[t], (lane & 15) * CPL + t, D, pos, rcp_scale,
+              log2_rcp_theta, &o0, &o1);
+    v[t] = __half2float(lo ? o0 : o1);
+  }
+}
+
 template <int D, int C>
 __global__ void __launch_bounds__(kCsThreads, 1)
     cluster_step_kernel(const __grid_constant__ CUtensorMap kv_map,
@@ -477,6 +497,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   __shared__ uint32_t kmin_s, kmax_s;     // key range of this CTA's ranked scores
   __shared__ int cnt_s;
   __shared__ int peer_m[C], peer_ovf[C];  // every CTA's candidate count and overflow flag
+  __shared__ __align__(16) __half q_rot[128];  // head h's q after RoPE (RoPE fused)
 
   cg::cluster_group cluster = cg::this_cluster();
   const int c = static_cast<int>(cluster.block_rank());
@@ -576,6 +597,14 @@ __global__ void __launch_bounds__(kCsThreads, 1)
 
   float qv[CPL];
   load_row<CPL>(a.q + static_cast<size_t>(h) * D + lane * CPL, qv);
+  const float rope_pos = static_cast<float>(a.rope_pos >= 0 ? a.rope_pos
+                                                            : (N - 1) * P + a.last_len - 1);
+  if (a.rope) {  // every warp rotates its copy; warp 0 keeps it for the decode
+    cs_rope_lane<CPL>(qv, lane, D, rope_pos, a.rope_rcp_scale, a.rope_log2_rcp_theta);
+    if (warp == 0)
+#pragma unroll
+      for (int t = 0; t < CPL; ++t) q_rot[lane * CPL + t] = __float2half_rn(qv[t]);
+  }
   uint32_t msk[CPL / 2];
 #pragma unroll
   for (int i = 0; i < CPL / 2; ++i)
@@ -911,12 +940,12 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       peer_m[tid] = px->m;
       peer_ovf[tid] = px->ovf;
     }
+    uint2* gkp = reinterpret_cast<uint2*>(gkey);  // {key, page} pairs: gkey and gpos regions
     if (gatherable)
       for (int g = tid; g < C * K; g += kCsThreads) {
         const int cc = g / K;
         const uint4 e = cluster.map_shared_rank(lst, cc)[g - cc * K];
-        gkey[g] = e.x;
-        gpos[g] = e.y;
+        gkp[g] = make_uint2(e.x, e.y);
       }
     __syncthreads();
 #pragma unroll
@@ -940,19 +969,22 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         i = tid / tpc;
         const int sub = tid - i * tpc;
         if (i < mine) {
-          const uint32_t mk = gkey[c * K + i], mpos = gpos[c * K + i];
+          const uint2 me = gkp[c * K + i];
 #pragma unroll
           for (int cc = 0; cc < C; ++cc) {
             if (cc == c) continue;
-            for (int g = cc * K + sub; g < (cc + 1) * K; g += tpc)
-              r += cs_beats(gkey[g], gpos[g], mk, mpos);
+#pragma unroll 4
+            for (int g = cc * K + sub; g < (cc + 1) * K; g += tpc) {
+              const uint2 e = gkp[g];
+              r += cs_beats(e.x, e.y, me.x, me.y);
+            }
           }
         }
         for (int off = tpc >> 1; off > 0; off >>= 1) r += __shfl_xor_sync(0xffffffffu, r, off);
         r += i;
         win = i < mine && sub == 0 && r < K;
       } else if (i < mine) {
-        const uint32_t mk = gkey[c * K + i], mpos = gpos[c * K + i];
+        const uint32_t mk = gkp[c * K + i].x, mpos = gkp[c * K + i].y;
         int lo[C], hi[C];  // binary searches of all lists in lockstep
 #pragma unroll
         for (int cc = 0; cc < C; ++cc) {
@@ -966,7 +998,8 @@ __global__ void __launch_bounds__(kCsThreads, 1)
           for (int cc = 0; cc < C; ++cc) {
             if (lo[cc] < hi[cc]) {
               const int mid = (lo[cc] + hi[cc]) >> 1;
-              if (cs_beats(gkey[mid], gpos[mid], mk, mpos)) lo[cc] = mid + 1;
+              const uint2 e = gkp[mid];
+              if (cs_beats(e.x, e.y, mk, mpos)) lo[cc] = mid + 1;
               else hi[cc] = mid;
               more = true;
             }
@@ -1257,9 +1290,15 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   for (int kk = 0; kk < NK; ++kk) {
     qb[kk][0] = qb[kk][1] = 0u;
     if (lane < 4) {
-      const uint32_t* qw = reinterpret_cast<const uint32_t*>(a.q + static_cast<size_t>(h) * D);
-      qb[kk][0] = __ldcg(qw + kk * 8 + lane);
-      qb[kk][1] = __ldcg(qw + kk * 8 + 4 + lane);
+      if (a.rope) {
+        const uint32_t* qw = reinterpret_cast<const uint32_t*>(q_rot);
+        qb[kk][0] = qw[kk * 8 + lane];
+        qb[kk][1] = qw[kk * 8 + 4 + lane];
+      } else {
+        const uint32_t* qw = reinterpret_cast<const uint32_t*>(a.q + static_cast<size_t>(h) * D);
+        qb[kk][0] = __ldcg(qw + kk * 8 + lane);
+        qb[kk][1] = __ldcg(qw + kk * 8 + 4 + lane);
+      }
     }
   }
   float m = -INFINITY, l = 0.f, acc[NK][4];
@@ -1296,6 +1335,14 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     __half* mv = a.meta + ((static_cast<size_t>(app_mpid) * 2 + 1) * P + mentry) * HD + col;
     if (is_last) {
       kn = *reinterpret_cast<const Vec*>(a.k_new + col);
+      if (a.rope) {  // rotate the new key; the rotated key also goes back in place
+        float kf[CPL];
+        load_row<CPL>(reinterpret_cast<const __half*>(&kn), kf);
+        cs_rope_lane<CPL>(kf, lane, D, rope_pos, a.rope_rcp_scale, a.rope_log2_rcp_theta);
+#pragma unroll
+        for (int t = 0; t < CPL; ++t) reinterpret_cast<__half*>(&kn)[t] = __float2half_rn(kf[t]);
+        *reinterpret_cast<Vec*>(const_cast<__half*>(a.k_new) + col) = kn;
+      }
       vn = *reinterpret_cast<const Vec*>(a.v_new + col);
       if (entry > 0 && meta_ok) {
         mxo = *reinterpret_cast<const Vec*>(mk);
@@ -1461,6 +1508,8 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     }
   }
   cluster_wait_acquire();  // every peer is past its last read of this CTA's memory
+  // the rotated q in place, once every CTA of the cluster has read the input
+  if (a.rope && c == 0 && tid < D) const_cast<__half*>(a.q)[static_cast<size_t>(h) * D + tid] = q_rot[tid];
 }
 
 using KernelFn = void (*)(CUtensorMap, CUtensorMap, ClusterStepArgs, CsShape);

@@ -83,6 +83,12 @@ struct ClusterStepArgs {
   // from its own mailbox and writes its state into every mailbox (fs).
   int p2p;
   ShardMail mail;
+  // RoPE fused into the step (rope != 0): q and k_new arrive unrotated and
+  // are rotated at position rope_pos (< 0: the request's own new-token
+  // position, (n_pages - 1) * P + last_len - 1) before use; the rotated q
+  // and k_new are written back in place (not by a propose pass).
+  int rope, rope_pos;
+  float rope_rcp_scale, rope_log2_rcp_theta;
 };
 
 enum { kShardNone = 0, kShardPropose = 1, kShardFinish = 2 };

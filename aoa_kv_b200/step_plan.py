@@ -31,6 +31,7 @@ class StepPlan:
                   (_lib.PLAN_CHAIN if chain else 0) | (_lib.PLAN_SHARD if shard else 0))
         self.page_budget = int(page_budget)
         self.max_ctas = int(max_ctas)
+        self.rope = None
 
     def run(self, q, k_new, v_new, o, kv_indices, num_kv_pages, kv_last_page_len,
             metadata_indices, selected=None, workspace=None, workspace_bytes=0, stream=None):
@@ -38,6 +39,12 @@ class StepPlan:
                   _addr(kv_indices), int(num_kv_pages), int(kv_last_page_len),
                   _addr(metadata_indices), _addr(selected), _addr(workspace),
                   int(workspace_bytes), stream)
+
+    def set_rope(self, rope_scale: float = 1.0, rope_theta: float = 1e4):
+        """Fuse RoPE into run(): q and k_new arrive unrotated and are left
+        rotated in place (rope_scale <= 0 turns it off)."""
+        _lib.call("aoakv_step_plan_set_rope", self._h, float(rope_scale), float(rope_theta))
+        self.rope = (float(rope_scale), float(rope_theta)) if rope_scale > 0 else None
 
     def info(self, num_kv_pages, want_selected=False):
         """(kernels per step, CTAs per head of the cluster launch or 0)."""

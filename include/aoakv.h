@@ -333,6 +333,16 @@ AOAKV_API int aoakv_step_plan_info(aoakv_step_plan plan, int32_t num_kv_pages,
                                    int32_t want_selected, int32_t* kernels_out,
                                    int32_t* cluster_out);
 AOAKV_API int aoakv_step_plan_destroy(aoakv_step_plan plan);
+/* RoPE fused into the plan's step (the reference applies it as its own op
+ * just before the append, utils/__init__.py:25-52 / decode_page.cuh:786-869):
+ * with rope_scale > 0, aoakv_step_plan_run takes q and k_new unrotated,
+ * rotates both at the new token's position ((num_kv_pages - 1) * page_size +
+ * kv_last_page_len - 1) exactly as aoakv_apply_rope_in_place does (same
+ * bits), uses them, and leaves the rotated q and k_new in place.
+ * rope_scale <= 0 turns it off (the default). Not used by the shard passes
+ * or the batched step. Call it between steps, not while one runs. */
+AOAKV_API int aoakv_step_plan_set_rope(aoakv_step_plan plan, float rope_scale,
+                                       float rope_theta);
 
 /* One sequence split over GPUs by page range (config 5's 128K-token decode;
  * the reference runs it on one GPU only). GPU g holds global pages

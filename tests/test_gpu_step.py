@@ -328,3 +328,54 @@ def test_step_back_to_back_same_layer(cuda, start_pages, budget, mode, sink):
     assert np.array_equal(after.meta, ref.meta)
     assert np.abs(after.vlog.astype(np.float32) - ref.vlog.astype(np.float32)).max() <= 2e-3
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("impl", ["cluster", "chain"])
+@pytest.mark.parametrize("S,budget,D", [(8192 + 7, 64, 128), (2000, 16, 64), (16 * 40, 64, 128)])
+def test_step_with_fused_rope_equals_rope_then_step(cuda, impl, S, budget, D):
+    """RoPE fused into the step (aoakv_step_plan_set_rope) gives the same bits
+    as aoakv_apply_rope_in_place followed by the step: output, selection,
+    the cache afterwards, and q and k left rotated in place; and it matches
+    the oracle's RoPE (kernel_tree.apply_rope) followed by kernel_tree.step."""
+    H, P = 32, 16
+    q, K, V = gen_qkv(S + D, H, S, D, "outlier")
+    n, last = (S + P - 1) // P, (S - 1) % P + 1
+    lays = []
+    for fused in (False, True):
+        lay = GpuLayer(n + 3, H, D, P, seed=9)
+        lay.fill(K[:-1], V[:-1])
+        plan = StepPlan(lay.kv, lay.cap, lay.meta, lay.mcap, lay.vlog, H, D, P, budget,
+                        _lib.SCORE_AOAKV, chain=impl == "chain")
+        qd, kd, vd = (torch.from_numpy(x).cuda() for x in (q, K[-1], V[-1]))
+        if fused:
+            plan.set_rope(1.0, 1e4)
+        else:
+            _lib.call("aoakv_apply_rope_in_place", ptr(qd), ptr(kd), 1, S - 1, H, D, 1.0, 1e4,
+                      stream())
+        ws_n = _lib.size_query("aoakv_step_workspace_size", H, D, lay.cap, budget)
+        ws = torch.zeros(ws_n, dtype=torch.uint8, device="cuda")
+        o = torch.empty(H, D, dtype=torch.float16, device="cuda")
+        sel = torch.full((H, budget), -9, dtype=torch.int32, device="cuda")
+        plan.run(qd, kd, vd, o, lay.kv_idx, n, last, lay.meta_idx, sel, ws, ws_n, stream())
+        torch.cuda.synchronize()
+        lays.append((o.cpu(), sel.cpu(), qd.cpu(), kd.cpu(), lay.kv.cpu(), lay.meta.cpu(),
+                     lay.vlog.cpu(), lay))
+    (o0, s0, q0, k0, kv0, m0, v0, lay0), (o1, s1, q1, k1, kv1, m1, v1, _) = lays
+    assert torch.equal(q0, q1) and torch.equal(k0, k1)
+    assert torch.equal(kv0, kv1) and torch.equal(m0, m1) and torch.equal(v0, v1)
+    assert torch.equal(s0, s1) and torch.equal(o0, o1)
+    # against the oracle: rotate, then the kernel-tree step
+    qr = kt.apply_rope(q[None], S - 1)[0]
+    kr = kt.apply_rope(K[-1][None], S - 1)[0]
+    np.testing.assert_allclose(q1.float().numpy(), qr.astype(np.float32), rtol=2e-3, atol=3e-3)
+    ref = kt.LayerCache(lay0.cap, H, D, P)
+    lay_ref = GpuLayer(n + 3, H, D, P, seed=9)
+    lay_ref.fill(K[:-1], V[:-1])
+    ref = lay_ref.snapshot()
+    want_o, want_sel = kt.step(q1.numpy(), k1.numpy(), V[-1], ref, lay_ref.kv_idx_np,
+                               lay_ref.meta_idx_np, n, last, budget, "aoakv", False)
+    got = logical(s1.numpy(), lay_ref.kv_idx_np, n)
+    want = logical(want_sel, lay_ref.kv_idx_np, n)
+    if got == want:
+        assert np.abs(o1.float().numpy() - want_o).max() < 2e-3
+    assert _lib.device_error() == 0
