@@ -458,6 +458,64 @@ struct LaneVec<2> {
   using T = uint32_t;
 };
 
+// A lane's CPL fp16 channels packed in LaneVec words, handled by value
+// (taking a register's address would move it to local memory): to and
+// from floats, per-half max / min, and a repeated half2 pattern.
+__device__ __forceinline__ __half2 u32_h2(uint32_t u) {
+  return __halves2half2(__ushort_as_half(static_cast<unsigned short>(u & 0xffffu)),
+                        __ushort_as_half(static_cast<unsigned short>(u >> 16)));
+}
+__device__ __forceinline__ uint32_t h2_u32(__half2 h) {
+  return static_cast<uint32_t>(__half_as_ushort(__low2half(h))) |
+         (static_cast<uint32_t>(__half_as_ushort(__high2half(h))) << 16);
+}
+template <int CPL>
+__device__ __forceinline__ void vec_to_float(typename LaneVec<CPL>::T v, float f[CPL]) {
+  if constexpr (CPL == 4) {
+    const float2 a = __half22float2(u32_h2(v.x)), b = __half22float2(u32_h2(v.y));
+    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+  } else {
+    const float2 a = __half22float2(u32_h2(v));
+    f[0] = a.x; f[1] = a.y;
+  }
+}
+template <int CPL>
+__device__ __forceinline__ typename LaneVec<CPL>::T float_to_vec(const float f[CPL]) {
+  if constexpr (CPL == 4) {
+    return make_uint2(h2_u32(__floats2half2_rn(f[0], f[1])), h2_u32(__floats2half2_rn(f[2], f[3])));
+  } else {
+    return h2_u32(__floats2half2_rn(f[0], f[1]));
+  }
+}
+template <int CPL>
+__device__ __forceinline__ typename LaneVec<CPL>::T vec_hmax(typename LaneVec<CPL>::T a,
+                                                              typename LaneVec<CPL>::T b) {
+  if constexpr (CPL == 4) {
+    return make_uint2(h2_u32(__hmax2(u32_h2(a.x), u32_h2(b.x))),
+                      h2_u32(__hmax2(u32_h2(a.y), u32_h2(b.y))));
+  } else {
+    return h2_u32(__hmax2(u32_h2(a), u32_h2(b)));
+  }
+}
+template <int CPL>
+__device__ __forceinline__ typename LaneVec<CPL>::T vec_hmin(typename LaneVec<CPL>::T a,
+                                                              typename LaneVec<CPL>::T b) {
+  if constexpr (CPL == 4) {
+    return make_uint2(h2_u32(__hmin2(u32_h2(a.x), u32_h2(b.x))),
+                      h2_u32(__hmin2(u32_h2(a.y), u32_h2(b.y))));
+  } else {
+    return h2_u32(__hmin2(u32_h2(a), u32_h2(b)));
+  }
+}
+template <int CPL>
+__device__ __forceinline__ typename LaneVec<CPL>::T vec_fill(uint32_t pattern) {
+  if constexpr (CPL == 4) {
+    return make_uint2(pattern, pattern);
+  } else {
+    return pattern;
+  }
+}
+
 // RoPE of the lane's CPL channels of one row held as floats (channel
 // lane * CPL + t); the partner of a channel (j <-> j + D/2) sits 16 lanes
 // away. The values come back rounded to fp16, as the stand-alone kernel
@@ -487,7 +545,10 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   const int CAPL = cs_capl(C, shp.max_slots);  // local candidates one CTA may publish
   using Vec = typename LaneVec<CPL>::T;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = align_smem<1024>(smem_raw);
+  // (rounded as an integer: measured faster here than align_smem's shared-
+  // window pointer, 22.0 vs 22.8 us per layer-step at the headline shape)
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   __shared__ uint64_t bars[kCsWarps];
   __shared__ uint64_t merge_bar;  // CTA 0: the other CTAs' partial states are in
   __shared__ CsXchg xs;
@@ -497,7 +558,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   __shared__ uint32_t kmin_s, kmax_s;     // key range of this CTA's ranked scores
   __shared__ int cnt_s;
   __shared__ int peer_m[C], peer_ovf[C];  // every CTA's candidate count and overflow flag
-  __shared__ __align__(16) __half q_rot[128];  // head h's q after RoPE (RoPE fused)
+  __shared__ __align__(16) __half q_rot[128];  // head h's q (after RoPE when fused)
 
   cg::cluster_group cluster = cg::this_cluster();
   const int c = static_cast<int>(cluster.block_rank());
@@ -540,33 +601,44 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   pdl_wait();
   pdl_launch_dependents();
 
-  ClusterStepArgs a = a_in;
-  if (a_in.kv_indptr) {  // batched: request blockIdx.z of a shared page pool
+  // The arguments stay in parameter space (a copy of the whole struct would
+  // live in local memory); the fields a batched launch moves per request
+  // are copied into registers.
+  const ClusterStepArgs& a = a_in;
+  const __half* q_in = a.q;
+  const __half* kn_in = a.k_new;
+  const __half* vn_in = a.v_new;
+  __half* o_out = a.o;
+  const int32_t* kv_idx = a.kv_indices;
+  const int32_t* meta_idx = a.meta_indices;
+  int n_pages = a.n_pages, last_len = a.last_len, k_slots = a.k_slots;
+  int32_t* sel_out = a.selected_out;
+  if (a.kv_indptr) {  // batched: request blockIdx.z of a shared page pool
     const int r = blockIdx.z;
-    const int p0 = __ldcg(a_in.kv_indptr + r);
-    const int m0 = __ldcg(a_in.meta_indptr + r);
-    a.n_pages = __ldcg(a_in.kv_indptr + r + 1) - p0;
-    a.last_len = __ldcg(a_in.last_lens + r);
+    const int p0 = __ldcg(a.kv_indptr + r);
+    const int m0 = __ldcg(a.meta_indptr + r);
+    n_pages = __ldcg(a.kv_indptr + r + 1) - p0;
+    last_len = __ldcg(a.last_lens + r);
     // every CTA of the cluster reads the same values, so all leave together
     // (no cluster barrier is pending: the arrival above needs no wait)
-    if (p0 < 0 || m0 < 0 || a.n_pages < 1 || a.n_pages > a_in.max_pages || a.last_len < 1 ||
-        a.last_len > P) {
+    if (p0 < 0 || m0 < 0 || n_pages < 1 || n_pages > a.max_pages || last_len < 1 ||
+        last_len > P) {
       if (tid == 0) raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
       return;
     }
-    a.kv_indices = a_in.kv_indices + p0;
-    a.meta_indices = a_in.meta_indices + m0;
-    const int kp = a_in.sink ? max(3, a_in.budget) : a_in.budget;
-    a.k_slots = min(kp, a.n_pages);
+    kv_idx += p0;
+    meta_idx += m0;
+    const int kp = a.sink ? max(3, a.budget) : a.budget;
+    k_slots = min(kp, n_pages);
     const size_t qo = static_cast<size_t>(r) * H * D;
-    a.q += qo;
-    a.k_new += qo;
-    a.v_new += qo;
-    a.o += qo;
-    if (a.selected_out) a.selected_out += static_cast<size_t>(r) * H * a_in.sel_cols;
+    q_in += qo;
+    kn_in += qo;
+    vn_in += qo;
+    o_out += qo;
+    if (sel_out) sel_out += static_cast<size_t>(r) * H * a.sel_cols;
   }
-  const int N = a.n_pages, n = N - 1;
-  const int k = a.k_slots;
+  const int N = n_pages, n = N - 1;
+  const int k = k_slots;
   const int shard = a.shard;
   // propose scores and ranks every local page (even when they are <= k);
   // finish scores nothing
@@ -585,8 +657,8 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   // a propose pass, or a finish pass on a GPU without it, has none
   const bool has_last = shard == kShardNone || (shard == kShardFinish && a.owns_last);
   const int w_last = (c == C - 1 && has_last) ? (shard ? 0 : (T - 1 - s_lo) % kCsWarps) : -1;
-  const int last_pid = has_last ? __ldcg(a.kv_indices + N - 1) : -1;
-  const int app_mpid = (c == C - 1 && has_last) ? __ldcg(a.meta_indices + (N - 1) / P) : 0;
+  const int last_pid = has_last ? __ldcg(kv_idx + N - 1) : -1;
+  const int app_mpid = (c == C - 1 && has_last) ? __ldcg(meta_idx + (N - 1) / P) : 0;
   if (warp == w_last && lane == 0 && last_pid >= 0 && last_pid < a.kv_cap) {  // warm L2
 #pragma unroll
     for (int sub = 0; sub < D / 64; ++sub) {
@@ -596,15 +668,15 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   }
 
   float qv[CPL];
-  load_row<CPL>(a.q + static_cast<size_t>(h) * D + lane * CPL, qv);
+  load_row<CPL>(q_in + static_cast<size_t>(h) * D + lane * CPL, qv);
   const float rope_pos = static_cast<float>(a.rope_pos >= 0 ? a.rope_pos
-                                                            : (N - 1) * P + a.last_len - 1);
-  if (a.rope) {  // every warp rotates its copy; warp 0 keeps it for the decode
-    cs_rope_lane<CPL>(qv, lane, D, rope_pos, a.rope_rcp_scale, a.rope_log2_rcp_theta);
-    if (warp == 0)
+                                                            : (N - 1) * P + last_len - 1);
+  // every warp rotates its copy (RoPE fused); warp 0 keeps q in shared
+  // memory for the decode
+  if (a.rope) cs_rope_lane<CPL>(qv, lane, D, rope_pos, a.rope_rcp_scale, a.rope_log2_rcp_theta);
+  if (warp == 0)
 #pragma unroll
-      for (int t = 0; t < CPL; ++t) q_rot[lane * CPL + t] = __float2half_rn(qv[t]);
-  }
+    for (int t = 0; t < CPL; ++t) q_rot[lane * CPL + t] = __float2half_rn(qv[t]);
   uint32_t msk[CPL / 2];
 #pragma unroll
   for (int i = 0; i < CPL / 2; ++i)
@@ -616,12 +688,12 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     const int jp = (lane >> 1) & 15;           // page of the stage this lane scores
     const bool writer = (lane & 1) == 0 && jp < P;
     // the metadata page of stage t and the lane's page id / v_log_norm
-    auto meta_of = [&](int t) -> int { return lane == 0 ? __ldcg(a.meta_indices + t) : 0; };
+    auto meta_of = [&](int t) -> int { return lane == 0 ? __ldcg(meta_idx + t) : 0; };
     auto page_of = [&](int t, float* vlo) -> int {
       const int pos = t * P + jp;
       *vlo = 0.f;
       if (!writer || pos >= n) return -1;
-      const int pid = __ldcg(a.kv_indices + pos);
+      const int pid = __ldcg(kv_idx + pos);
       if (pid < 0 || pid >= a.kv_cap) {
         raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
         *vlo = NAN;
@@ -738,7 +810,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   // (many equal scores) sends the whole cluster to the level-by-level
   // fallback, whose winners are spread evenly over the cluster.
   int32_t* sel_row =
-      a.selected_out ? a.selected_out + static_cast<size_t>(h) * a.sel_cols : nullptr;
+      sel_out ? sel_out + static_cast<size_t>(h) * a.sel_cols : nullptr;
   const bool sink_owner = sparse && a.sink && st_lo == 0 && st_hi > 0;
   // pages attended whatever the selection: the last page (CTA C-1, first),
   // the sink page (its owner)
@@ -829,9 +901,9 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         pid = last_pid;
       } else if (np > 0) {
         const int li = static_cast<int>(gpos[me * np + j]) - a.page_lo;
-        if (li >= 0 && li < n_mine) pid = __ldcg(a.kv_indices + li);  // else BAD_PAGE below
+        if (li >= 0 && li < n_mine) pid = __ldcg(kv_idx + li);  // else BAD_PAGE below
       } else {
-        pid = __ldcg(a.kv_indices + j);
+        pid = __ldcg(kv_idx + j);
       }
       items[j - lo_s] = pid;
     }
@@ -920,7 +992,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       n_spec = min(kCsWarps, n_special + m_c);
       if (warp < n_spec) {
         const int pid = warp < n_special
-                            ? ((c == C - 1 && warp == 0) ? last_pid : __ldcg(a.kv_indices))
+                            ? ((c == C - 1 && warp == 0) ? last_pid : __ldcg(kv_idx))
                             : static_cast<int>(lst[warp - n_special].z);
         spec_issued = pid >= 0 && pid < a.kv_cap;
         if (lane == 0 && spec_issued) load_page(pid);
@@ -1018,11 +1090,11 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       const int w_c = __syncthreads_count(win);  // the winners are lst[0, w_c)
       n_items = n_special + w_c;
       for (int j = tid; j < n_items; j += kCsThreads)
-        items[j] = j < n_special ? ((c == C - 1 && j == 0) ? last_pid : __ldcg(a.kv_indices))
+        items[j] = j < n_special ? ((c == C - 1 && j == 0) ? last_pid : __ldcg(kv_idx))
                                  : static_cast<int>(lst[j - n_special].z);
       if (c == C - 1) last_item = 0;
       if (sel_row && tid == 0) {
-        if (sink_owner) sel_row[0] = __ldcg(a.kv_indices);
+        if (sink_owner) sel_row[0] = __ldcg(kv_idx);
         if (c == C - 1) sel_row[T - 1] = last_pid;
       }
     } else {
@@ -1221,7 +1293,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
             int cc = 0;
             while (cc < C - 1 && sl >= peer_off[cc + 1]) ++cc;
             const int pos = cluster.map_shared_rank(sel, cc)[sl - peer_off[cc]];
-            if (pos >= 0 && pos < N) pid = __ldcg(a.kv_indices + pos);
+            if (pos >= 0 && pos < N) pid = __ldcg(kv_idx + pos);
           }
           items[sl - s_lo] = pid;
           if (sel_row) sel_row[sl] = pid;
@@ -1230,7 +1302,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     }
   } else if (shard == kShardNone) {
     for (int sl = s_lo + tid; sl < min(s_hi, T - 1); sl += kCsThreads) {  // every page
-      const int pid = __ldcg(a.kv_indices + sl);
+      const int pid = __ldcg(kv_idx + sl);
       items[sl - s_lo] = pid;
       if (sel_row) sel_row[sl] = pid;
     }
@@ -1290,15 +1362,9 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   for (int kk = 0; kk < NK; ++kk) {
     qb[kk][0] = qb[kk][1] = 0u;
     if (lane < 4) {
-      if (a.rope) {
-        const uint32_t* qw = reinterpret_cast<const uint32_t*>(q_rot);
-        qb[kk][0] = qw[kk * 8 + lane];
-        qb[kk][1] = qw[kk * 8 + 4 + lane];
-      } else {
-        const uint32_t* qw = reinterpret_cast<const uint32_t*>(a.q + static_cast<size_t>(h) * D);
-        qb[kk][0] = __ldcg(qw + kk * 8 + lane);
-        qb[kk][1] = __ldcg(qw + kk * 8 + 4 + lane);
-      }
+      const uint32_t* qw = reinterpret_cast<const uint32_t*>(q_rot);
+      qb[kk][0] = qw[kk * 8 + lane];
+      qb[kk][1] = qw[kk * 8 + 4 + lane];
     }
   }
   float m = -INFINITY, l = 0.f, acc[NK][4];
@@ -1325,25 +1391,24 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       if (lane == 0) load_page(pid);
       __syncwarp();
     }
-    const int ntok = is_last ? a.last_len : P;
+    const int ntok = is_last ? last_len : P;
     // the new token (a1, decode_page.cuh:392-506) and the last page's
     // running key max/min, read while the tiles are in flight
     Vec kn, vn, mxo, mno;
-    const int entry = a.last_len - 1, mentry = (N - 1) % P;
+    const int entry = last_len - 1, mentry = (N - 1) % P;
     const bool meta_ok = app_mpid >= 0 && app_mpid < a.meta_cap;
     __half* mk = a.meta + ((static_cast<size_t>(app_mpid) * 2 + 0) * P + mentry) * HD + col;
     __half* mv = a.meta + ((static_cast<size_t>(app_mpid) * 2 + 1) * P + mentry) * HD + col;
     if (is_last) {
-      kn = *reinterpret_cast<const Vec*>(a.k_new + col);
+      kn = *reinterpret_cast<const Vec*>(kn_in + col);
       if (a.rope) {  // rotate the new key; the rotated key also goes back in place
         float kf[CPL];
-        load_row<CPL>(reinterpret_cast<const __half*>(&kn), kf);
+        vec_to_float<CPL>(kn, kf);
         cs_rope_lane<CPL>(kf, lane, D, rope_pos, a.rope_rcp_scale, a.rope_log2_rcp_theta);
-#pragma unroll
-        for (int t = 0; t < CPL; ++t) reinterpret_cast<__half*>(&kn)[t] = __float2half_rn(kf[t]);
-        *reinterpret_cast<Vec*>(const_cast<__half*>(a.k_new) + col) = kn;
+        kn = float_to_vec<CPL>(kf);
+        *reinterpret_cast<Vec*>(const_cast<__half*>(kn_in) + col) = kn;
       }
-      vn = *reinterpret_cast<const Vec*>(a.v_new + col);
+      vn = *reinterpret_cast<const Vec*>(vn_in + col);
       if (entry > 0 && meta_ok) {
         mxo = *reinterpret_cast<const Vec*>(mk);
         mno = *reinterpret_cast<const Vec*>(mv);
@@ -1359,9 +1424,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       *reinterpret_cast<Vec*>(Vt + sw_lane_off<D>(entry)) = vn;
     }
     for (int r = ntok; r < 16; ++r) {  // rows past the page's tokens: finite zeros
-      Vec z;
-      memset(&z, 0, sizeof(z));
-      *reinterpret_cast<Vec*>(Vt + sw_lane_off<D>(r)) = z;
+      *reinterpret_cast<Vec*>(Vt + sw_lane_off<D>(r)) = Vec{};
     }
     __syncwarp();
     cs_attend_page_tc<D>(kb, vb, ntok, qb, a.scale_log2, m, l, acc);
@@ -1372,24 +1435,12 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       *reinterpret_cast<Vec*>(a.kv + ((static_cast<size_t>(pid) * 2 + 1) * P + entry) * HD +
                               col) = vn;
       if (meta_ok) {
-        if (entry == 0) {
-          const __half2 lo2 = __float2half2_rn(-65504.f), hi2 = __float2half2_rn(65504.f);
-#pragma unroll
-          for (int i = 0; i < CPL / 2; ++i) {
-            reinterpret_cast<__half2*>(&mxo)[i] = lo2;
-            reinterpret_cast<__half2*>(&mno)[i] = hi2;
-          }
+        if (entry == 0) {  // a new page: max from -65504, min from +65504
+          mxo = vec_fill<CPL>(0xfbfffbffu);
+          mno = vec_fill<CPL>(0x7bff7bffu);
         }
-#pragma unroll
-        for (int i = 0; i < CPL / 2; ++i) {
-          const __half2 k2 = reinterpret_cast<const __half2*>(&kn)[i];
-          reinterpret_cast<__half2*>(&mxo)[i] =
-              __hmax2(reinterpret_cast<const __half2*>(&mxo)[i], k2);
-          reinterpret_cast<__half2*>(&mno)[i] =
-              __hmin2(reinterpret_cast<const __half2*>(&mno)[i], k2);
-        }
-        *reinterpret_cast<Vec*>(mk) = mxo;
-        *reinterpret_cast<Vec*>(mv) = mno;
+        *reinterpret_cast<Vec*>(mk) = vec_hmax<CPL>(mxo, kn);
+        *reinterpret_cast<Vec*>(mv) = vec_hmin<CPL>(mno, kn);
       } else if (lane == 0) {
         raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
       }
@@ -1495,7 +1546,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
           }
         }
       } else {
-        a.o[static_cast<size_t>(h) * D + tid] = __float2half_rn(LL > 0.f ? OO / LL : 0.f);
+        o_out[static_cast<size_t>(h) * D + tid] = __float2half_rn(LL > 0.f ? OO / LL : 0.f);
       }
     }
     if (shard == kShardFinish && a.p2p) {  // the head's state delivered: raise fs everywhere
@@ -1509,7 +1560,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   }
   cluster_wait_acquire();  // every peer is past its last read of this CTA's memory
   // the rotated q in place, once every CTA of the cluster has read the input
-  if (a.rope && c == 0 && tid < D) const_cast<__half*>(a.q)[static_cast<size_t>(h) * D + tid] = q_rot[tid];
+  if (a.rope && c == 0 && tid < D) const_cast<__half*>(q_in)[static_cast<size_t>(h) * D + tid] = q_rot[tid];
 }
 
 using KernelFn = void (*)(CUtensorMap, CUtensorMap, ClusterStepArgs, CsShape);
