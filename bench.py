@@ -662,16 +662,27 @@ def longctx_key(a, world, rank, dev, peak):
                 plans[i].run(q, k, v, o[i], lay.kv_idx, n_total, last_len, lay.meta_idx,
                              None, ws, ws.numel(), torch.cuda.current_stream().cuda_stream)
         launches = plans[0].info(n_total)[0] * L
-    else:
-        dec = sharded.ShardedDecoder(torch.distributed.group.WORLD, H, D, P, kpages, a.method)
-
-        def one_step():
-            for i, (lay, (q, k, v)) in enumerate(zip(layers, news)):
-                o[i].copy_(dec.step(lay, q, k, v)[0])
-        launches = 3 * L
-    graph = capture(one_step, dev)
     steps = max(10, a.steps // 2)
-    ms = time_replays(graph.replay, steps, a.warmup, world, dev)
+    nccl_us = None
+    if world == 1:
+        graph = capture(one_step, dev)
+        ms = time_replays(graph.replay, steps, a.warmup, world, dev)
+    else:
+        # both exchanges, the same data: NCCL all_gathers, then the kernels'
+        # own peer stores (the value)
+        for exchange in ("nccl", "p2p"):
+            dec = sharded.ShardedDecoder(torch.distributed.group.WORLD, H, D, P, kpages,
+                                         a.method, exchange=exchange, device=dev)
+
+            def one_step():
+                for i, (lay, (q, k, v)) in enumerate(zip(layers, news)):
+                    o[i].copy_(dec.step(lay, q, k, v)[0])
+            graph = capture(one_step, dev)
+            ms = time_replays(graph.replay, steps, a.warmup, world, dev)
+            if exchange == "nccl":
+                nccl_us = ms * 1e3 / (steps * L)
+                del graph
+        launches = 3 * L
     _lib.check_device()
     us = ms * 1e3 / (steps * L)
 
@@ -714,6 +725,9 @@ def longctx_key(a, world, rank, dev, peak):
     per_gpu, pages_dec = [r[0] for r in got], [r[1] for r in got]
     del graph
     torch.cuda.synchronize()
+    if world > 1 and dec.mailbox is not None:  # every rank past its last pass first
+        barrier(world)
+        dec.mailbox.close()
     if rank != 0:
         return None
     total = sum(per_gpu)
@@ -725,6 +739,7 @@ def longctx_key(a, world, rank, dev, peak):
         "max_gpu_bytes": max(per_gpu), "per_gpu_bytes": per_gpu,
         "decode_head_pages_per_gpu": pages_dec,
         "max_abs_err": err, "selection_equal": sel_equal,
+        "nccl_exchange_us": None if nccl_us is None else round(nccl_us, 3),
         "checked_against": ("the sharded decoder run as one rank (propose and finish passes, "
                             "packed merge) on the same data, layer 0" if world == 1 else
                             "the one-GPU step over the whole sequence on rank 0, layer 0"),
@@ -732,9 +747,11 @@ def longctx_key(a, world, rank, dev, peak):
                                f"{L}-layer step, q,K,V~N(0,1) seed 4",
                    "pages": n_total, "pages_per_gpu": n_local,
                    "parallelism": "1 GPU, one step launch per layer" if world == 1 else
-                   f"page range x{world}; per layer: propose launch, all_gather of candidates "
-                   f"({world}x{H}x{kpages - 1}x8 B), finish launch, all_gather of partial "
-                   f"states ({world}x{H}x{D + 1}x4 B), merge launch; NCCL, one CUDA graph"},
+                   f"page range x{world}; per layer: propose launch (stores its "
+                   f"{H}x{kpages - 1}x8 B of candidates into every GPU's mailbox over NVLink), "
+                   f"finish launch (waits for every GPU's flag; stores its {H}x{D + 1}x4 B "
+                   f"partial state the same way), merge launch; no collective; one CUDA "
+                   f"graph. nccl_exchange_us: the same with two NCCL all_gathers instead"},
     }
     if launches is not None:
         out["gpu_launches"] = launches * steps
