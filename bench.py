@@ -34,7 +34,9 @@ Extra keys of the same line (each its own workload; see their "config"):
                     for 131071 tokens in one pass (N = 1 only)
   config2           config 2 at 8192 tokens: each kernel alone and the step
                     as one launch and as the chain (N = 1 only)
---mode model times config 3 (Llama-2-7B-shaped decode, budget sweep).
+  config3           config 3: a 32-layer Llama-2-7B-shaped decode token,
+                    contexts 16K/32K x budgets 512-4096, attention share
+                    (N = 1 only; --mode model prints it as its own line)
 --impl reference times the reference's CPU simulation path (the numpy port
 in oracle/sim.py of filter_util.py + quest_attention.py) on the host cores.
 """
@@ -76,7 +78,7 @@ def parse():
                          "longctx / batched: that key alone; model: config 3; kernels: each "
                          "kernel of one headline layer alone, L2 flushed before every launch "
                          "(the workload of the per-kernel ncu summaries)")
-    ap.add_argument("--extras", default="longctx,batched,prefill_metadata,config2",
+    ap.add_argument("--extras", default="longctx,batched,prefill_metadata,config2,config3",
                     help="comma list of extra keys for the headline line ('' = none)")
     ap.add_argument("--layers", type=int, default=32, help="headline layers per step")
     ap.add_argument("--ctx", type=int, default=32768, help="headline context tokens")
@@ -559,10 +561,11 @@ def run_headline(a):
     extras = [x for x in a.extras.split(",") if x]
     for key in extras:
         fn = {"longctx": longctx_key, "batched": batched_key,
-              "prefill_metadata": prefill_key, "config2": config2_key}.get(key)
+              "prefill_metadata": prefill_key, "config2": config2_key,
+              "config3": lambda *x: model_key(*x, steps=5, warmup=2)}.get(key)
         if fn is None:
             raise SystemExit(f"unknown extra key {key!r}")
-        if key in ("prefill_metadata", "config2") and world > 1:
+        if key in ("prefill_metadata", "config2", "config3") and world > 1:
             continue  # single-GPU workloads: reported at N = 1
         val = fn(a, world, rank, dev, peak)
         if line is not None:
@@ -1033,22 +1036,22 @@ def run_single(a, key):
 MODEL_METRIC = "ms/token, 32-layer Llama-2-7B-shaped decode, sparse attention (layers 2-31)"
 
 
-def run_model(a):
+def model_key(a, world, rank, dev, peak, steps=None, warmup=None):
     """Config 3: one decode token through a 32-layer Llama-2-7B-shaped model
     with random fp16 weights (hidden 4096, 32 heads, head_dim 128, MLP 11008,
-    vocab 32000): RMSNorm, q/k/v GEMVs, RoPE (aoakv_apply_rope_in_place),
-    attention through InferenceController.decode_step (layers 0-1 dense, as
-    in the reference's skip layers, llama.py:428-439; the rest with the token
-    budget), o_proj, SwiGLU MLP, final norm, LM head and a device-side argmax,
-    captured in one CUDA graph; contexts 16384 and 32768 x budgets
-    512/1024/2048/4096 (KV ~ N(0,1), seed 2). The GEMVs are torch (cuBLAS);
-    the attention share is timed by replaying a graph of only the attention
-    calls."""
+    vocab 32000): RMSNorm, q/k/v GEMVs, attention through
+    InferenceController.decode_step with RoPE fused into the step (layers 0-1
+    dense, as in the reference's skip layers, llama.py:428-439; the rest with
+    the token budget), o_proj, SwiGLU MLP, final norm, LM head and a
+    device-side argmax, captured in one CUDA graph; contexts 16384 and 32768
+    x budgets 512/1024/2048/4096 (KV ~ N(0,1), seed 2). The GEMVs are torch
+    (cuBLAS); the attention share is timed by replaying a graph of only the
+    attention calls."""
     import torch
 
     import aoa_kv_b200 as ak
-    dev = init_gpu(1, int(os.environ.get("LOCAL_RANK", "0")))
-    ak._lib.load()
+    steps = steps or a.steps
+    warmup = warmup if warmup is not None else a.warmup
     L, HID, FF, VOCAB = 32, 4096, 11008, 32000
     gen = torch.Generator(device=dev).manual_seed(2)
 
@@ -1063,7 +1066,6 @@ def run_model(a):
     norm_f = torch.ones(HID, device=dev, dtype=torch.float16)
     weight_bytes = sum(t.numel() * 2 for lw in layers for t in lw.values()) + \
         (emb.numel() + lm_head.numel() + norm_f.numel()) * 2
-    peak, _ = load_peak()
 
     def rmsnorm(x, g):
         xf = x.float()
@@ -1083,6 +1085,7 @@ def run_model(a):
         ctl.end_forward()
         ctl.prepare_metadata(1)
         ctl.begin_forward(1)
+        ctl.fuse_rope(1.0, 1e4)
         dense_budget = ctl.kv_cache.pool.capacity  # layers 0-1: every page
         token = torch.zeros(1, dtype=torch.long, device=dev)
         q_buf = torch.empty(L, 1, H, D, dtype=torch.float16, device=dev)
@@ -1105,8 +1108,7 @@ def run_model(a):
                     q_buf[layer].copy_((h @ lw["wq"]).view(1, H, D))
                     k_buf[layer].copy_((h @ lw["wk"]).view(1, H, D))
                     v_buf[layer].copy_((h @ lw["wv"]).view(1, H, D))
-                    ak.apply_rope_in_place(q_buf[layer], k_buf[layer], S - 1)
-                    attention(layer)
+                    attention(layer)  # RoPE at position S - 1 inside the step
                     x = x + o_buf[layer].view(1, HID) @ lw["wo"]
                     h = rmsnorm(x, lw["ln2"])
                     x = x + (torch.nn.functional.silu(h @ lw["wg"]) * (h @ lw["wu"])) @ lw["wd"]
@@ -1117,8 +1119,8 @@ def run_model(a):
                 for layer in range(L):
                     attention(layer)
             g_tok, g_att = capture(token_step, dev), capture(attention_only, dev)
-            ms_tok = time_replays(g_tok.replay, a.steps, a.warmup, 1, dev) / a.steps
-            ms_att = time_replays(g_att.replay, a.steps, a.warmup, 1, dev) / a.steps
+            ms_tok = time_replays(g_tok.replay, steps, warmup, 1, dev) / steps
+            ms_att = time_replays(g_att.replay, steps, warmup, 1, dev) / steps
             ak.check_device()
             att_bytes = 2 * step_bytes(S, S) + (L - 2) * step_bytes(S, budget)
             results.append({"context": S, "budget": budget, "ms_per_token": round(ms_tok, 4),
@@ -1129,18 +1131,30 @@ def run_model(a):
         ctl.clean_states()
         del ctl
         torch.cuda.empty_cache()
+    del layers, emb, lm_head
+    torch.cuda.empty_cache()
     head = next(r for r in results if r["context"] == 32768 and r["budget"] == 1024)
-    print(json.dumps({
-        "metric": MODEL_METRIC, "value": head["ms_per_token"], "unit": "ms", "n_gpus": 1,
-        "steps": a.steps, "warmup": a.warmup, "ms_per_step": head["ms_per_token"],
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-        "data": "synthetic",
+    return {
+        "metric": MODEL_METRIC, "value": head["ms_per_token"], "unit": "ms",
+        "steps": steps, "warmup": warmup,
         "config": {"workload": "Llama-2-7B-shaped decode, random weights, KV~N(0,1) seed 2, "
-                               "layers 0-1 dense; value at ctx 32768, budget 1024",
+                               "layers 0-1 dense, RoPE fused into the attention step; value "
+                               "at ctx 32768, budget 1024",
                    "weight_bytes": weight_bytes},
         "sweep": results,
         "weights_ideal_ms": round(weight_bytes / (peak * 1e9) * 1e3, 4),
-    }), flush=True)
+    }
+
+
+def run_model(a):
+    dev = init_gpu(1, int(os.environ.get("LOCAL_RANK", "0")))
+    from aoa_kv_b200 import _lib
+    _lib.load()
+    peak, _ = load_peak()
+    line = model_key(a, 1, 0, dev, peak)
+    line.update({"n_gpus": 1, "ms_per_step": line["value"], "higher_is_better": False,
+                 "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic"})
+    print(json.dumps(line), flush=True)
 
 
 # ----------------------------------------------- each kernel, one layer
