@@ -167,24 +167,45 @@ __device__ __forceinline__ void rope_pair(float x0, float x1, int j, int D, floa
   *o1 = __float2half_rn(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s)));
 }
 
-// Flags in another GPU's memory (peer pointers over NVLink): a release add
-// and a bounded acquire wait, both at system scope. The wait returns false
-// and records AOAKV_DEV_ERR_TIMEOUT after about a second.
-__device__ __forceinline__ void flag_add_release_sys(uint32_t* f, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+// Words exchanged with other GPUs through their memory (peer pointers over
+// NVLink) carry their own epoch: a 64-bit {value, epoch} store is single-copy
+// atomic, so a reader that sees the expected epoch also sees the value, and
+// no fence or flag is needed. Relaxed at system scope; the wait gives up
+// (AOAKV_DEV_ERR_TIMEOUT, returns the stale word) after about 0.1 s.
+__device__ __forceinline__ void tagged_store_sys(uint64_t* p, uint32_t value, uint32_t epoch) {
+  const uint64_t w = static_cast<uint64_t>(value) | (static_cast<uint64_t>(epoch) << 32);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-__device__ __forceinline__ uint32_t flag_load_acquire_sys(const uint32_t* f) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-  return v;
+// A pair of tagged words in one 16-byte access (each 8-byte half is still
+// single-copy atomic on its own; volatile global accesses are relaxed at
+// system scope). p is 16-byte aligned.
+__device__ __forceinline__ void tagged_store2_sys(uint64_t* p, uint32_t v0, uint32_t v1,
+                                                  uint32_t epoch) {
+  const uint64_t e = static_cast<uint64_t>(epoch) << 32;
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(e | v0), "l"(e | v1)
+               : "memory");
 }
-__device__ __forceinline__ bool flag_wait_sys(const uint32_t* f, uint32_t target, int* err) {
-  for (uint32_t i = 0; i < (1u << 24); ++i) {
-    if (static_cast<int32_t>(flag_load_acquire_sys(f) - target) >= 0) return true;
-    if (i > 64) __nanosleep(64);
+__device__ __forceinline__ uint2 tagged_wait2_sys(const uint64_t* p, uint32_t epoch, int* err) {
+  uint64_t w0 = 0, w1 = 0;
+  for (uint32_t i = 0; i < (1u << 20); ++i) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p)
+                 : "memory");
+    if (static_cast<uint32_t>(w0 >> 32) == epoch && static_cast<uint32_t>(w1 >> 32) == epoch)
+      return make_uint2(static_cast<uint32_t>(w0), static_cast<uint32_t>(w1));
+    if (i > 32) __nanosleep(100);
   }
   raise_dev_error(err, AOAKV_DEV_ERR_TIMEOUT);
-  return false;
+  return make_uint2(static_cast<uint32_t>(w0), static_cast<uint32_t>(w1));
+}
+__device__ __forceinline__ uint32_t tagged_wait_sys(const uint64_t* p, uint32_t epoch, int* err) {
+  uint64_t w = 0;
+  for (uint32_t i = 0; i < (1u << 20); ++i) {
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    if (static_cast<uint32_t>(w >> 32) == epoch) return static_cast<uint32_t>(w);
+    if (i > 32) __nanosleep(100);
+  }
+  raise_dev_error(err, AOAKV_DEV_ERR_TIMEOUT);
+  return static_cast<uint32_t>(w);
 }
 
 // 3-D tiled TMA load global -> shared, completion counted on `bar`.

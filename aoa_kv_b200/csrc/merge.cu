@@ -64,35 +64,33 @@ __global__ void merge_packed_kernel(const float* states, int G, int H, int D, __
 }
 
 // The merge of a sharded step whose states arrive in this GPU's mailbox
-// (peer stores): waits until every GPU delivered this step's state of every
-// head (fs), merges head blockIdx.x, and the last head to finish closes the
-// step's exchanges (ep).
+// (tagged words stored by every GPU's finish pass): head blockIdx.x waits for
+// this exchange's epoch on every word it reads, merges, and the last head to
+// finish closes the exchange (ep).
 __global__ void merge_mailbox_kernel(ShardMail m, int world, int rank, int H, int D,
                                      int proposals, __half* o, int* err) {
   const int h = blockIdx.x;
   uint32_t* ep = reinterpret_cast<uint32_t*>(m.base[rank] + m.ep_off);
-  if (threadIdx.x == 0) {
-    const uint32_t target = (__ldcg(ep + 1) + 1u) * static_cast<uint32_t>(H);
-    const uint32_t* fs = reinterpret_cast<const uint32_t*>(m.base[rank] + m.fs_off);
-    for (int g = 0; g < world; ++g) flag_wait_sys(fs + g, target, err);
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-  }
-  __syncthreads();
-  const float* states = reinterpret_cast<const float*>(m.base[rank] + m.state_off);
+  const uint32_t epoch = __ldcg(ep + 1) + 1u;
+  const uint64_t* box = reinterpret_cast<const uint64_t*>(m.base[rank] + m.state_off);
   const size_t row = static_cast<size_t>(D) + 1;
+  __shared__ float lse_s[8];
+  if (threadIdx.x < world)
+    lse_s[threadIdx.x] = __uint_as_float(
+        tagged_wait_sys(box + (static_cast<size_t>(threadIdx.x) * H + h) * row + D, epoch, err));
+  __syncthreads();
   float mx = -INFINITY;
-  for (int g = 0; g < world; ++g)
-    mx = fmaxf(mx, __ldcg(states + (static_cast<size_t>(g) * H + h) * row + D));
+  for (int g = 0; g < world; ++g) mx = fmaxf(mx, lse_s[g]);
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float acc = 0.f, sum = 0.f;
     if (mx != -INFINITY) {
       for (int g = 0; g < world; ++g) {
-        const float* st = states + (static_cast<size_t>(g) * H + h) * row;
-        const float l = __ldcg(st + D);
+        const float l = lse_s[g];
         if (l == -INFINITY) continue;
         const float w = expf(l - mx);
         sum += w;
-        acc += w * __ldcg(st + d);
+        acc += w * __uint_as_float(
+                       tagged_wait_sys(box + (static_cast<size_t>(g) * H + h) * row + d, epoch, err));
       }
     }
     o[static_cast<size_t>(h) * D + d] = __float2half_rn(sum > 0.f ? acc / sum : 0.f);

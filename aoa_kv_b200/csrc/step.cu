@@ -471,8 +471,7 @@ int shard_propose(const aoakv_step_plan_s* plan, const aoakv_shard_mailbox_s* mb
     a.mail = mb->mail;
     a.world = mb->world;
     a.rank = mb->rank;
-    a.cand_out = reinterpret_cast<uint2*>(mb->local + mb->mail.cand_off) +
-                 static_cast<size_t>(mb->rank) * plan->H * (k - 1);
+    a.cand_out = reinterpret_cast<uint2*>(mb->local + mb->mail.stage_off);
   } else {
     AOAKV_CHECK_ARG(cand_out != nullptr, "shard_propose: cand_out is NULL");
     a.cand_out = static_cast<uint2*>(cand_out);
@@ -498,7 +497,7 @@ int shard_finish(const aoakv_step_plan_s* plan, const aoakv_shard_mailbox_s* mb,
                     "shard_finish: mailbox not connected, or made for other sizes");
     world = mb->world;
     rank = mb->rank;
-    cand_all = mb->local + mb->mail.cand_off;
+    cand_all = mb->local + mb->mail.cand_off;  // read as tagged words by the kernel
     a.p2p = 1;
     a.mail = mb->mail;
   } else {
@@ -592,14 +591,12 @@ extern "C" int aoakv_shard_mailbox_create(aoakv_shard_mailbox* mb_out, int32_t w
   mb->max_prop = max_proposals;
   ShardMail& m = mb->mail;
   size_t off = 0;
-  m.cand_off = 0;
-  off = mb_up(static_cast<size_t>(world) * num_heads * max_proposals * 8);
-  m.state_off = static_cast<uint32_t>(off);
-  off += mb_up(static_cast<size_t>(world) * num_heads * (head_dim + 1) * 4);
-  m.fc_off = static_cast<uint32_t>(off);
-  off += 256;
-  m.fs_off = static_cast<uint32_t>(off);
-  off += 256;
+  m.cand_off = 0;  // two tagged 64-bit words per proposal
+  off = mb_up(static_cast<size_t>(world) * num_heads * max_proposals * 16);
+  m.state_off = static_cast<uint32_t>(off);  // one tagged 64-bit word per value
+  off += mb_up(static_cast<size_t>(world) * num_heads * (head_dim + 1) * 8);
+  m.stage_off = static_cast<uint32_t>(off);  // this GPU's own {key, page} list
+  off += mb_up(static_cast<size_t>(num_heads) * max_proposals * 8);
   m.ep_off = static_cast<uint32_t>(off);
   off += 256;
   mb->bytes = off;

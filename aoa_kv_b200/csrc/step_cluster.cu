@@ -844,23 +844,24 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     const int n_mine = N - (a.owns_last ? 1 : 0);  // local pages besides the last
     int w = 0;
     if (np > 0) {
-      if (a.p2p) {  // every GPU's proposals of this step are in this GPU's mailbox
-        if (tid == 0) {
-          const uint32_t* ep =
-              reinterpret_cast<const uint32_t*>(a.mail.base[me] + a.mail.ep_off);
-          const uint32_t target = (__ldcg(ep) + 1u) * static_cast<uint32_t>(H);
-          const uint32_t* fc =
-              reinterpret_cast<const uint32_t*>(a.mail.base[me] + a.mail.fc_off);
-          for (int g = 0; g < G; ++g) flag_wait_sys(fc + g, target, a.err);
-          asm volatile("fence.acq_rel.sys;" ::: "memory");
+      if (a.p2p) {  // every GPU's list, from this GPU's mailbox, once tagged with this epoch
+        const uint32_t epoch =
+            __ldcg(reinterpret_cast<const uint32_t*>(a.mail.base[me] + a.mail.ep_off)) + 1u;
+        const uint64_t* box = reinterpret_cast<const uint64_t*>(a.mail.base[me] + a.mail.cand_off);
+        for (int g = tid; g < G * np; g += kCsThreads) {
+          const int gg = g / np, i = g - gg * np;
+          const uint2 e =
+              tagged_wait2_sys(box + ((static_cast<size_t>(gg) * H + h) * np + i) * 2, epoch, a.err);
+          gkey[g] = e.x;
+          gpos[g] = e.y;
         }
-        __syncthreads();
-      }
-      for (int g = tid; g < G * np; g += kCsThreads) {
-        const int gg = g / np, i = g - gg * np;
-        const uint2 e = __ldcg(a.cand_in + (static_cast<size_t>(gg) * H + h) * np + i);
-        gkey[g] = e.x;
-        gpos[g] = e.y;
+      } else {
+        for (int g = tid; g < G * np; g += kCsThreads) {
+          const int gg = g / np, i = g - gg * np;
+          const uint2 e = __ldcg(a.cand_in + (static_cast<size_t>(gg) * H + h) * np + i);
+          gkey[g] = e.x;
+          gpos[g] = e.y;
+        }
       }
       __syncthreads();
       // global rank of entry i of list g: i plus, in every other list, the
@@ -1331,21 +1332,19 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     // every other GPU and raises fc there.
     cluster_arrive_release();
     cluster_wait_acquire();
-    if (a.p2p && c == 0) {
+    if (a.p2p && c == 0) {  // the head's list, tagged, into every GPU's mailbox
       const int np = a.n_prop;
+      const uint32_t epoch =
+          __ldcg(reinterpret_cast<const uint32_t*>(a.mail.base[a.rank] + a.mail.ep_off)) + 1u;
       const uint2* src = a.cand_out + static_cast<size_t>(h) * np;
-      for (int g = 0; g < a.world; ++g) {
-        if (g == a.rank) continue;
-        uint2* dst = reinterpret_cast<uint2*>(a.mail.base[g] + a.mail.cand_off) +
-                     (static_cast<size_t>(a.rank) * H + h) * np;
-        for (int i = tid; i < np; i += kCsThreads) dst[i] = __ldcg(src + i);
+      for (int i = tid; i < np; i += kCsThreads) {
+        const uint2 e = __ldcg(src + i);
+        for (int g = 0; g < a.world; ++g) {
+          uint64_t* w = reinterpret_cast<uint64_t*>(a.mail.base[g] + a.mail.cand_off) +
+                        ((static_cast<size_t>(a.rank) * H + h) * np + i) * 2;
+          tagged_store2_sys(w, e.x, e.y, epoch);
+        }
       }
-      __threadfence_system();
-      __syncthreads();
-      if (tid == 0)
-        for (int g = 0; g < a.world; ++g)
-          flag_add_release_sys(
-              reinterpret_cast<uint32_t*>(a.mail.base[g] + a.mail.fc_off) + a.rank, 1u);
     }
     return;
   }
@@ -1537,25 +1536,20 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         if (!a.p2p) {
           a.state_out[at + tid] = ov;
           if (tid == 0) a.state_out[at + D] = lse;
-        } else {  // into every GPU's mailbox, this GPU's row
+        } else {  // tagged, into every GPU's mailbox, this GPU's row
+          const uint32_t epoch =
+              __ldcg(reinterpret_cast<const uint32_t*>(a.mail.base[a.rank] + a.mail.ep_off) +
+                     1) + 1u;
           for (int g = 0; g < a.world; ++g) {
-            float* so = reinterpret_cast<float*>(a.mail.base[g] + a.mail.state_off) +
-                        static_cast<size_t>(a.rank) * H * (D + 1) + at;
-            so[tid] = ov;
-            if (tid == 0) so[D] = lse;
+            uint64_t* so = reinterpret_cast<uint64_t*>(a.mail.base[g] + a.mail.state_off) +
+                           static_cast<size_t>(a.rank) * H * (D + 1) + at;
+            tagged_store_sys(so + tid, __float_as_uint(ov), epoch);
+            if (tid == 0) tagged_store_sys(so + D, __float_as_uint(lse), epoch);
           }
         }
       } else {
         o_out[static_cast<size_t>(h) * D + tid] = __float2half_rn(LL > 0.f ? OO / LL : 0.f);
       }
-    }
-    if (shard == kShardFinish && a.p2p) {  // the head's state delivered: raise fs everywhere
-      __threadfence_system();
-      __syncthreads();
-      if (tid == 0)
-        for (int g = 0; g < a.world; ++g)
-          flag_add_release_sys(
-              reinterpret_cast<uint32_t*>(a.mail.base[g] + a.mail.fs_off) + a.rank, 1u);
     }
   }
   cluster_wait_acquire();  // every peer is past its last read of this CTA's memory

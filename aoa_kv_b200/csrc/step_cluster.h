@@ -15,15 +15,17 @@ constexpr int kShardMaxWorld = 8;
 // The exchange buffers of a page-range sharded sequence when the GPUs write
 // into each other's memory (aoakv_shard_mailbox_*): every rank's mailbox,
 // peers' mapped over NVLink, all with the same layout. Per mailbox:
-//   cand  [world, H, n_prop] {key, global page}: proposals, rank-major
-//   state [world, H, D + 1] fp32: partial states, rank-major
-//   fc[8], fs[8]: per sender, heads delivered (proposals / states), summed
-//                 over the steps
+//   cand  [world, H, n_prop, 2] 64-bit words {key | epoch}, {page | epoch}:
+//         proposals, sender-major
+//   state [world, H, D + 1] 64-bit words {fp32 bits | epoch}: partial states
+//   stage [H, n_prop] {key, page}: this GPU's own proposals before they are
+//         sent (local)
 //   ep[3]: proposal exchanges done, state exchanges done, heads merged in
-//          the current step (written by this GPU's merge only)
+//          the current exchange (written by this GPU's merge only); the n-th
+//          exchange of each kind tags its words with epoch n
 struct ShardMail {
   uint8_t* base[kShardMaxWorld];
-  uint32_t cand_off, state_off, fc_off, fs_off, ep_off;
+  uint32_t cand_off, state_off, stage_off, ep_off;
 };
 
 struct ClusterStepArgs {
@@ -78,9 +80,9 @@ struct ClusterStepArgs {
   int owns_last, dense;
   float* state_out;
   // p2p != 0: the exchanges go through `mail` instead of the caller:
-  // propose forwards each head's list to every other GPU's mailbox and
-  // raises fc there; finish first waits for every GPU's fc, reads cand_in
-  // from its own mailbox and writes its state into every mailbox (fs).
+  // propose writes each head's list, tagged with the exchange's epoch, into
+  // every GPU's mailbox; finish reads the lists from its own mailbox (waiting
+  // for the epoch) and writes its tagged state into every mailbox.
   int p2p;
   ShardMail mail;
   // RoPE fused into the step (rope != 0): q and k_new arrive unrotated and

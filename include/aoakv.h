@@ -394,12 +394,14 @@ AOAKV_API int aoakv_merge_packed_states(const float* states, int32_t num_parts,
 /* The same three passes with the two exchanges done by the kernels
  * themselves (no collective library): each GPU owns a mailbox in its own
  * memory, mapped into every other GPU's address space (CUDA IPC, NVLink
- * peer access), and the propose pass stores each head's list straight into
- * every other GPU's mailbox and raises a per-rank flag there (a release add
- * at system scope); the finish pass waits for every GPU's flag (bounded:
- * AOAKV_DEV_ERR_TIMEOUT after about a second, never a hang), ranks, decodes
- * and stores its partial state into every mailbox the same way; the merge
- * waits for every GPU's states and writes o. Per layer and token:
+ * peer access). The propose pass stores each head's list straight into every
+ * GPU's mailbox; the finish pass reads every GPU's lists from its own
+ * mailbox, ranks, decodes and stores its partial state into every mailbox the
+ * same way; the merge reads the states and writes o. Every 64-bit word
+ * travels with the number of the exchange it belongs to (a single-copy-
+ * atomic store of {value, epoch}), and a reader waits on the words it needs
+ * until they carry the current number, so no fence or flag is needed; the
+ * wait is bounded (AOAKV_DEV_ERR_TIMEOUT, never a hang). Per layer and token:
  *   aoakv_shard_propose_p2p (only when a selection runs, as above),
  *   aoakv_shard_finish_p2p, aoakv_shard_merge_p2p(with_proposals = whether
  *   the propose pass ran).
