@@ -56,10 +56,8 @@ int launch_estimate_hs(const EstimateArgs& a, int D, cudaStream_t s, bool tma);
 
 int launch_estimate_hs(const EstimateArgs& a, int D, cudaStream_t s) {
   const bool aoa = a.mode == AOAKV_SCORE_AOAKV;
-  const char* impl = std::getenv("AOAKV_EST_IMPL");  // "regs": A/B comparisons
   const bool tma = a.H % 8 == 0 && reinterpret_cast<uintptr_t>(a.meta) % 16 == 0 &&
-                   (!aoa || reinterpret_cast<uintptr_t>(a.vlog) % 16 == 0) &&
-                   !(impl && std::strcmp(impl, "regs") == 0);
+                   (!aoa || reinterpret_cast<uintptr_t>(a.vlog) % 16 == 0);
   return launch_estimate_hs(a, D, s, tma);
 }
 
