@@ -45,6 +45,9 @@ struct DecodeArgs {
   int* err;
   float* o_f32;                // if set: fp32 output [H, D] instead of o
   float* lse;                  // if set: natural-log sum of exp of the scores [H]
+  int group;                   // > 1: query head h reads KV head h / group (GQA):
+                               // its page ids from row h / group, its K/V
+                               // tiles from that head; q, o per query head
 };
 
 __host__ __device__ constexpr int dec_merge_bytes(int D, int nw = kDecWarps) {
@@ -87,6 +90,7 @@ __device__ __forceinline__ void decode_issue(const DecodeArgs& a,
                                              int c, uint64_t* bars, int* tok,
                                              __half* tiles, int D,
                                              const int* win = nullptr, int win_lo = 0) {
+  if (a.group > 1) h /= a.group;  // the KV head this query head reads
   const int n_slots = a.n_sel + 1;
   const int s0 = c * a.chunk_pages;
   const int ns = min(n_slots, s0 + a.chunk_pages) - s0;

@@ -39,6 +39,8 @@ int make_meta_tmap(CUtensorMap* map, const void* meta, int H, int D, int P, int 
 int launch_decode(const DecodeArgs& a, const CUtensorMap& tmap, int D,
                   const DecodePlan& pl, cudaStream_t s, bool pdl);
 int launch_estimate(const EstimateArgs& a, int D, cudaStream_t s);
+// GQA: a.H = KV heads, a.q holds a.H * group query heads (gqa.cu).
+int launch_gqa_estimate(const EstimateArgs& a, int D, int group, cudaStream_t s);
 int launch_topk(const TopkArgs& a, int rows, cudaStream_t s, bool pdl);
 
 }  // namespace aoakv

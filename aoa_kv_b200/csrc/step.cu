@@ -309,6 +309,132 @@ int plan_kernels(const aoakv_step_plan_s* p, int N, bool want_selected) {
 
 using namespace aoakv;
 
+namespace aoakv {
+namespace {
+
+// The GQA step: append (KV heads), group scoring, top-k per KV head, decode
+// per query head from its KV head's pages; stream-ordered with programmatic
+// dependent launch like the chain.
+int run_gqa(const void* q, const void* k_new, const void* v_new, void* o, void* kv,
+            const int32_t* kv_indices, int N, int last_len, int kv_cap, void* meta,
+            const int32_t* meta_indices, int meta_cap, void* vlog, int Hq, int Hk, int D,
+            int P, int budget, int mode, int sink, int32_t* selected_out, void* workspace,
+            size_t workspace_bytes, cudaStream_t s) {
+  AOAKV_CHECK_ARG(q && k_new && v_new && o && kv && kv_indices && meta && meta_indices && vlog,
+                  "step_gqa: NULL pointer argument");
+  AOAKV_CHECK_ARG(Hk >= 1 && Hq >= Hk && Hq % Hk == 0 && Hq / Hk <= 16,
+                  "step_gqa: num_qo_heads must be a multiple (1 to 16) of num_kv_heads");
+  int rc = check_plan_args(Hk, D, P, kv_cap, meta_cap, budget, mode);
+  if (rc) return rc;
+  AOAKV_CHECK_ARG(N >= 1 && N <= kv_cap && last_len >= 1 && last_len <= P,
+                  "step_gqa: bad num_kv_pages or kv_last_page_len");
+  const int group = Hq / Hk;
+  int k_pages, k;
+  step_budget(N, budget, sink, &k_pages, &k);
+  const bool sparse = N > k && k > 1;
+  AOAKV_CHECK_ARG(!sparse || N - 1 <= kTopkMaxN, "step_gqa: more than 49153 pages");
+  const StepWs lay = step_ws_layout(Hq, D, N, k_pages);
+  AOAKV_CHECK_ARG(workspace != nullptr, "step_gqa: workspace is NULL");
+  if (workspace_bytes < lay.total)
+    return set_error(AOAKV_ERR_WORKSPACE,
+                     "step_gqa: workspace smaller than aoakv_step_workspace_size(num_qo_heads, "
+                     "...) = " + std::to_string(lay.total));
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  rc = aoakv_append_kv_cache_decode(k_new, v_new, kv, kv_indices, N, last_len, kv_cap, meta,
+                                    meta_indices, (N + P - 1) / P, (N - 1) % P + 1, meta_cap,
+                                    vlog, Hk, D, P, AOAKV_LAYOUT_NHD, s);
+  if (rc) return rc;
+  DecodeArgs da = {};
+  da.q = static_cast<const __half*>(q);
+  da.o = static_cast<__half*>(o);
+  da.last_len = last_len;
+  da.last_page_ptr = kv_indices + (N - 1);
+  da.H = Hq;
+  da.P = P;
+  da.kv_cap = kv_cap;
+  da.group = group;
+  da.scale_log2 = (1.f / std::sqrt(static_cast<float>(D))) * 1.4426950408889634f;
+  da.err = dev_error_ptr();
+  int32_t* sel_idx = reinterpret_cast<int32_t*>(ws + lay.idx_off);
+  if (sparse) {
+    EstimateArgs ea = {};
+    ea.q = static_cast<const __half*>(q);
+    ea.meta = static_cast<const __half*>(meta);
+    ea.meta_indices = meta_indices;
+    ea.kv_indices = kv_indices;
+    ea.vlog = static_cast<const __half*>(vlog);
+    ea.out = ws + lay.scores_off;
+    ea.out_stride = N;
+    ea.out_f32 = 1;
+    ea.n_score = N - 1;
+    ea.H = Hk;
+    ea.P = P;
+    ea.meta_cap = meta_cap;
+    ea.kv_cap = kv_cap;
+    ea.mode = mode;
+    ea.two_rsqrt_d = 2.f / std::sqrt(static_cast<float>(D));
+    ea.err = da.err;
+    rc = launch_gqa_estimate(ea, D, group, s);
+    if (rc) return rc;
+    TopkArgs ta;
+    ta.scores = ws + lay.scores_off;
+    ta.s_stride = N;
+    ta.in_idx = kv_indices;
+    ta.in_stride = 0;
+    ta.out_vals = nullptr;
+    ta.ov_stride = 0;
+    ta.out_idx = sel_idx;
+    ta.oi_stride = k - 1;
+    ta.f32 = 1;
+    ta.n = N - 1;
+    ta.k = k - 1;
+    ta.sink = sink;
+    rc = launch_topk(ta, Hk, s, true);
+    if (rc) return rc;
+    da.indices = sel_idx;
+    da.idx_stride = k - 1;
+    da.n_sel = k - 1;
+  } else {
+    da.indices = kv_indices;
+    da.idx_stride = 0;
+    da.n_sel = N > k ? 0 : N - 1;
+  }
+  CUtensorMap tmap;
+  rc = make_kv_tmap(&tmap, kv, Hk, D, P, kv_cap);
+  if (rc) return rc;
+  const DecodePlan pl = plan_decode(Hq, da.n_sel + 1, D, P);
+  da.chunk_pages = pl.chunk_pages;
+  da.n_chunks = pl.n_chunks;
+  carve_decode_ws(ws + lay.dec_off, Hq, D, da.n_sel + 1, da);
+  rc = launch_decode(da, tmap, D, pl, s, sparse);
+  if (rc) return rc;
+  if (selected_out) {
+    fill_selected_kernel<<<Hk, 128, 0, s>>>(selected_out, k_pages, da.indices, da.idx_stride,
+                                            da.n_sel, da.last_page_ptr, Hk);
+    AOAKV_CUDA_TRY(cudaGetLastError(), "fill_selected launch");
+  }
+  return AOAKV_OK;
+}
+
+}  // namespace
+}  // namespace aoakv
+
+extern "C" int aoakv_decode_step_gqa(
+    const void* q, const void* k_new, const void* v_new, void* o, void* kv_data,
+    const int32_t* kv_indices, int32_t num_kv_pages, int32_t kv_last_page_len,
+    int32_t kv_capacity_pages, void* metadata_data, const int32_t* metadata_indices,
+    int32_t metadata_capacity_pages, void* v_log_norm, int32_t num_qo_heads,
+    int32_t num_kv_heads, int32_t head_dim, int32_t page_size, int32_t page_budget,
+    int32_t score_mode, int32_t sink_first_page, int32_t* selected_out, void* workspace,
+    size_t workspace_bytes, void* stream) {
+  AOAKV_NVTX("aoakv_decode_step_gqa");
+  return run_gqa(q, k_new, v_new, o, kv_data, kv_indices, num_kv_pages, kv_last_page_len,
+                 kv_capacity_pages, metadata_data, metadata_indices, metadata_capacity_pages,
+                 v_log_norm, num_qo_heads, num_kv_heads, head_dim, page_size, page_budget,
+                 score_mode, sink_first_page != 0, selected_out, workspace, workspace_bytes,
+                 static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int aoakv_step_workspace_size(int32_t num_heads, int32_t head_dim,
                                          int32_t max_pages, int32_t max_page_budget,
                                          size_t* bytes) {

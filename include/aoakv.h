@@ -464,6 +464,29 @@ AOAKV_API int aoakv_decode_step_grid(
     int32_t sink_first_page, int32_t* selected_out, void* workspace,
     size_t workspace_bytes, int32_t max_ctas, void* stream);
 
+/* Grouped-query attention (GQA; the reference's CUDA tree is MHA only,
+ * docs/KERNEL_DIFF.md:66-76): the step of aoakv_decode_step for
+ * num_qo_heads query heads sharing num_kv_heads KV heads (num_qo_heads a
+ * multiple of num_kv_heads, at most 16 query heads per KV head; query head h
+ * reads KV head h / (num_qo_heads / num_kv_heads)). Group-consistent
+ * selection as in filtering/filter_util.py: each KV head scores its pages
+ * once for its whole group — QUEST sums the group's page bounds (:219-221),
+ * AOAKV takes the logsumexp over the group of 2*bound/sqrt(head_dim) and
+ * adds 2*v_log_norm (:352-361, :367) — and every query head of the group
+ * attends the same pages. q, o: [num_qo_heads, head_dim]; k_new, v_new,
+ * the caches and v_log_norm use num_kv_heads; selected_out (optional) is
+ * [num_kv_heads, B] as for aoakv_decode_step. Runs as four launches
+ * (append, group scoring, top-k, decode); the workspace is
+ * aoakv_step_workspace_size(num_qo_heads, ...). */
+AOAKV_API int aoakv_decode_step_gqa(
+    const void* q, const void* k_new, const void* v_new, void* o, void* kv_data,
+    const int32_t* kv_indices, int32_t num_kv_pages, int32_t kv_last_page_len,
+    int32_t kv_capacity_pages, void* metadata_data, const int32_t* metadata_indices,
+    int32_t metadata_capacity_pages, void* v_log_norm, int32_t num_qo_heads,
+    int32_t num_kv_heads, int32_t head_dim, int32_t page_size, int32_t page_budget,
+    int32_t score_mode, int32_t sink_first_page, int32_t* selected_out, void* workspace,
+    size_t workspace_bytes, void* stream);
+
 /* Batched decode step (config 4's single launch; no reference counterpart:
  * the reference hard-wires batch 1, decode_attn.cuh:504-509): the step of
  * aoakv_decode_step for num_requests requests whose pages live in ONE layer

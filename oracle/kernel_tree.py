@@ -214,3 +214,49 @@ def step(q: np.ndarray, k_new: np.ndarray, v_new: np.ndarray, c: LayerCache,
         sel = np.tile(kv_indices[: n_pages - 1], (c.H, 1))
     out = sparse_decode(q, c, sel, last, last_len)
     return out, np.concatenate([sel, np.full((c.H, 1), last)], axis=1)
+
+
+def estimate_gqa(q: np.ndarray, c: LayerCache, meta_indices: np.ndarray,
+                 kv_indices: np.ndarray, n_pages: int, mode: str) -> np.ndarray:
+    """Group-consistent page scores for q [Hq, D] over a cache of Hkv heads
+    (query head h reads KV head h // g, g = Hq / Hkv): the kernel tree's page
+    bound per query head, combined per KV head as the simulation does —
+    quest: the group's bounds summed (filter_util.py:219-221); aoakv:
+    logsumexp over the group of 2*s/sqrt(D) (:352-361), plus 2*vlog of the
+    KV head's page (:367). Returns float32 [Hkv, N-1]."""
+    g = q.shape[0] // c.H
+    s = np.stack([estimate(q[i::g], c, meta_indices, kv_indices, n_pages, "quest")
+                  for i in range(g)])  # [g, Hkv, n]
+    if mode == "quest":
+        return s.sum(axis=0, dtype=F32).astype(F32)
+    x = F32(2.0 / math.sqrt(c.D)) * s
+    m = x.max(axis=0)
+    lse = m + np.log(np.exp(x - m[None]).sum(axis=0, dtype=F32))
+    p = np.arange(n_pages - 1)
+    vl = c.vlog[kv_indices[p]].astype(F32).T  # [Hkv, n]
+    return (lse + F32(2) * vl).astype(F32)
+
+
+def step_gqa(q: np.ndarray, k_new: np.ndarray, v_new: np.ndarray, c: LayerCache,
+             kv_indices: np.ndarray, meta_indices: np.ndarray, n_pages: int, last_len: int,
+             page_budget: int, mode: str, sink: bool):
+    """step() for GQA: q [Hq, D], k_new / v_new and the cache with Hkv heads;
+    the selection per KV head from estimate_gqa, every query head of a group
+    attending its KV head's pages. Returns (out [Hq, D], attended page ids
+    [Hkv, k] with the last page last)."""
+    g = q.shape[0] // c.H
+    append_decode(c, kv_indices, meta_indices, n_pages, last_len, k_new, v_new)
+    kp = max(3, page_budget) if sink else page_budget
+    k = min(kp, n_pages)
+    last = int(kv_indices[n_pages - 1])
+    if n_pages > k and k > 1:
+        sc = estimate_gqa(q, c, meta_indices, kv_indices, n_pages, mode)
+        sel = kv_indices[topk_positions(sc, k - 1, sink)]
+    elif n_pages > k:
+        sel = np.zeros((c.H, 0), np.int64)
+    else:
+        sel = np.tile(kv_indices[: n_pages - 1], (c.H, 1))
+    out = np.zeros((q.shape[0], c.D), F32)
+    for i in range(g):
+        out[i::g] = sparse_decode(q[i::g], c, sel, last, last_len)
+    return out, np.concatenate([sel, np.full((c.H, 1), last)], axis=1)

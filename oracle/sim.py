@@ -3,10 +3,11 @@
 TEST INFRASTRUCTURE ONLY (see oracle/__init__.py): the checker for the CUDA
 path's ``sink_first_page=1`` mode and the timed CPU baseline.
 
-Shapes follow the reference with the batch dimension squeezed (b = 1) and
-one query head per KV head (MHA, num_key_value_groups = 1, so the GQA
-logsumexp at filter_util.py:352-361 is the identity):
-    q [H, D];  K, V [H, S, D];  page filters [H, N, 2, D] (max at 0, min at 1).
+Shapes follow the reference with the batch dimension squeezed (b = 1):
+    q [Hq, D];  K, V [Hkv, S, D];  page filters [Hkv, N, 2, D] (max at 0,
+    min at 1); groups = Hq / Hkv query heads per KV head (1 for MHA, where
+    the group sum / logsumexp of filter_util.py:219-221 and :352-361 is the
+    identity). Query head h reads KV head h // groups (repeat_kv).
 All arithmetic is float32, as the simulation runs on the CPU (fp16 inputs are
 upcast). Page ids are logical (0 .. N-1).
 
@@ -79,7 +80,7 @@ def update_mean_page_filters(means: np.ndarray, v_new: np.ndarray, past_len: int
 
 
 def attn_weights_for_selection(q: np.ndarray, filters: np.ndarray, page_size: int,
-                               seq_len: int, expand: bool = True) -> np.ndarray:
+                               seq_len: int, expand: bool = True, groups: int = 1) -> np.ndarray:
     """fu:968-1018. Quest upper bound per token, [H, S].
 
     sign = +1 where q > 0 else -1 (fu:990); bound = |q| . max(sign*kmax,
@@ -87,6 +88,8 @@ def attn_weights_for_selection(q: np.ndarray, filters: np.ndarray, page_size: in
     to its page_size tokens and runs one matmul (fu:1004-1016); expand=False
     computes the same numbers per page and repeats the result instead.
     """
+    if groups > 1:  # repeat_filter: every query head reads its KV head's filters
+        filters = np.repeat(filters, groups, axis=0)
     sign = np.where(q > 0, F32(1), F32(-1))
     pos_q = q * sign
     max_key = (filters * sign[:, None, None, :]).max(axis=2)  # [H, N, D]
@@ -118,10 +121,13 @@ def topk_pages(scores: np.ndarray, k: int) -> np.ndarray:
     return np.sort(order, axis=-1)
 
 
-def quest_scores(w: np.ndarray, page_size: int, fixed: bool) -> np.ndarray:
+def quest_scores(w: np.ndarray, page_size: int, fixed: bool, groups: int = 1) -> np.ndarray:
     """fu:165-228 (local_heavy_hitter_mask_group_consistent_sum): page score
-    = amax of the token bound; fixed forces pages 0 and N-1 (fu:226-228)."""
+    = amax of the token bound, summed over the query heads of a KV head's
+    group (fu:219-221); fixed forces pages 0 and N-1 (fu:226-228). [Hkv, N]."""
     cs = chunk_scores(w, page_size).astype(F32)
+    if groups > 1:
+        cs = cs.reshape(-1, groups, cs.shape[-1]).sum(axis=1, dtype=F32)
     if fixed:
         cs[:, 0] = FMAX
         cs[:, -1] = FMAX
@@ -129,14 +135,20 @@ def quest_scores(w: np.ndarray, page_size: int, fixed: bool) -> np.ndarray:
 
 
 def aoakv_scores(w: np.ndarray, page_size: int, v_page_mean: np.ndarray,
-                 fixed: bool) -> np.ndarray:
+                 fixed: bool, groups: int = 1) -> np.ndarray:
     """fu:269-377 (local_heavy_hitter_mask_value_aware_group_consistent_sum):
-    2 * amax / sqrt(d) (fu:329) + 2 * log(||mean V_page|| + 1e-8) (fu:325,
-    fu:367); fixed forces pages 0 and N-1 (fu:375-377)."""
+    2 * amax / sqrt(d) (fu:329), logsumexp over the query heads of a KV
+    head's group (fu:352-361), + 2 * log(||mean V_page|| + 1e-8) of the KV
+    head (fu:325, fu:367); fixed forces pages 0 and N-1 (fu:375-377). [Hkv, N]."""
     D = v_page_mean.shape[-1]
     log_v = np.log(np.linalg.norm(v_page_mean, axis=-1).astype(F32) + F32(LOG_EPS)).astype(F32)
     cs = chunk_scores(w, page_size).astype(F32)
-    cs = F32(2) * (cs / F32(math.sqrt(D))) + F32(2) * log_v
+    cs = F32(2) * (cs / F32(math.sqrt(D)))
+    if groups > 1:
+        g = cs.reshape(-1, groups, cs.shape[-1])
+        m = g.max(axis=1)
+        cs = (m + np.log(np.exp(g - m[:, None]).sum(axis=1, dtype=F32))).astype(F32)
+    cs = cs + F32(2) * log_v
     if fixed:
         cs[:, 0] = FMAX
         cs[:, -1] = FMAX
@@ -182,7 +194,10 @@ def decode_step(state: SimLayerState, q: np.ndarray, k_new: np.ndarray, v_new: n
                 expand: bool = True):
     """One decode token of a layer with layer_id >= 2 (qa:249-356 for aoakv,
     qa:90-167 for quest). Mutates `state` (appends the token) and returns
-    (out [H, D], selected page ids [H, k] ascending, page scores [H, N])."""
+    (out [Hq, D], selected page ids [Hkv, k] ascending, page scores
+    [Hkv, N]); Hq / Hkv query heads share a KV head (GQA) when q has more
+    heads than the state."""
+    groups = q.shape[0] // state.K.shape[0]
     P = state.page_size
     past = state.seq_len
     if method == "aoakv":
@@ -192,15 +207,19 @@ def decode_step(state: SimLayerState, q: np.ndarray, k_new: np.ndarray, v_new: n
     state.filters = update_page_filters(state.filters, k_new.astype(F32), past, P)
     S = past + 1
     state.seq_len = S
-    w = attn_weights_for_selection(q.astype(F32), state.filters, P, S, expand=expand)
+    w = attn_weights_for_selection(q.astype(F32), state.filters, P, S, expand=expand,
+                                   groups=groups)
     tb = min(S, token_budget)  # qa:137 / qa:326
     if method == "aoakv":
-        scores = aoakv_scores(w, P, state.v_mean, fixed)
+        scores = aoakv_scores(w, P, state.v_mean, fixed, groups)
     elif method == "quest":
-        scores = quest_scores(w, P, fixed)
+        scores = quest_scores(w, P, fixed, groups)
     else:
         raise ValueError(f"unknown method {method!r}")
     k = page_budget_k(tb, P, scores.shape[1])
     sel = topk_pages(scores, k)
-    out = masked_decode(q.astype(F32), state.K, state.V, token_mask(sel, S, P))
+    mask = np.repeat(token_mask(sel, S, P), groups, axis=0)  # repeat_kv of the mask
+    K, V = (state.K, state.V) if groups == 1 else (np.repeat(state.K, groups, axis=0),
+                                                   np.repeat(state.V, groups, axis=0))
+    out = masked_decode(q.astype(F32), K, V, mask)
     return out, sel, scores

@@ -35,3 +35,11 @@ def digest(*arrays: np.ndarray) -> str:
     for a in arrays:
         h.update(np.ascontiguousarray(a).tobytes())
     return h.hexdigest()
+
+
+def gen_gqa(seed: int, Hq: int, Hkv: int, S: int, D: int, dist: str = "normal"):
+    """GQA inputs: K, V [S, Hkv, D] as gen_qkv draws them for Hkv heads, and
+    q [Hq, D] from a second generator (seed + 7777)."""
+    _, K, V = gen_qkv(seed, Hkv, S, D, dist)
+    q = np.random.default_rng(seed + 7777).standard_normal((Hq, D), dtype=np.float32)
+    return q.astype(np.float16), K, V

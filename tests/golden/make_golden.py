@@ -37,7 +37,7 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
-from gen import digest, gen_qkv  # noqa: E402
+from gen import digest, gen_gqa, gen_qkv  # noqa: E402
 
 REF: Path  # the reference checkout's root, set by main()
 TESTS: Path  # its kernels/aoa_kv/quest/tests
@@ -56,6 +56,13 @@ SIM_CASES = [
     ("sim_aoakv_fixed_d64", 17, 8, 333, 64, 16, 96, "aoakv", True, "outlier"),
     ("sim_aoakv_fixed_h32", 18, 32, 1024, 128, 16, 256, "aoakv", True, "normal"),
     ("sim_quest_fixed_h32", 18, 32, 1024, 128, 16, 256, "quest", True, "normal"),
+]
+
+GQA_CASES = [
+    # name, seed, Hq, Hkv, S, D, P, token_budget, method, fixed, dist
+    ("sim_aoakv_fixed_gqa4", 19, 8, 2, 333, 128, 16, 96, "aoakv", True, "outlier"),
+    ("sim_quest_fixed_gqa4", 19, 8, 2, 333, 128, 16, 96, "quest", True, "outlier"),
+    ("sim_aoakv_fixed_gqa2_d64", 20, 8, 4, 500, 64, 16, 128, "aoakv", True, "normal"),
 ]
 
 KT_EST_CASES = [  # name, seed, kv_len (test_estimate.py:77 parameter list)
@@ -90,8 +97,11 @@ def load_ref_test(name: str):
 
 def ref_sim_decode(fu, q, K, V, P, budget, method, fixed):
     """Decode branch of quest_attention.py for one layer with layer_id >= 2,
-    after a prefill of the first S-1 tokens (:227-243), batch 1, MHA, fp32."""
+    after a prefill of the first S-1 tokens (:227-243), batch 1, fp32; q may
+    have more heads than K and V (GQA: query head h reads KV head h // g, the
+    repeat_kv of the attention)."""
     S, H, D = K.shape
+    groups = q.shape[0] // H
     past = S - 1
     Kt = torch.from_numpy(K.astype(np.float32)).permute(1, 0, 2)[None].contiguous()
     Vt = torch.from_numpy(V.astype(np.float32)).permute(1, 0, 2)[None].contiguous()
@@ -101,9 +111,10 @@ def ref_sim_decode(fu, q, K, V, P, budget, method, fixed):
     cur_k, cur_v = Kt[:, :, past:], Vt[:, :, past:]
     if method == "aoakv":                                              # qa:254-260
         vmean = fu.update_mean_page_filters(vmean.unsqueeze(-2), cur_v, past, P).squeeze(-2)
-    attn = torch.matmul(qt, Kt.transpose(2, 3)) / math.sqrt(D)         # qa:265-268
+    Kr = Kt.repeat_interleave(groups, dim=1) if groups > 1 else Kt     # repeat_kv
+    attn = torch.matmul(qt, Kr.transpose(2, 3)) / math.sqrt(D)         # qa:265-268
     filters = fu.update_page_filters(filters, cur_k, past, P)          # qa:291-293
-    w = fu.compute_attn_weights_for_selection(qt, filters, 1, P, S, math.ceil(S / P))  # qa:297-300
+    w = fu.compute_attn_weights_for_selection(qt, filters, groups, P, S, math.ceil(S / P))  # qa:297-300
     tb = min(S, budget)                                                # qa:326
     seen = {}
     orig_topk = torch.Tensor.topk
@@ -116,17 +127,18 @@ def ref_sim_decode(fu, q, K, V, P, budget, method, fixed):
     try:
         if method == "aoakv":                                          # qa:328-332
             mask = fu.local_heavy_hitter_mask_value_aware_group_consistent_sum(
-                w, tb, P, vmean, 1, D, fixed)
+                w, tb, P, vmean, groups, D, fixed)
         else:                                                          # qa:139-143
-            mask, _ = fu.local_heavy_hitter_mask_group_consistent_sum(w, tb, P, 1, fixed)
+            mask, _ = fu.local_heavy_hitter_mask_group_consistent_sum(w, tb, P, groups, fixed)
     finally:
         torch.Tensor.topk = orig_topk
     attn[~mask] = torch.tensor(torch.finfo(attn.dtype).min)            # qa:347
     p = torch.nn.functional.softmax(attn, dim=-1, dtype=torch.float32)  # qa:351
-    out = torch.matmul(p, Vt)[0, :, 0]                                 # qa:353-356
+    Vr = Vt.repeat_interleave(groups, dim=1) if groups > 1 else Vt
+    out = torch.matmul(p, Vr)[0, :, 0]                                 # qa:353-356
     N = math.ceil(S / P)
     pad = N * P - S
-    page_sel = torch.cat([mask[0, :, 0], torch.zeros(H, pad, dtype=torch.bool)], 1)
+    page_sel = torch.cat([mask[0, ::groups, 0], torch.zeros(H, pad, dtype=torch.bool)], 1)
     page_sel = page_sel.reshape(H, N, P).any(-1)
     sel = np.stack([np.nonzero(r)[0] for r in page_sel.numpy()]).astype(np.int32)
     scores = seen["scores"].reshape(H, N).numpy().astype(np.float32)
@@ -153,6 +165,14 @@ def main():
         out, sel, scores = ref_sim_decode(fu, q, K, V, P, budget, method, fixed)
         meta = dict(seed=seed, H=H, S=S, D=D, P=P, token_budget=budget, method=method,
                     fixed=fixed, dist=dist, digest=digest(q, K, V))
+        save(name, meta, out=out, sel=sel, scores=scores)
+        print(name, sel.shape, out.shape)
+
+    for name, seed, Hq, Hkv, S, D, P, budget, method, fixed, dist in GQA_CASES:
+        q, K, V = gen_gqa(seed, Hq, Hkv, S, D, dist)
+        out, sel, scores = ref_sim_decode(fu, q, K, V, P, budget, method, fixed)
+        meta = dict(seed=seed, Hq=Hq, Hkv=Hkv, H=Hkv, S=S, D=D, P=P, token_budget=budget,
+                    method=method, fixed=fixed, dist=dist, digest=digest(q, K, V))
         save(name, meta, out=out, sel=sel, scores=scores)
         print(name, sel.shape, out.shape)
 

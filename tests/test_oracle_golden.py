@@ -6,16 +6,24 @@ import math
 import numpy as np
 import pytest
 
-from gen import digest, gen_qkv
+from gen import digest, gen_gqa, gen_qkv
 from helpers import golden_names, load_golden, selection_mismatch
 from oracle import kernel_tree as kt
 from oracle import sim
 
 
+def _sim_inputs(meta):
+    if "Hq" in meta:  # GQA case: Hq query heads over Hkv KV heads
+        return gen_gqa(meta["seed"], meta["Hq"], meta["Hkv"], meta["S"], meta["D"], meta["dist"])
+    return gen_qkv(meta["seed"], meta["H"], meta["S"], meta["D"], meta["dist"])
+
+
 @pytest.mark.parametrize("name", golden_names("sim_"))
 def test_sim_oracle_matches_reference_simulation(name):
+    """MHA and GQA cases (the GQA ones pin the group sum / logsumexp of
+    filter_util.py:219-221 and :352-361 and the replicated mask)."""
     meta, g = load_golden(name)
-    q, K, V = gen_qkv(meta["seed"], meta["H"], meta["S"], meta["D"], meta["dist"])
+    q, K, V = _sim_inputs(meta)
     assert digest(q, K, V) == meta["digest"], "input regeneration diverged"
     Kh, Vh = K.astype(np.float32).transpose(1, 0, 2), V.astype(np.float32).transpose(1, 0, 2)
     st = sim.SimLayerState(Kh[:, :-1], Vh[:, :-1], meta["P"])
@@ -32,11 +40,14 @@ def test_sim_expand_equals_per_page(name):
     """The reference's token-expanded bound (fu:1004-1016) equals the
     per-page bound the kernels compute."""
     meta, _ = load_golden(name)
-    q, K, _ = gen_qkv(meta["seed"], meta["H"], meta["S"], meta["D"], meta["dist"])
+    q, K, _ = _sim_inputs(meta)
     Kh = K.astype(np.float32).transpose(1, 0, 2)
     f = sim.get_max_min_filters(Kh, meta["P"])
-    a = sim.attn_weights_for_selection(q.astype(np.float32), f, meta["P"], meta["S"], expand=True)
-    b = sim.attn_weights_for_selection(q.astype(np.float32), f, meta["P"], meta["S"], expand=False)
+    grp = q.shape[0] // Kh.shape[0]
+    a = sim.attn_weights_for_selection(q.astype(np.float32), f, meta["P"], meta["S"], expand=True,
+                                       groups=grp)
+    b = sim.attn_weights_for_selection(q.astype(np.float32), f, meta["P"], meta["S"],
+                                       expand=False, groups=grp)
     np.testing.assert_allclose(a, b, rtol=1e-5, atol=1e-4)
 
 
