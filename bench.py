@@ -37,6 +37,8 @@ Extra keys of the same line (each its own workload; see their "config"):
   config3           config 3: a 32-layer Llama-2-7B-shaped decode token,
                     contexts 16K/32K x budgets 512-4096, attention share
                     (N = 1 only; --mode model prints it as its own line)
+  gqa               the GQA step (32 query / 8 KV heads) at the headline's
+                    context and budget (N = 1 only)
 --impl reference times the reference's CPU simulation path (the numpy port
 in oracle/sim.py of filter_util.py + quest_attention.py) on the host cores.
 """
@@ -78,7 +80,7 @@ def parse():
                          "longctx / batched: that key alone; model: config 3; kernels: each "
                          "kernel of one headline layer alone, L2 flushed before every launch "
                          "(the workload of the per-kernel ncu summaries)")
-    ap.add_argument("--extras", default="longctx,batched,prefill_metadata,config2,config3",
+    ap.add_argument("--extras", default="longctx,batched,prefill_metadata,config2,config3,gqa",
                     help="comma list of extra keys for the headline line ('' = none)")
     ap.add_argument("--layers", type=int, default=32, help="headline layers per step")
     ap.add_argument("--ctx", type=int, default=32768, help="headline context tokens")
@@ -562,10 +564,10 @@ def run_headline(a):
     for key in extras:
         fn = {"longctx": longctx_key, "batched": batched_key,
               "prefill_metadata": prefill_key, "config2": config2_key,
-              "config3": lambda *x: model_key(*x, steps=5, warmup=2)}.get(key)
+              "config3": lambda *x: model_key(*x, steps=5, warmup=2), "gqa": gqa_key}.get(key)
         if fn is None:
             raise SystemExit(f"unknown extra key {key!r}")
-        if key in ("prefill_metadata", "config2", "config3") and world > 1:
+        if key in ("prefill_metadata", "config2", "config3", "gqa") and world > 1:
             continue  # single-GPU workloads: reported at N = 1
         val = fn(a, world, rank, dev, peak)
         if line is not None:
@@ -884,6 +886,69 @@ def batched_key(a, world, rank, dev, peak):
 
 
 # ------------------------------------------------- config 5 prefill build
+def gqa_key(a, world, rank, dev, peak):
+    """Grouped-query attention (a Llama-3-8B-like layer: 32 query heads over
+    8 KV heads, head_dim 128), 32K context, budget 1024, outlier K (seed 1):
+    aoakv_decode_step_gqa over 16 layers (16 x 12.6 MB > L2) in a CUDA graph,
+    µs per layer-step. Bytes: the KV heads' metadata and K/V, the query
+    heads' q and o."""
+    import numpy as np
+    import torch
+
+    from aoa_kv_b200 import _lib
+    Hq, Hk, ctx, budget, L = 32, 8, a.ctx, a.budget, 16
+    n = (ctx + P - 1) // P
+    kp = budget // P
+    stream = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator(device=dev).manual_seed(1)
+    layers = []
+    for _ in range(L):
+        cap = n + 1
+        kv = torch.empty(cap, 2, P, Hk, D, dtype=torch.float16, device=dev)
+        meta = torch.empty(-(-cap // P), 2, P, Hk, D, dtype=torch.float16, device=dev)
+        vlog = torch.zeros(cap, Hk, dtype=torch.float16, device=dev)
+        idx = torch.arange(cap, dtype=torch.int32, device=dev)
+        midx = torch.arange(meta.shape[0], dtype=torch.int32, device=dev)
+        scale = torch.exp(torch.randn(Hk, D, device=dev, generator=g))
+        K = (torch.randn(ctx, Hk, D, device=dev, generator=g) * scale).half()
+        V = torch.randn(ctx, Hk, D, device=dev, generator=g).half()
+        q = torch.randn(Hq, D, device=dev, generator=g).half()
+        S = ctx - 1
+        n0 = -(-S // P)
+        _lib.call("aoakv_append_kv_cache_prefill", K.data_ptr(), V.data_ptr(), S, kv.data_ptr(),
+                  idx.data_ptr(), n0, (S - 1) % P + 1, cap, meta.data_ptr(), midx.data_ptr(),
+                  -(-n0 // P), (n0 - 1) % P + 1, meta.shape[0], vlog.data_ptr(), Hk, D, P, 0,
+                  stream)
+        layers.append((kv, meta, vlog, idx, midx, q, K[-1].clone(), V[-1].clone(),
+                       torch.empty(Hq, D, dtype=torch.float16, device=dev)))
+        del K, V
+    ws_n = _lib.size_query("aoakv_step_workspace_size", Hq, D, n + 1, kp)
+    ws = torch.zeros(ws_n, dtype=torch.uint8, device=dev)
+    mode = _lib.SCORE_AOAKV if a.method == "aoakv" else _lib.SCORE_QUEST
+
+    def run():
+        st = torch.cuda.current_stream().cuda_stream
+        for kv, meta, vlog, idx, midx, q, k, v, o in layers:
+            _lib.call("aoakv_decode_step_gqa", q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                      o.data_ptr(), kv.data_ptr(), idx.data_ptr(), n, (ctx - 1) % P + 1,
+                      kv.shape[0], meta.data_ptr(), midx.data_ptr(), meta.shape[0],
+                      vlog.data_ptr(), Hq, Hk, D, P, kp, mode, 0, None, ws.data_ptr(), ws_n, st)
+    graph = capture(run, dev)
+    steps = max(10, a.steps // 2)
+    ms = time_replays(graph.replay, steps, 3, world, dev)
+    _lib.check_device()
+    us = ms * 1e3 / (steps * L)
+    b = ((n - 1) * Hk * (2 * D * 2 + (2 if a.method == "aoakv" else 0)) +
+         kp * P * Hk * D * 2 * 2 + 2 * Hq * D * 2)
+    del graph, layers
+    return {"metric": f"GQA sparse-decode µs/layer @{ctx} ctx, {budget} budget, 32 query / 8 KV "
+                      f"heads", "value": round(us, 3), "unit": "us", "roofline": roof(b, us, peak),
+            "gpu_launches": 4 * L * steps,
+            "config": {"workload": f"{L} layers, Hq 32, Hkv 8, head_dim 128, ctx {ctx}, budget "
+                                   f"{budget}, outlier K seed 1; append, group scoring, top-k, "
+                                   f"decode (four launches)"}}
+
+
 def prefill_key(a, world, rank, dev, peak):
     """Config 5's prefill: aoakv_append_kv_cache_prefill of a.long_ctx - 1
     tokens of one layer in one pass (KV pages, key max/min metadata of every
