@@ -5,8 +5,7 @@ Public surface, named after the reference's quest.utils
 
     TensorLayout, KvCache, InferenceController, BatchDecodeWithPagedKVCacheWrapper,
     append_kv, decode_estimate, decode_topk, decode_sparse_attn,
-    apply_rope_in_place, rms_norm_forward, and prefill_forward (not built
-    here: it raises NotImplementedError)
+    apply_rope_in_place, rms_norm_forward, prefill_forward
 
 plus ``topk_filtering`` (the raw top-k op),
 ``InferenceController.decode_step`` (append + estimate + top-k + decode in one
@@ -17,12 +16,14 @@ from ._lib import AoaKvError, check_device, device_error
 from .controller import InferenceController, KvCache, KvPool, TensorLayout
 from .decode_wrapper import BatchDecodeWithPagedKVCacheWrapper
 from .ops import (append_kv, apply_rope_in_place, decode_estimate, decode_sparse_attn,
-                  decode_topk, prefill_forward, rms_norm_forward, topk_filtering)
+                  decode_topk, prefill_forward, prefill_with_paged_kv_cache, rms_norm_forward,
+                  topk_filtering)
 from .step_plan import StepPlan
 
 __all__ = [
     "TensorLayout", "KvCache", "KvPool", "InferenceController",
-    "BatchDecodeWithPagedKVCacheWrapper", "append_kv", "prefill_forward", "decode_estimate",
+    "BatchDecodeWithPagedKVCacheWrapper", "append_kv", "prefill_forward",
+    "prefill_with_paged_kv_cache", "decode_estimate",
     "decode_topk", "decode_sparse_attn", "rms_norm_forward", "apply_rope_in_place",
     "topk_filtering", "StepPlan", "AoaKvError", "check_device", "device_error",
 ]

@@ -81,6 +81,8 @@ SIGNATURES = {
     "aoakv_shard_finish_p2p": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32,
                                _c_i32, _c_p, _c_p, _c_p],
     "aoakv_shard_merge_p2p": [_c_p, _c_i32, _c_p, _c_p],
+    "aoakv_prefill_paged": [_c_p, _c_p, _c_p, _c_p, _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32,
+                            _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_f, _c_p],
     "aoakv_decode_step_gqa": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p,
                               _c_p, _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                               _c_i32, _c_i32, _c_p, _c_p, _c_size, _c_p],

@@ -92,6 +92,27 @@ int make_kv_tmap_sw128(CUtensorMap* map, const void* kv, int H, int D, int P, in
   return AOAKV_OK;
 }
 
+int make_q_tmap_sw128(CUtensorMap* map, const void* q, int H, int D, int rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(AOAKV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (reinterpret_cast<uintptr_t>(q) % 16)
+    return set_error(AOAKV_ERR_INVALID_ARG, "q must be 16-byte aligned");
+  if (D % 64) return set_error(AOAKV_ERR_UNSUPPORTED, "swizzled q tiles need head_dim % 64 == 0");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2,
+                           static_cast<cuuint64_t>(H) * D * 2};
+  cuuint32_t box[3] = {64u, 1u, 128u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(q), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(AOAKV_ERR_CUDA,
+                     "cuTensorMapEncodeTiled (q rows) failed with CUresult " + std::to_string(r));
+  return AOAKV_OK;
+}
+
 int make_meta_tmap(CUtensorMap* map, const void* meta, int H, int D, int P, int meta_cap,
                    int box_heads) {
   auto fn = encode_fn();

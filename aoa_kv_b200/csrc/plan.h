@@ -31,6 +31,9 @@ int make_kv_tmap(CUtensorMap* map, const void* kv, int H, int D, int P, int cap)
 // V) rows arrive as D/64 tiles of P rows x 128 bytes, 16-byte units of row r
 // permuted by r mod 8 (bank-conflict-free 8x8 matrix loads).
 int make_kv_tmap_sw128(CUtensorMap* map, const void* kv, int H, int D, int P, int cap);
+// 3-D tensor map over rows [rows, H, D] fp16 (q of a prefill): box {64, 1,
+// 128} with the 128-byte swizzle, one 64-channel block of 128 rows.
+int make_q_tmap_sw128(CUtensorMap* map, const void* q, int H, int D, int rows);
 // 3-D tensor map over one layer's metadata pages: dims {D, H, meta_cap*2*P},
 // box {D, box_heads, 1} (one page's max or min block for box_heads heads).
 int make_meta_tmap(CUtensorMap* map, const void* meta, int H, int D, int P, int meta_cap,

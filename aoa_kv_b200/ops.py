@@ -144,14 +144,52 @@ def decode_sparse_attn(q: torch.Tensor, iController: InferenceController, layer_
     return o
 
 
-def _not_built(name: str, where: str):
-    raise NotImplementedError(
-        f"{name} ({where}) is outside the sparse-decode path this library builds; "
-        "use the reference or torch for it")
+def prefill_with_paged_kv_cache(q: torch.Tensor, kv_data: torch.Tensor, kv_indices: torch.Tensor,
+                                kv_last_page_len: int, causal: bool = True, layout: int = 0,
+                                allow_fp16_qk_reduction: bool = False, rope_scale: float = 1.0,
+                                rope_theta: float = 1e4, lse: Optional[torch.Tensor] = None,
+                                sm_scale: Optional[float] = None) -> torch.Tensor:
+    """ops/csrc/batch_prefill.cu:27-116: attention of q [qo_len, Hq, D] over
+    one sequence's paged KV, kv_data [cap, 2, P, Hk, D] (NHD), pages
+    kv_indices (int32, last page last, holding kv_last_page_len tokens).
+    Causal: query i attends KV tokens <= i + kv_len - qo_len. Returns o like
+    q. The reference runs with RoPE off and fp32 score accumulation, so
+    rope_scale, rope_theta and allow_fp16_qk_reduction change nothing here
+    either. lse (optional, [qo_len, Hq] fp32) receives the natural-log
+    log-sum-exp of every row."""
+    _check_half_cuda(q, "q")
+    _check_half_cuda(kv_data, "kv_data")
+    _check_i32_cuda(kv_indices, "kv_indices")
+    if q.dim() != 3 or kv_data.dim() != 5 or kv_data.size(1) != 2:
+        raise RuntimeError("q must be [qo_len, H, D] and kv_data [pages, 2, P, H, D]")
+    if int(layout) != _lib.LAYOUT_NHD:
+        raise RuntimeError("prefill_with_paged_kv_cache: only the NHD layout is built")
+    if q.size(2) != kv_data.size(4):
+        raise RuntimeError("q and kv_data head_dim differ")
+    if lse is not None:
+        _check_cuda_contig(lse, "lse")
+        if lse.dtype != torch.float32 or lse.shape != q.shape[:2]:
+            raise RuntimeError("lse must be float32 [qo_len, num_qo_heads]")
+    o = torch.empty_like(q)
+    _lib.call("aoakv_prefill_paged", _ptr(q), _ptr(o), _ptr(lse), _ptr(kv_data), kv_data.size(0),
+              _ptr(kv_indices), kv_indices.numel(), int(kv_last_page_len), q.size(0), q.size(1),
+              kv_data.size(3), q.size(2), kv_data.size(2), int(layout), int(bool(causal)),
+              0.0 if sm_scale is None else float(sm_scale), _stream(q))
+    return o
 
 
-def prefill_forward(q, iController, layer_idx, rope_scale=None, rope_theta=None):
-    _not_built("prefill_forward", "utils/__init__.py:133-175")
+def prefill_forward(q: torch.Tensor, iController: InferenceController, layer_idx: int,
+                    rope_scale: Optional[float] = None,
+                    rope_theta: Optional[float] = None) -> torch.Tensor:
+    """utils/__init__.py:127-172: causal self-attention of the prompt's q
+    [S, H, D] over the layer's paged cache, whose K/V (and metadata) the
+    caller has already appended for these tokens."""
+    c = iController
+    return prefill_with_paged_kv_cache(q, c.kv_cache.buf_layer(layer_idx),
+                                       c.kv_indices_with_last, c.kv_cache.last_page_len, True,
+                                       c.layout, False,
+                                       1.0 if rope_scale is None else rope_scale,
+                                       1e4 if rope_theta is None else rope_theta)
 
 
 def apply_rope_in_place(q: torch.Tensor, k: torch.Tensor, past_kv_len: int,

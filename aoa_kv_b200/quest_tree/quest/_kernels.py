@@ -8,8 +8,8 @@ Differences, all documented in include/aoakv.h:
     == logical page id is assumed (a fresh KvPool hands out pages in order).
   * topk_filtering ignores ``buf`` (no scratch is needed) and any head count
     is accepted (the reference asserts 32, topk.cu:28).
-  * prefill_with_paged_kv_cache, apply_rope_in_place and rms_norm_forward are
-    outside the sparse-decode path and raise NotImplementedError.
+  * prefill_with_paged_kv_cache runs the tcgen05 prefill kernel; like the
+    reference (RotaryMode::kNone) it applies no RoPE.
 """
 from __future__ import annotations
 
@@ -106,8 +106,12 @@ class BatchDecodeWithPagedKVCachePyTorchWrapper:
                         paged_kv_last_page_len, paged_kv_last_page_idx, rope_scale, rope_theta)
 
 
-def prefill_with_paged_kv_cache(*args, **kwargs):
-    _ops._not_built("prefill_with_paged_kv_cache", "ops/csrc/batch_prefill.cu")
+def prefill_with_paged_kv_cache(q, kv_data, kv_indices, kv_last_page_len, causal, layout,
+                                allow_fp16_qk_reduction, rope_scale, rope_theta):
+    """batch_prefill.cu:27-116 (pybind prefill_with_paged_kv_cache)."""
+    return _ops.prefill_with_paged_kv_cache(q, kv_data, kv_indices, kv_last_page_len, causal,
+                                            int(layout), allow_fp16_qk_reduction, rope_scale,
+                                            rope_theta)
 
 
 def apply_rope_in_place(q, k, past_kv_len, rope_scale, rope_theta):

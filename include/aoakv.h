@@ -464,6 +464,28 @@ AOAKV_API int aoakv_decode_step_grid(
     int32_t sink_first_page, int32_t* selected_out, void* workspace,
     size_t workspace_bytes, int32_t max_ctas, void* stream);
 
+/* Paged prefill attention (ops/csrc/batch_prefill.cu:27-116,
+ * prefill_with_paged_kv_cache; kernel include/prefill/prefill.cuh:688-1119):
+ * one sequence of qo_len new tokens, q and o [qo_len, num_qo_heads,
+ * head_dim] fp16, attending the layer's paged KV (NHD pages
+ * [kv_capacity_pages, 2, page_size, num_kv_heads, head_dim]) of kv_len =
+ * (num_kv_pages - 1) * page_size + kv_last_page_len tokens, whose K/V
+ * already include the new tokens. Query i sits at position kv_len - qo_len +
+ * i; causal != 0 lets it attend KV tokens j <= i + kv_len - qo_len (needs
+ * qo_len <= kv_len). Query head h reads KV head h / (num_qo_heads /
+ * num_kv_heads). sm_scale <= 0 means 1/sqrt(head_dim). lse (optional,
+ * [qo_len, num_qo_heads] fp32) receives each row's natural-log
+ * log-sum-exp of the scaled scores. head_dim 64 or 128; page_size 8, 16,
+ * 32, 64 or 128. One launch on the tcgen05 tensor cores (accumulators in
+ * tensor memory); no workspace, no allocation, no synchronisation. The
+ * reference's rope_scale / rope_theta arguments are not taken: it runs this
+ * kernel with RoPE off (RotaryMode::kNone, batch_prefill.cu:96). */
+AOAKV_API int aoakv_prefill_paged(
+    const void* q, void* o, float* lse, const void* kv_data, int32_t kv_capacity_pages,
+    const int32_t* kv_indices, int32_t num_kv_pages, int32_t kv_last_page_len, int32_t qo_len,
+    int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+    int32_t layout, int32_t causal, float sm_scale, void* stream);
+
 /* Grouped-query attention (GQA; the reference's CUDA tree is MHA only,
  * docs/KERNEL_DIFF.md:66-76): the step of aoakv_decode_step for
  * num_qo_heads query heads sharing num_kv_heads KV heads (num_qo_heads a

@@ -260,3 +260,31 @@ def step_gqa(q: np.ndarray, k_new: np.ndarray, v_new: np.ndarray, c: LayerCache,
     for i in range(g):
         out[i::g] = sparse_decode(q[i::g], c, sel, last, last_len)
     return out, np.concatenate([sel, np.full((c.H, 1), last)], axis=1)
+
+
+def prefill_attention(q: np.ndarray, K: np.ndarray, V: np.ndarray, causal: bool = True,
+                      sm_scale: float | None = None) -> tuple[np.ndarray, np.ndarray]:
+    """Prefill attention of one sequence (ops/csrc/batch_prefill.cu:27-116;
+    the reference test's CPU form quest/tests/test_prefill_attention.py:17-40):
+    q [Sq, Hq, D], K and V [Skv, Hk, D] (the whole sequence, new tokens
+    last). Query i attends KV tokens j <= i + Skv - Sq when causal; scores
+    q.k * sm_scale (1/sqrt(D) by default), softmax in fp32; query head h uses
+    KV head h // (Hq / Hk). Returns o [Sq, Hq, D] fp32 and the natural-log
+    log-sum-exp [Sq, Hq] of the scaled scores."""
+    Sq, Hq, D = q.shape
+    Skv, Hk = K.shape[0], K.shape[1]
+    g = Hq // Hk
+    scale = 1.0 / math.sqrt(D) if sm_scale is None else sm_scale
+    qf = q.astype(F32).transpose(1, 0, 2)                       # [Hq, Sq, D]
+    kf = np.repeat(K.astype(F32).transpose(1, 0, 2), g, axis=0)  # [Hq, Skv, D]
+    vf = np.repeat(V.astype(F32).transpose(1, 0, 2), g, axis=0)
+    s = np.matmul(qf, kf.transpose(0, 2, 1)) * F32(scale)      # [Hq, Sq, Skv]
+    if causal:
+        allowed = np.arange(Skv)[None, :] <= (np.arange(Sq)[:, None] + (Skv - Sq))
+        s = np.where(allowed[None], s, -np.inf)
+    m = s.max(axis=-1, keepdims=True)
+    p = np.exp(s - m)
+    l = p.sum(axis=-1, keepdims=True)
+    o = np.matmul(p / l, vf)                                    # [Hq, Sq, D]
+    lse = (m + np.log(l))[..., 0]                               # [Hq, Sq]
+    return o.transpose(1, 0, 2).astype(F32), lse.T.astype(F32)

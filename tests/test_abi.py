@@ -101,3 +101,23 @@ def test_merge_and_map_argument_checks():
     _expect("aoakv_merge_states", None, 1, 2, 32, 128, 1, None, None, match="NULL")
     _expect("aoakv_map_pages", 1, -1, 0, 4, 1, 1, None, match="bad sizes")
     _expect("aoakv_map_pages", 1, 0, 0, 4, 1, 1, None, code=0)  # nothing to map: no launch
+
+
+def _prefill_args(qo_len=10, n_pages=2, last=16, hq=32, hk=32, d=128, p=16, causal=1):
+    # q, o, lse, kv_data, cap, kv_indices, n_pages, last_len, qo_len, hq, hk, d, p, layout,
+    # causal, sm_scale, stream (pointers are dummies: every case fails or returns before use)
+    return (16, 16, None, 16, 8, 16, n_pages, last, qo_len, hq, hk, d, p, 0, causal,
+            ctypes.c_float(0.0), None)
+
+
+def test_prefill_rejects_bad_shapes():
+    _expect("aoakv_prefill_paged", *_prefill_args(d=96), match="head_dim")
+    _expect("aoakv_prefill_paged", *_prefill_args(p=24), match="page_size")
+    _expect("aoakv_prefill_paged", *_prefill_args(hq=12, hk=8), match="multiple")
+    _expect("aoakv_prefill_paged", *_prefill_args(last=17), match="kv_last_page_len")
+    # causal needs qo_len <= kv_len = (2 - 1) * 16 + 3 = 19
+    _expect("aoakv_prefill_paged", *_prefill_args(qo_len=20, last=3), match="qo_len <= kv_len")
+
+
+def test_prefill_empty_query_is_a_no_op():
+    _expect("aoakv_prefill_paged", *_prefill_args(qo_len=0), code=0)
