@@ -7,16 +7,18 @@
 // quest/tests/test_prefill_attention.py:34-36); scale 1/sqrt(D) unless
 // given. Query head h reads KV head h / (Hq / Hk).
 //
-// One CTA per (128-query tile, query head), 192 threads:
+// One CTA per (128-query tile, query head), 224 threads:
 //   warps 0-3  softmax: thread r owns query row r (tensor-memory lane r)
-//   warp 4     TMA: the Q tile once, then K and V tiles of 128 tokens (one
-//              box per page and 64-channel half) through a 2-stage ring
+//   warp 4     TMA: the Q tile once, then K tiles of 128 tokens (one box per
+//              page and 64-channel half) through a 3-stage ring
+//   warp 6     TMA: the V tiles through a 2-stage ring
 //   warp 5     tensor memory allocation; one thread issues the MMAs
 // Per KV tile j:  S_j = Q K_j^T   (M 128, N 128, K D) into S buffer j % 2
 //                 softmax warps read S_j, write P_j (fp16) to shared memory
 //                 O += P_j V_j     (M 128, N D, K 128; V read MN-major)
 // S_{j+1} is issued before PV_j, so the tensor cores compute the next
-// scores while the softmax warps exponentiate. A row's running max is only
+// scores while the softmax warps exponentiate. A K tile is released when its
+// S is done, a V tile when its PV is: the K ring runs further ahead. A row's running max is only
 // raised (and its O row rescaled in tensor memory) when the tile's max
 // exceeds it by more than 8 in log2 units; P then stays <= 256, well inside
 // fp16, and the final O / l is unchanged by which max was used.
@@ -31,8 +33,9 @@ namespace aoakv {
 namespace {
 
 constexpr int kPfRows = 128;                   // query rows per CTA, KV tokens per tile
-constexpr int kPfThreads = 192;
-constexpr int kPfStages = 2;
+constexpr int kPfThreads = 224;
+constexpr int kPfKStages = 3;                  // K tiles are freed as soon as S_j is done
+constexpr int kPfVStages = 2;                  // V tiles only after PV_j
 constexpr uint32_t kPfBlock = kPfRows * 128;   // 128 rows x 64 fp16: one swizzled block
 constexpr uint32_t kPfTmemCols = 512;
 constexpr uint32_t kPfTmemO = 256u;            // S buffers at columns 0 and 128
@@ -53,9 +56,11 @@ struct PrefillArgs {
 template <int D>
 struct PfLayout {
   static constexpr int NH = D / 64;                      // 64-channel blocks
+  static constexpr uint32_t tile = NH * kPfBlock;        // one Q, K or V tile
   static constexpr uint32_t q = 0;
-  static constexpr uint32_t kv = NH * kPfBlock;          // stage s: K at kv + s*2*NH*block
-  static constexpr uint32_t p = kv + kPfStages * 2 * NH * kPfBlock;
+  static constexpr uint32_t k = tile;                    // kPfKStages tiles
+  static constexpr uint32_t v = k + kPfKStages * tile;   // kPfVStages tiles
+  static constexpr uint32_t p = v + kPfVStages * tile;   // 128 x 128 fp16: 2 blocks
   static constexpr uint32_t bars = p + 2 * kPfBlock;
   static constexpr uint32_t bytes = bars + 256;
 };
@@ -76,6 +81,42 @@ __device__ __forceinline__ bool pf_wait_warp(uint64_t* bar, uint32_t parity, int
   return __all_sync(0xffffffffu, pf_wait(bar, parity, err, abort_flag));
 }
 
+// One thread streams the K (kvsel 0) or V (kvsel 1) tiles of the CTA's KV
+// range through a ring of `stages` tiles: one TMA box per page and 64-channel
+// block; pages past the sequence read as zeros (page id = capacity is out
+// of the tensor map). Waits at the end for its own copies still in flight.
+template <int NH>
+__device__ void pf_produce(const PrefillArgs& a, const CUtensorMap* map, uint8_t* ring,
+                           int stages, uint64_t* full, uint64_t* empty, int kvsel, int hk,
+                           int n_tiles, volatile int* abort_flag) {
+  const int per_tile = kPfRows / a.P;
+  int issued = 0;
+  for (int j = 0; j < n_tiles; ++j) {
+    const int s = j % stages;
+    if (j >= stages && !pf_wait(&empty[s], ((j / stages) - 1) & 1, a.err, abort_flag)) break;
+    uint8_t* buf = ring + s * NH * kPfBlock;
+    mbar_arrive_expect_tx(&full[s], NH * kPfBlock);
+    for (int pi = 0; pi < per_tile; ++pi) {
+      const int g = j * per_tile + pi;
+      int phys = a.kv_cap;
+      if (g < a.n_pages) {
+        phys = __ldg(a.kv_indices + g);
+        if (phys < 0 || phys >= a.kv_cap) {
+          raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
+          phys = a.kv_cap;
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < NH; ++c)
+        tma_load_3d(buf + c * kPfBlock + pi * a.P * 128, map, c * 64, hk,
+                    (2 * phys + kvsel) * a.P, &full[s]);
+    }
+    issued = j + 1;
+  }
+  for (int j = max(0, issued - stages); j < issued; ++j)
+    mbar_wait_bounded(&full[j % stages], (j / stages) & 1, a.err);
+}
+
 template <int D>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap qmap,
@@ -86,10 +127,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint8_t* smem = align_smem<1024>(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::bars);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;                 // [kPfStages]
-  uint64_t* v_full = k_full + kPfStages;       // [kPfStages]
-  uint64_t* kv_empty = v_full + kPfStages;     // [kPfStages]
-  uint64_t* s_full = kv_empty + kPfStages;     // [2]
+  uint64_t* k_full = q_full + 1;               // [kPfKStages]
+  uint64_t* k_empty = k_full + kPfKStages;     // [kPfKStages]
+  uint64_t* v_full = k_empty + kPfKStages;     // [kPfVStages]
+  uint64_t* v_empty = v_full + kPfVStages;     // [kPfVStages]
+  uint64_t* s_full = v_empty + kPfVStages;     // [2]
   uint64_t* p_ready = s_full + 2;
   uint64_t* o_done = p_ready + 1;
   uint64_t* mma_idle = o_done + 1;
@@ -105,14 +147,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int last_q = min(q0 + kPfRows, a.qo_len) - 1;
   const int kv_hi = a.causal ? min(a.kv_len, last_q + off + 1) : a.kv_len;
   const int n_tiles = (kv_hi + kPfRows - 1) / kPfRows;
-  const int pages_per_tile = kPfRows / a.P;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < kPfStages; ++s) {
+    for (int s = 0; s < kPfKStages; ++s) {
       mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < kPfVStages; ++s) {
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
@@ -131,46 +175,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 4) {
-    // ------------------------------------------------------------ producer
+    // -------------------------------------------------- Q and K producer
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, NH * kPfBlock);
       for (int c = 0; c < NH; ++c)
         tma_load_3d(smem + L::q + c * kPfBlock, &qmap, c * 64, h, q0, q_full);
-      int issued = 0;
-      for (int j = 0; j < n_tiles; ++j) {
-        const int s = j % kPfStages;
-        if (j >= kPfStages &&
-            !pf_wait(&kv_empty[s], ((j / kPfStages) - 1) & 1, a.err, abort_flag))
-          break;
-        uint8_t* kb = smem + L::kv + s * 2 * NH * kPfBlock;
-        uint8_t* vb = kb + NH * kPfBlock;
-        mbar_arrive_expect_tx(&k_full[s], NH * kPfBlock);
-        mbar_arrive_expect_tx(&v_full[s], NH * kPfBlock);
-        for (int pi = 0; pi < pages_per_tile; ++pi) {
-          const int g = j * pages_per_tile + pi;
-          int phys = a.kv_cap;  // past the sequence: page id cap reads zeros
-          if (g < a.n_pages) {
-            phys = __ldg(a.kv_indices + g);
-            if (phys < 0 || phys >= a.kv_cap) {
-              raise_dev_error(a.err, AOAKV_DEV_ERR_BAD_PAGE);
-              phys = a.kv_cap;
-            }
-          }
-          for (int c = 0; c < NH; ++c) {
-            const uint32_t dst = c * kPfBlock + pi * a.P * 128;
-            tma_load_3d(kb + dst, &kvmap, c * 64, hk, 2 * phys * a.P, &k_full[s]);
-            tma_load_3d(vb + dst, &kvmap, c * 64, hk, (2 * phys + 1) * a.P, &v_full[s]);
-          }
-        }
-        issued = j + 1;
-      }
-      // copies still in flight must land before the CTA can exit
-      for (int j = max(0, issued - kPfStages); j < issued; ++j) {
-        const int s = j % kPfStages;
-        mbar_wait_bounded(&k_full[s], (j / kPfStages) & 1, a.err);
-        mbar_wait_bounded(&v_full[s], (j / kPfStages) & 1, a.err);
-      }
+      pf_produce<NH>(a, &kvmap, smem + L::k, kPfKStages, k_full, k_empty, 0, hk, n_tiles,
+                     abort_flag);
+      mbar_wait_bounded(q_full, 0, a.err);
     }
+  } else if (warp == 6) {
+    // ------------------------------------------------------- V producer
+    if (lane == 0)
+      pf_produce<NH>(a, &kvmap, smem + L::v, kPfVStages, v_full, v_empty, 1, hk, n_tiles,
+                     abort_flag);
   } else if (warp == 5) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
@@ -179,10 +197,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const uint32_t q_addr = smem_addr(smem + L::q);
       const uint32_t p_addr = smem_addr(smem + L::p);
       auto issue_s = [&](int j) -> bool {
-        const int s = j % kPfStages;
-        if (!pf_wait(&k_full[s], (j / kPfStages) & 1, a.err, abort_flag)) return false;
+        const int s = j % kPfKStages;
+        if (!pf_wait(&k_full[s], (j / kPfKStages) & 1, a.err, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_addr(smem + L::kv + s * 2 * NH * kPfBlock);
+        const uint32_t k_addr = smem_addr(smem + L::k + s * L::tile);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const uint32_t o = (k >> 2) * kPfBlock + (k & 3) * 32;
@@ -190,16 +208,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                       umma_desc_sw128(k_addr + o, 16, 1024), id_s, k > 0);
         }
         umma_commit(&s_full[j & 1]);
+        umma_commit(&k_empty[s]);
         return true;
       };
       bool ok = pf_wait(q_full, 0, a.err, abort_flag) && issue_s(0);
       for (int j = 0; ok && j < n_tiles; ++j) {
+        // S_{j+1} first: the tensor cores compute it while the softmax warps
+        // still work on tile j
         if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        const int s = j % kPfStages;
+        const int s = j % kPfVStages;
         if (!pf_wait(p_ready, j & 1, a.err, abort_flag)) break;
-        if (!pf_wait(&v_full[s], (j / kPfStages) & 1, a.err, abort_flag)) break;
+        if (!pf_wait(&v_full[s], (j / kPfVStages) & 1, a.err, abort_flag)) break;
         tc_fence_after();
-        const uint32_t v_addr = smem_addr(smem + L::kv + (s * 2 + 1) * NH * kPfBlock);
+        const uint32_t v_addr = smem_addr(smem + L::v + s * L::tile);
 #pragma unroll
         for (int k = 0; k < kPfRows / 16; ++k) {
           umma_f16_ss(tmem + kPfTmemO,
@@ -208,12 +229,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                       (j > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(o_done);
-        umma_commit(&kv_empty[s]);
+        umma_commit(&v_empty[s]);
       }
       umma_commit(mma_idle);  // every MMA issued above has finished
       mbar_wait_bounded(mma_idle, 0, a.err);
     }
-  } else {
+  } else if (warp < 4) {
     // ------------------------------------------------------------- softmax
     // Every branch around a tensor-memory access is warp-uniform (votes):
     // tcgen05.ld / st are .sync.aligned.
@@ -230,12 +251,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       tc_fence_after();
       float sv[128];
+      {
+        uint32_t u[128];
+        tmem_ld128(lane_base + (j & 1) * 128u, u);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t u[32];
-        tmem_ld32(lane_base + (j & 1) * 128u + c * 32, u);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(u[i]);
+        for (int i = 0; i < 128; ++i) sv[i] = __uint_as_float(u[i]);
       }
       const int kv0 = j * kPfRows;
       const int lim = row_hi - kv0;  // valid columns [0, lim)
@@ -244,9 +264,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         for (int i = 0; i < 128; ++i)
           if (i >= lim) sv[i] = -INFINITY;
       }
-      float mx = -INFINITY;
+      float mx8[8];  // eight independent chains: one warp per scheduler has no
+                     // other warps to hide a 128-long dependent chain behind
 #pragma unroll
-      for (int i = 0; i < 128; ++i) mx = fmaxf(mx, sv[i]);
+      for (int t = 0; t < 8; ++t) mx8[t] = sv[t];
+#pragma unroll
+      for (int i = 8; i < 128; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
+      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       mx *= a.scale_log2;
       const bool raise = mx > m_run + kPfRescale;
       const float f = raise ? ex2_approx(m_run - mx) : 1.f;  // 0 while m_run is -inf
@@ -258,7 +283,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, raise && l_run > 0.f)) {
+        if (__any_sync(0xffffffffu, raise)) {
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             uint32_t u[32];
@@ -276,13 +301,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       // the last tile may hold cache slots past kv_len (the last page's
       // unused tail): zero those V rows, since 0 * NaN would poison O
       if (kv0 + kPfRows > a.kv_len) {
-        const int s = j % kPfStages;
-        if (!pf_wait_warp(&v_full[s], (j / kPfStages) & 1, a.err, abort_flag)) {
+        const int s = j % kPfVStages;
+        if (!pf_wait_warp(&v_full[s], (j / kPfVStages) & 1, a.err, abort_flag)) {
           ok = false;
           break;
         }
         if (r >= a.kv_len - kv0) {
-          uint8_t* vb = smem + L::kv + (s * 2 + 1) * NH * kPfBlock + r * 128;
+          uint8_t* vb = smem + L::v + s * L::tile + r * 128;
 #pragma unroll
           for (int c = 0; c < NH; ++c)
 #pragma unroll
@@ -291,7 +316,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
       }
       const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
-      float sum = 0.f;
+      float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint8_t* prow = smem + L::p + r * 128;
 #pragma unroll
       for (int cc = 0; cc < 16; ++cc) {  // 16 units of 8 columns
@@ -300,7 +325,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         for (int t = 0; t < 4; ++t) {
           const float p0 = ex2_approx(fmaf(sv[cc * 8 + 2 * t], a.scale_log2, neg_m));
           const float p1 = ex2_approx(fmaf(sv[cc * 8 + 2 * t + 1], a.scale_log2, neg_m));
-          sum += p0 + p1;
+          sum8[t] += p0;
+          sum8[t + 4] += p1;
           const __half2 hp = __floats2half2_rn(p0, p1);
           w[t] = *reinterpret_cast<const uint32_t*>(&hp);
         }
@@ -308,7 +334,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         *reinterpret_cast<uint4*>(prow + (cc >> 3) * kPfBlock + unit * 16) =
             make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l_run += sum;
+      l_run += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) +
+               ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       fence_proxy_async_smem();  // P (and zeroed V rows) visible to the tensor cores
       tc_fence_before();
       mbar_arrive(p_ready);

@@ -98,6 +98,25 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
       : "memory");
 }
 
+// 128 consecutive fp32 columns of this thread's lane in one load.
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&v)[128]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {"
+      "%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
+      "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, "
+      "%64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, "
+      "%80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95, "
+      "%96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, "
+      "%112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127"
+      "}, [%128];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : AOAKV_R8(0), AOAKV_R8(8), AOAKV_R8(16), AOAKV_R8(24), AOAKV_R8(32), AOAKV_R8(40), AOAKV_R8(48), AOAKV_R8(56), AOAKV_R8(64), AOAKV_R8(72), AOAKV_R8(80), AOAKV_R8(88), AOAKV_R8(96), AOAKV_R8(104), AOAKV_R8(112), AOAKV_R8(120)
+      : "r"(taddr)
+      : "memory");
+}
+
 // Stores 32 columns of this thread's lane; completes before it returns.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
   asm volatile(
