@@ -7,21 +7,26 @@
 // quest/tests/test_prefill_attention.py:34-36); scale 1/sqrt(D) unless
 // given. Query head h reads KV head h / (Hq / Hk).
 //
-// One CTA per (128-query tile, query head), 224 threads:
-//   warps 0-3  softmax: thread r owns query row r (tensor-memory lane r)
-//   warp 4     TMA: the Q tile once, then K tiles of 128 tokens (one box per
-//              page and 64-channel half) through a 3-stage ring
-//   warp 6     TMA: the V tiles through a 2-stage ring
-//   warp 5     tensor memory allocation; one thread issues the MMAs
-// Per KV tile j:  S_j = Q K_j^T   (M 128, N 128, K D) into S buffer j % 2
-//                 softmax warps read S_j, write P_j (fp16) to shared memory
-//                 O += P_j V_j     (M 128, N D, K 128; V read MN-major)
-// S_{j+1} is issued before PV_j, so the tensor cores compute the next
-// scores while the softmax warps exponentiate. A K tile is released when its
-// S is done, a V tile when its PV is: the K ring runs further ahead. A row's running max is only
-// raised (and its O row rescaled in tensor memory) when the tile's max
-// exceeds it by more than 8 in log2 units; P then stays <= 256, well inside
-// fp16, and the final O / l is unchanged by which max was used.
+// One CTA per (256-query block, query head): two query tiles A and B of 128
+// rows share every K/V tile. 352 threads:
+//   warps 0-3  softmax of tile A: thread r owns row r (tensor-memory lane r)
+//   warps 4-7  softmax of tile B, same lanes, its own tensor-memory columns
+//   warp 8     TMA: the Q tiles once, then K tiles of 128 tokens (one box per
+//              page and 64-channel block) through a 3-stage ring
+//   warp 10    TMA: the V tiles through a 2-stage ring
+//   warp 9     tensor memory allocation; one thread issues the MMAs
+// Tensor memory (512 columns): S_A / P_A, S_B / P_B (128 each), O_A, O_B.
+// Per KV tile j the MMA thread issues, in this order,
+//   PV_A(j)    O_A += P_A(j) V_j   (P_A read from tensor memory)
+//   S_A(j+1)   S_A = Q_A K_{j+1}^T (over P_A: after PV_A(j) in issue order)
+//   PV_B(j), S_B(j+1)
+// so the tensor cores work on one tile while the softmax warps of the other
+// exponentiate. Each softmax warp reads its S row, writes P (fp16) over the
+// first 64 columns of S, and signals; the completion of S(j+1) also means
+// PV(j) is done, so O can be rescaled right then. A row's running max is
+// only raised (and its O row rescaled) when the tile's max exceeds it by
+// more than 8 in log2 units; P then stays <= 256, well inside fp16, and the
+// final O / l does not depend on which max was used.
 #include <cudaTypedefs.h>
 
 #include <cmath>
@@ -32,13 +37,12 @@
 namespace aoakv {
 namespace {
 
-constexpr int kPfRows = 128;                   // query rows per CTA, KV tokens per tile
-constexpr int kPfThreads = 224;
-constexpr int kPfKStages = 3;                  // K tiles are freed as soon as S_j is done
-constexpr int kPfVStages = 2;                  // V tiles only after PV_j
+constexpr int kPfRows = 128;                   // rows per query tile, KV tokens per tile
+constexpr int kPfThreads = 352;
+constexpr int kPfKStages = 3;                  // K tiles are freed as soon as both S are done
+constexpr int kPfVStages = 2;                  // V tiles after both PV
 constexpr uint32_t kPfBlock = kPfRows * 128;   // 128 rows x 64 fp16: one swizzled block
 constexpr uint32_t kPfTmemCols = 512;
-constexpr uint32_t kPfTmemO = 256u;            // S buffers at columns 0 and 128
 constexpr float kPfRescale = 8.f;              // log2 growth that forces a rescale
 
 struct PrefillArgs {
@@ -48,7 +52,7 @@ struct PrefillArgs {
   int n_pages, kv_len, kv_cap;
   int qo_len, Hq, group, P;
   int causal;
-  int n_qtiles;
+  int n_blocks;                // 256-row query blocks
   float scale_log2;            // sm_scale * log2(e)
   int* err;
 };
@@ -57,11 +61,10 @@ template <int D>
 struct PfLayout {
   static constexpr int NH = D / 64;                      // 64-channel blocks
   static constexpr uint32_t tile = NH * kPfBlock;        // one Q, K or V tile
-  static constexpr uint32_t q = 0;
-  static constexpr uint32_t k = tile;                    // kPfKStages tiles
+  static constexpr uint32_t q = 0;                       // Q_A, Q_B
+  static constexpr uint32_t k = 2 * tile;                // kPfKStages tiles
   static constexpr uint32_t v = k + kPfKStages * tile;   // kPfVStages tiles
-  static constexpr uint32_t p = v + kPfVStages * tile;   // 128 x 128 fp16: 2 blocks
-  static constexpr uint32_t bars = p + 2 * kPfBlock;
+  static constexpr uint32_t bars = v + kPfVStages * tile;
   static constexpr uint32_t bytes = bars + 256;
 };
 
@@ -117,6 +120,142 @@ __device__ void pf_produce(const PrefillArgs& a, const CUtensorMap* map, uint8_t
     mbar_wait_bounded(&full[j % stages], (j / stages) & 1, a.err);
 }
 
+// KV tiles a query tile needs: causal rows stop at their diagonal.
+__device__ __forceinline__ int pf_tiles(const PrefillArgs& a, int row0) {
+  if (row0 >= a.qo_len) return 0;
+  const int last = min(row0 + kPfRows, a.qo_len) - 1;
+  const int hi = a.causal ? min(a.kv_len, last + a.kv_len - a.qo_len + 1) : a.kv_len;
+  return (hi + kPfRows - 1) / kPfRows;
+}
+
+// The softmax warpgroup of one query tile (rows row0 ..): n_tiles KV tiles,
+// S / P at tensor-memory column s_col, O at o_col.
+template <int D>
+__device__ void pf_softmax(const PrefillArgs& a, uint8_t* smem, uint32_t tmem, int row0,
+                           int n_tiles, int zero_from, uint32_t s_col, uint32_t o_col,
+                           uint64_t* s_full, uint64_t* p_ready, uint64_t* o_final,
+                           uint64_t* v_full, int h, volatile int* abort_flag) {
+  using L = PfLayout<D>;
+  const int warp = (threadIdx.x >> 5) & 3;
+  const int r = (threadIdx.x & 127);  // row of the tile, tensor-memory lane
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  const int q_row = row0 + r;
+  const int row_hi = min(a.kv_len, a.causal ? q_row + a.kv_len - a.qo_len + 1 : a.kv_len);
+  float m_run = -INFINITY, l_run = 0.f;
+  for (int j = 0; j < n_tiles; ++j) {
+    if (!pf_wait_warp(&s_full[0], j & 1, a.err, abort_flag)) return;
+    tc_fence_after();
+    const int lim = row_hi - j * kPfRows;  // valid columns [0, lim)
+    // pass 1: the tile's row max
+    float mx8[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) mx8[t] = -INFINITY;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t u[64];
+      tmem_ld64(lane_base + s_col + half * 64, u);
+      const int lh = lim - half * 64;
+      if (lh < 64) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (i >= lh) u[i] = 0xff800000u;  // -inf
+      }
+#pragma unroll
+      for (int i = 0; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(u[i]));
+    }
+    float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                     fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+    mx *= a.scale_log2;
+    const bool raise = mx > m_run + kPfRescale;
+    const float f = raise ? ex2_approx(m_run - mx) : 1.f;  // 0 while m_run is -inf
+    // S(j) complete means PV(j-1) is too: O holds tiles < j
+    if (j > 0 && __any_sync(0xffffffffu, raise)) {
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t u[32];
+        tmem_ld32(lane_base + o_col + c * 32, u);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * f);
+        tmem_st32(lane_base + o_col + c * 32, u);
+      }
+    }
+    if (raise) {
+      l_run *= f;
+      m_run = mx;
+    }
+    // the tile holding kv_len may hold cache slots past it (the last page's
+    // unused tail): zero those V rows, since 0 * NaN would poison O. The
+    // first warpgroup to attend the tile does it, before its PV.
+    const int kv0 = j * kPfRows;
+    if (kv0 + kPfRows > a.kv_len && j >= zero_from) {
+      const int s = j % kPfVStages;
+      if (!pf_wait_warp(&v_full[s], (j / kPfVStages) & 1, a.err, abort_flag)) return;
+      if (r >= a.kv_len - kv0) {
+        uint8_t* vb = smem + L::v + s * L::tile + r * 128;
+#pragma unroll
+        for (int c = 0; c < L::NH; ++c)
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<uint4*>(vb + c * kPfBlock + u * 16) = make_uint4(0, 0, 0, 0);
+      }
+      fence_proxy_async_smem();
+    }
+    // pass 2: P = 2^(s * scale_log2 - m), fp16, over the first 64 columns
+    const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
+    float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t u[64];
+      tmem_ld64(lane_base + s_col + half * 64, u);
+      const int lh = lim - half * 64;
+      if (lh < 64) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (i >= lh) u[i] = 0xff800000u;
+      }
+      uint32_t pk[32];
+#pragma unroll
+      for (int t = 0; t < 32; ++t) {
+        const float p0 = ex2_approx(fmaf(__uint_as_float(u[2 * t]), a.scale_log2, neg_m));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(u[2 * t + 1]), a.scale_log2, neg_m));
+        sum8[t & 7] += p0 + p1;
+        const __half2 hp = __floats2half2_rn(p0, p1);
+        pk[t] = *reinterpret_cast<const uint32_t*>(&hp);
+      }
+      tmem_st32(lane_base + s_col + half * 32, pk);
+    }
+    l_run += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) +
+             ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+    tc_fence_before();
+    mbar_arrive(p_ready);
+  }
+  if (n_tiles == 0 || !pf_wait_warp(o_final, 0, a.err, abort_flag)) return;
+  tc_fence_after();
+  const bool live = q_row < a.qo_len;
+  const float inv = live ? 1.f / l_run : 0.f;
+  __half* dst = a.o + (static_cast<size_t>(live ? q_row : 0) * a.Hq + h) * D;
+#pragma unroll
+  for (int c = 0; c < D / 32; ++c) {
+    uint32_t u[32];
+    tmem_ld32(lane_base + o_col + c * 32, u);  // whole warp, rows past qo_len too
+    if (live) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint32_t w[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const __half2 hv = __floats2half2_rn(__uint_as_float(u[g * 8 + 2 * t]) * inv,
+                                               __uint_as_float(u[g * 8 + 2 * t + 1]) * inv);
+          w[t] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
+        *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+  if (live && a.lse)
+    a.lse[static_cast<size_t>(q_row) * a.Hq + h] = (m_run + log2f(l_run)) * 0.6931471805599453f;
+}
+
 template <int D>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap qmap,
@@ -131,22 +270,21 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* k_empty = k_full + kPfKStages;     // [kPfKStages]
   uint64_t* v_full = k_empty + kPfKStages;     // [kPfVStages]
   uint64_t* v_empty = v_full + kPfVStages;     // [kPfVStages]
-  uint64_t* s_full = v_empty + kPfVStages;     // [2]
-  uint64_t* p_ready = s_full + 2;
-  uint64_t* o_done = p_ready + 1;
-  uint64_t* mma_idle = o_done + 1;
+  uint64_t* s_full = v_empty + kPfVStages;     // [2]: tiles A, B
+  uint64_t* p_ready = s_full + 2;              // [2]
+  uint64_t* o_final = p_ready + 2;
+  uint64_t* mma_idle = o_final + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_idle + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = a.causal ? a.n_qtiles - 1 - static_cast<int>(blockIdx.x)
+  const int qb = a.causal ? a.n_blocks - 1 - static_cast<int>(blockIdx.x)
                           : static_cast<int>(blockIdx.x);  // causal: longest rows first
   const int h = blockIdx.y, hk = h / a.group;
-  const int q0 = qt * kPfRows;
-  const int off = a.kv_len - a.qo_len;
-  const int last_q = min(q0 + kPfRows, a.qo_len) - 1;
-  const int kv_hi = a.causal ? min(a.kv_len, last_q + off + 1) : a.kv_len;
-  const int n_tiles = (kv_hi + kPfRows - 1) / kPfRows;
+  const int q0 = qb * 2 * kPfRows;
+  const int n_a = pf_tiles(a, q0), n_b = pf_tiles(a, q0 + kPfRows);
+  const int n_tiles = max(n_a, n_b);  // n_b is n_a or n_a + 1, or 0 past qo_len
+  // tensor-memory columns of tile t: S / P at 128 t, O at 256 + 128 t
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -158,220 +296,121 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    mbar_init(&s_full[0], 1);
-    mbar_init(&s_full[1], 1);
-    mbar_init(p_ready, 128);
-    mbar_init(o_done, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_ready[t], 128);
+    }
+    mbar_init(o_final, 1);
     mbar_init(mma_idle, 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&qmap);
     tma_prefetch_desc(&kvmap);
   }
-  if (warp == 5) tmem_alloc(tmem_slot, kPfTmemCols);
+  if (warp == 9) tmem_alloc(tmem_slot, kPfTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
-    // -------------------------------------------------- Q and K producer
+  if (warp == 8) {
+    // ---------------------------------------------- Q and K producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, NH * kPfBlock);
-      for (int c = 0; c < NH; ++c)
-        tma_load_3d(smem + L::q + c * kPfBlock, &qmap, c * 64, h, q0, q_full);
+      const int nq = n_b > 0 ? 2 : 1;
+      mbar_arrive_expect_tx(q_full, nq * NH * kPfBlock);
+      for (int t = 0; t < nq; ++t)
+        for (int c = 0; c < NH; ++c)
+          tma_load_3d(smem + L::q + t * L::tile + c * kPfBlock, &qmap, c * 64, h,
+                      q0 + t * kPfRows, q_full);
       pf_produce<NH>(a, &kvmap, smem + L::k, kPfKStages, k_full, k_empty, 0, hk, n_tiles,
                      abort_flag);
       mbar_wait_bounded(q_full, 0, a.err);
     }
-  } else if (warp == 6) {
-    // ------------------------------------------------------- V producer
+  } else if (warp == 10) {
+    // ---------------------------------------------------- V producer
     if (lane == 0)
       pf_produce<NH>(a, &kvmap, smem + L::v, kPfVStages, v_full, v_empty, 1, hk, n_tiles,
                      abort_flag);
-  } else if (warp == 5) {
-    // ---------------------------------------------------------- MMA issuer
+  } else if (warp == 9) {
+    // ------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t id_s = umma_idesc_f16_f32(128, 128, 0, 0);
       constexpr uint32_t id_o = umma_idesc_f16_f32(128, D, 0, 1);
       const uint32_t q_addr = smem_addr(smem + L::q);
-      const uint32_t p_addr = smem_addr(smem + L::p);
-      auto issue_s = [&](int j) -> bool {
-        const int s = j % kPfKStages;
-        if (!pf_wait(&k_full[s], (j / kPfKStages) & 1, a.err, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t k_addr = smem_addr(smem + L::k + s * L::tile);
+      auto issue_s = [&](int t, int j) {  // S_t(j) = Q_t K_j^T
+        const uint32_t qa = q_addr + t * L::tile;
+        const uint32_t ka = smem_addr(smem + L::k + (j % kPfKStages) * L::tile);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const uint32_t o = (k >> 2) * kPfBlock + (k & 3) * 32;
-          umma_f16_ss(tmem + (j & 1) * 128u, umma_desc_sw128(q_addr + o, 16, 1024),
-                      umma_desc_sw128(k_addr + o, 16, 1024), id_s, k > 0);
+          umma_f16_ss(tmem + t * 128u, umma_desc_sw128(qa + o, 16, 1024),
+                      umma_desc_sw128(ka + o, 16, 1024), id_s, k > 0);
         }
-        umma_commit(&s_full[j & 1]);
-        umma_commit(&k_empty[s]);
-        return true;
+        umma_commit(&s_full[t]);
       };
-      bool ok = pf_wait(q_full, 0, a.err, abort_flag) && issue_s(0);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        // S_{j+1} first: the tensor cores compute it while the softmax warps
-        // still work on tile j
-        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        const int s = j % kPfVStages;
-        if (!pf_wait(p_ready, j & 1, a.err, abort_flag)) break;
-        if (!pf_wait(&v_full[s], (j / kPfVStages) & 1, a.err, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t v_addr = smem_addr(smem + L::v + s * L::tile);
+      auto issue_pv = [&](int t, int j) {  // O_t += P_t(j) V_j
+        const uint32_t va = smem_addr(smem + L::v + (j % kPfVStages) * L::tile);
 #pragma unroll
-        for (int k = 0; k < kPfRows / 16; ++k) {
-          umma_f16_ss(tmem + kPfTmemO,
-                      umma_desc_sw128(p_addr + (k >> 2) * kPfBlock + (k & 3) * 32, 16, 1024),
-                      umma_desc_sw128(v_addr + k * 16 * 128, kPfBlock, 1024), id_o,
+        for (int k = 0; k < kPfRows / 16; ++k)
+          umma_f16_ts(tmem + 256u + t * 128u, tmem + t * 128u + k * 8,
+                      umma_desc_sw128(va + k * 16 * 128, kPfBlock, 1024), id_o,
                       (j > 0 || k > 0) ? 1u : 0u);
-        }
-        umma_commit(o_done);
-        umma_commit(&v_empty[s]);
+      };
+      bool ok = pf_wait(q_full, 0, a.err, abort_flag) &&
+                pf_wait(&k_full[0], 0, a.err, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < 2; ++t)
+          if ((t == 0 ? n_a : n_b) > 0) issue_s(t, 0);
+        umma_commit(&k_empty[0]);
       }
-      umma_commit(mma_idle);  // every MMA issued above has finished
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int vs = j % kPfVStages;
+        if (!pf_wait(&v_full[vs], (j / kPfVStages) & 1, a.err, abort_flag)) break;
+        const bool next = j + 1 < n_tiles;
+        bool k_ready = false;
+        for (int t = 0; t < 2; ++t) {
+          const int n_t = t == 0 ? n_a : n_b;
+          if (j < n_t) {
+            if (!pf_wait(&p_ready[t], j & 1, a.err, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(t, j);
+          }
+          if (next && j + 1 < n_t) {
+            if (!k_ready) {
+              if (!pf_wait(&k_full[(j + 1) % kPfKStages], ((j + 1) / kPfKStages) & 1, a.err,
+                           abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              k_ready = true;
+            }
+            issue_s(t, j + 1);
+          }
+        }
+        if (!ok) break;
+        if (next) umma_commit(&k_empty[(j + 1) % kPfKStages]);
+        umma_commit(&v_empty[vs]);
+      }
+      umma_commit(o_final);  // every MMA issued above has finished
+      umma_commit(mma_idle);
       mbar_wait_bounded(mma_idle, 0, a.err);
     }
-  } else if (warp < 4) {
-    // ------------------------------------------------------------- softmax
-    // Every branch around a tensor-memory access is warp-uniform (votes):
-    // tcgen05.ld / st are .sync.aligned.
-    const int r = threadIdx.x;  // query row of the tile, tensor-memory lane
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    const int q_row = q0 + r;
-    const int row_hi = min(a.kv_len, a.causal ? q_row + off + 1 : a.kv_len);
-    float m_run = -INFINITY, l_run = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      if (!pf_wait_warp(&s_full[j & 1], (j >> 1) & 1, a.err, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float sv[128];
-      {
-        uint32_t u[128];
-        tmem_ld128(lane_base + (j & 1) * 128u, u);
-#pragma unroll
-        for (int i = 0; i < 128; ++i) sv[i] = __uint_as_float(u[i]);
-      }
-      const int kv0 = j * kPfRows;
-      const int lim = row_hi - kv0;  // valid columns [0, lim)
-      if (lim < kPfRows) {
-#pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (i >= lim) sv[i] = -INFINITY;
-      }
-      float mx8[8];  // eight independent chains: one warp per scheduler has no
-                     // other warps to hide a 128-long dependent chain behind
-#pragma unroll
-      for (int t = 0; t < 8; ++t) mx8[t] = sv[t];
-#pragma unroll
-      for (int i = 8; i < 128; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
-      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      mx *= a.scale_log2;
-      const bool raise = mx > m_run + kPfRescale;
-      const float f = raise ? ex2_approx(m_run - mx) : 1.f;  // 0 while m_run is -inf
-      // PV_{j-1} accumulates into O and reads the P buffer: it must be done
-      // before O is rescaled or P_j is written
-      if (j > 0) {
-        if (!pf_wait_warp(o_done, (j - 1) & 1, a.err, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, raise)) {
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t u[32];
-            tmem_ld32(lane_base + kPfTmemO + c * 32, u);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * f);
-            tmem_st32(lane_base + kPfTmemO + c * 32, u);
-          }
-        }
-      }
-      if (raise) {
-        l_run *= f;
-        m_run = mx;
-      }
-      // the last tile may hold cache slots past kv_len (the last page's
-      // unused tail): zero those V rows, since 0 * NaN would poison O
-      if (kv0 + kPfRows > a.kv_len) {
-        const int s = j % kPfVStages;
-        if (!pf_wait_warp(&v_full[s], (j / kPfVStages) & 1, a.err, abort_flag)) {
-          ok = false;
-          break;
-        }
-        if (r >= a.kv_len - kv0) {
-          uint8_t* vb = smem + L::v + s * L::tile + r * 128;
-#pragma unroll
-          for (int c = 0; c < NH; ++c)
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              *reinterpret_cast<uint4*>(vb + c * kPfBlock + u * 16) = make_uint4(0, 0, 0, 0);
-        }
-      }
-      const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
-      float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      uint8_t* prow = smem + L::p + r * 128;
-#pragma unroll
-      for (int cc = 0; cc < 16; ++cc) {  // 16 units of 8 columns
-        uint32_t w[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float p0 = ex2_approx(fmaf(sv[cc * 8 + 2 * t], a.scale_log2, neg_m));
-          const float p1 = ex2_approx(fmaf(sv[cc * 8 + 2 * t + 1], a.scale_log2, neg_m));
-          sum8[t] += p0;
-          sum8[t + 4] += p1;
-          const __half2 hp = __floats2half2_rn(p0, p1);
-          w[t] = *reinterpret_cast<const uint32_t*>(&hp);
-        }
-        const int unit = (cc & 7) ^ (r & 7);
-        *reinterpret_cast<uint4*>(prow + (cc >> 3) * kPfBlock + unit * 16) =
-            make_uint4(w[0], w[1], w[2], w[3]);
-      }
-      l_run += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) +
-               ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
-      fence_proxy_async_smem();  // P (and zeroed V rows) visible to the tensor cores
-      tc_fence_before();
-      mbar_arrive(p_ready);
-    }
-    if (ok && pf_wait_warp(o_done, (n_tiles - 1) & 1, a.err, abort_flag)) {
-      tc_fence_after();
-      const bool live = q_row < a.qo_len;
-      const float inv = live ? 1.f / l_run : 0.f;
-      __half* dst = a.o + (static_cast<size_t>(live ? q_row : 0) * a.Hq + h) * D;
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t u[32];
-        tmem_ld32(lane_base + kPfTmemO + c * 32, u);  // whole warp, rows past qo_len too
-        if (live) {
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint32_t w[4];
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const __half2 hv = __floats2half2_rn(__uint_as_float(u[g * 8 + 2 * t]) * inv,
-                                                   __uint_as_float(u[g * 8 + 2 * t + 1]) * inv);
-              w[t] = *reinterpret_cast<const uint32_t*>(&hv);
-            }
-            *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
-        }
-      }
-      if (live && a.lse)
-        a.lse[static_cast<size_t>(q_row) * a.Hq + h] =
-            (m_run + log2f(l_run)) * 0.6931471805599453f;
-    }
+  } else {
+    // ------------------------------------------- softmax, tiles A and B
+    const int t = warp >> 2;
+    pf_softmax<D>(a, smem, tmem, q0 + t * kPfRows, t == 0 ? n_a : n_b, t == 0 ? 0 : n_a,
+                  t * 128u, 256u + t * 128u, &s_full[t], &p_ready[t], o_final, v_full, h,
+                  abort_flag);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5) {
+  if (warp == 9) {
     __syncwarp();
     tmem_dealloc(tmem, kPfTmemCols);
   }
@@ -431,7 +470,7 @@ extern "C" int aoakv_prefill_paged(const void* q, void* o, float* lse, const voi
   a.group = num_qo_heads / num_kv_heads;
   a.P = page_size;
   a.causal = causal != 0;
-  a.n_qtiles = (qo_len + kPfRows - 1) / kPfRows;
+  a.n_blocks = (qo_len + 2 * kPfRows - 1) / (2 * kPfRows);
   const float scale = sm_scale > 0.f ? sm_scale : 1.f / std::sqrt(static_cast<float>(head_dim));
   a.scale_log2 = scale * 1.4426950408889634f;
   a.err = dev_error_ptr();
@@ -442,7 +481,7 @@ extern "C" int aoakv_prefill_paged(const void* q, void* o, float* lse, const voi
   AOAKV_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(smem)),
                  "prefill smem attribute");
-  const dim3 grid(a.n_qtiles, num_qo_heads);
+  const dim3 grid(a.n_blocks, num_qo_heads);
   auto s = static_cast<cudaStream_t>(stream);
   if (head_dim == 128)
     prefill_attn_kernel<128><<<grid, kPfThreads, smem, s>>>(qmap, kvmap, a);

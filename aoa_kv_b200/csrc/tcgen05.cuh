@@ -47,6 +47,19 @@ __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T: A (M x K, K-major) sits in tensor
+// memory, row i in lane i, two 16-bit elements per 32-bit column (element k
+// in column k / 2, the even element in the low half).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrives once on `bar` when every tcgen05 operation this thread issued so
 // far has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -94,6 +107,21 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
       "[%32];\n\t"
       "tcgen05.wait::ld.sync.aligned;"
       : AOAKV_R8(0), AOAKV_R8(8), AOAKV_R8(16), AOAKV_R8(24)
+      : "r"(taddr)
+      : "memory");
+}
+
+// 64 consecutive fp32 columns of this thread's lane in one load.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&v)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
+      "%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
+      "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63"
+      "}, [%64];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : AOAKV_R8(0), AOAKV_R8(8), AOAKV_R8(16), AOAKV_R8(24), AOAKV_R8(32), AOAKV_R8(40), AOAKV_R8(48), AOAKV_R8(56)
       : "r"(taddr)
       : "memory");
 }
