@@ -18,6 +18,7 @@ from .decode_wrapper import BatchDecodeWithPagedKVCacheWrapper
 from .ops import (append_kv, apply_rope_in_place, decode_estimate, decode_sparse_attn,
                   decode_topk, prefill_forward, prefill_with_paged_kv_cache, rms_norm_forward,
                   topk_filtering)
+from .page_table import DevicePageTable
 from .step_plan import StepPlan
 
 __all__ = [
@@ -25,7 +26,8 @@ __all__ = [
     "BatchDecodeWithPagedKVCacheWrapper", "append_kv", "prefill_forward",
     "prefill_with_paged_kv_cache", "decode_estimate",
     "decode_topk", "decode_sparse_attn", "rms_norm_forward", "apply_rope_in_place",
-    "topk_filtering", "StepPlan", "AoaKvError", "check_device", "device_error",
+    "topk_filtering", "StepPlan", "DevicePageTable", "AoaKvError", "check_device",
+    "device_error",
 ]
 
 

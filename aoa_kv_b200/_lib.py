@@ -15,7 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libaoakv.so"
 
 OK = 0
 ERR_NAMES = {1: "INVALID_ARG", 2: "UNSUPPORTED", 3: "CUDA", 4: "WORKSPACE"}
-DEV_ERR_NAMES = {0: "OK", 1: "BAD_PAGE", 2: "TIMEOUT"}
+DEV_ERR_NAMES = {0: "OK", 1: "BAD_PAGE", 2: "TIMEOUT", 3: "NO_PAGES"}
 DTYPE_F16, DTYPE_F32 = 0, 1
 LAYOUT_NHD, LAYOUT_HND = 0, 1
 SCORE_QUEST, SCORE_AOAKV = 0, 1
@@ -70,6 +70,15 @@ SIGNATURES = {
     "aoakv_decode_step_batched": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_p, _c_p, _c_p, _c_p,
                                   _c_i32, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                                   _c_i32, _c_i32, _c_i32, _c_p, _c_p],
+    "aoakv_page_table_bytes": [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_sizep],
+    "aoakv_page_table_create": [_c_pp, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_size,
+                                _c_p],
+    "aoakv_page_table_destroy": [_c_p],
+    "aoakv_page_table_append": [_c_p, _c_i32, _c_i32, _c_p],
+    "aoakv_page_table_release": [_c_p, _c_i32, _c_p],
+    "aoakv_page_table_layout": [_c_p, ctypes.POINTER(ctypes.c_int64)],
+    "aoakv_decode_step_table": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_p, _c_i32, _c_p,
+                                _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p],
     "aoakv_shard_propose": [_c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_p],
     "aoakv_shard_finish": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_p,
                            _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_p],

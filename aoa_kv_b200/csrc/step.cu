@@ -23,6 +23,7 @@
 
 #include "decode.cuh"
 #include "estimate.cuh"
+#include "page_table.h"
 #include "plan.h"
 #include "step_cluster.h"
 #include "topk.cuh"
@@ -886,15 +887,18 @@ extern "C" int aoakv_decode_step_grid(
                           workspace_bytes, max_ctas, stream);
 }
 
-extern "C" int aoakv_decode_step_batched(
-    const void* q, const void* k_new, const void* v_new, void* o, void* kv_data,
-    int32_t kv_capacity_pages, const int32_t* kv_indptr, const int32_t* kv_indices,
-    const int32_t* kv_last_page_len, void* metadata_data, int32_t metadata_capacity_pages,
-    const int32_t* metadata_indptr, const int32_t* metadata_indices, void* v_log_norm,
-    int32_t num_requests, int32_t max_pages, int32_t num_heads, int32_t head_dim,
-    int32_t page_size, int32_t page_budget, int32_t score_mode, int32_t sink_first_page,
-    int32_t* selected_out, void* stream) {
-  AOAKV_NVTX("aoakv_decode_step_batched");
+namespace aoakv {
+// The batched step; kv_ends (optional) gives each request's page-list end
+// (a device page table's layout) instead of kv_indptr[r + 1].
+static int run_batched(const void* q, const void* k_new, const void* v_new, void* o,
+                       void* kv_data, int32_t kv_capacity_pages, const int32_t* kv_indptr,
+                       const int32_t* kv_ends, const int32_t* kv_indices,
+                       const int32_t* kv_last_page_len, void* metadata_data,
+                       int32_t metadata_capacity_pages, const int32_t* metadata_indptr,
+                       const int32_t* metadata_indices, void* v_log_norm, int32_t num_requests,
+                       int32_t max_pages, int32_t num_heads, int32_t head_dim, int32_t page_size,
+                       int32_t page_budget, int32_t score_mode, int32_t sink_first_page,
+                       int32_t* selected_out, void* stream) {
   AOAKV_CHECK_ARG(q && k_new && v_new && o && kv_data && kv_indptr && kv_indices &&
                       kv_last_page_len && metadata_data && metadata_indptr && metadata_indices &&
                       v_log_norm,
@@ -944,10 +948,48 @@ extern "C" int aoakv_decode_step_batched(
   a.sel_cols = k_pages;
   a.err = dev_error_ptr();
   a.kv_indptr = kv_indptr;
+  a.kv_ends = kv_ends;
   a.meta_indptr = metadata_indptr;
   a.last_lens = kv_last_page_len;
   a.budget = page_budget;
   a.max_pages = max_pages;
   return launch_cluster_step(a, kv_sw, meta_map, D, cp, static_cast<cudaStream_t>(stream),
                              num_requests);
+}
+}  // namespace aoakv
+
+extern "C" int aoakv_decode_step_batched(
+    const void* q, const void* k_new, const void* v_new, void* o, void* kv_data,
+    int32_t kv_capacity_pages, const int32_t* kv_indptr, const int32_t* kv_indices,
+    const int32_t* kv_last_page_len, void* metadata_data, int32_t metadata_capacity_pages,
+    const int32_t* metadata_indptr, const int32_t* metadata_indices, void* v_log_norm,
+    int32_t num_requests, int32_t max_pages, int32_t num_heads, int32_t head_dim,
+    int32_t page_size, int32_t page_budget, int32_t score_mode, int32_t sink_first_page,
+    int32_t* selected_out, void* stream) {
+  AOAKV_NVTX("aoakv_decode_step_batched");
+  return run_batched(q, k_new, v_new, o, kv_data, kv_capacity_pages, kv_indptr, nullptr,
+                     kv_indices, kv_last_page_len, metadata_data, metadata_capacity_pages,
+                     metadata_indptr, metadata_indices, v_log_norm, num_requests, max_pages,
+                     num_heads, head_dim, page_size, page_budget, score_mode, sink_first_page,
+                     selected_out, stream);
+}
+
+extern "C" int aoakv_decode_step_table(
+    aoakv_page_table table, const void* q, const void* k_new, const void* v_new, void* o,
+    void* kv_data, int32_t kv_capacity_pages, void* metadata_data,
+    int32_t metadata_capacity_pages, void* v_log_norm, int32_t num_heads, int32_t head_dim,
+    int32_t page_budget, int32_t score_mode, int32_t sink_first_page, int32_t* selected_out,
+    void* stream) {
+  AOAKV_NVTX("aoakv_decode_step_table");
+  AOAKV_CHECK_ARG(table != nullptr, "table step: NULL table");
+  const PageTable* pt = reinterpret_cast<const PageTable*>(table);
+  const PageTableLayout& L = pt->L;
+  AOAKV_CHECK_ARG(L.cap <= kv_capacity_pages && L.mcap <= metadata_capacity_pages,
+                  "table step: the table's pools are larger than the given caches");
+  int32_t* b = pt->buf;
+  return run_batched(q, k_new, v_new, o, kv_data, kv_capacity_pages, b + L.kv_start,
+                     b + L.kv_end, b + L.kv_indices, b + L.last_len, metadata_data,
+                     metadata_capacity_pages, b + L.meta_start, b + L.meta_indices, v_log_norm,
+                     L.R, L.M, num_heads, head_dim, L.P, page_budget, score_mode,
+                     sink_first_page, selected_out, stream);
 }

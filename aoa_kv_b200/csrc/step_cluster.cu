@@ -617,8 +617,9 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     const int r = blockIdx.z;
     const int p0 = __ldcg(a.kv_indptr + r);
     const int m0 = __ldcg(a.meta_indptr + r);
-    n_pages = __ldcg(a.kv_indptr + r + 1) - p0;
+    n_pages = __ldcg(a.kv_ends ? a.kv_ends + r : a.kv_indptr + r + 1) - p0;
     last_len = __ldcg(a.last_lens + r);
+    if (a.kv_ends && n_pages == 0) return;  // an empty page-table slot
     // every CTA of the cluster reads the same values, so all leave together
     // (no cluster barrier is pending: the arrival above needs no wait)
     if (p0 < 0 || m0 < 0 || n_pages < 1 || n_pages > a.max_pages || last_len < 1 ||

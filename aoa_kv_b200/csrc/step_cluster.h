@@ -56,6 +56,8 @@ struct ClusterStepArgs {
   const int32_t* kv_indptr;
   const int32_t* meta_indptr;
   const int32_t* last_lens;
+  const int32_t* kv_ends;       // optional: request r's pages end at kv_ends[r] (not
+                                // kv_indptr[r+1]); then an empty request is skipped silently
   int budget;
   int max_pages;                // a request with more pages (or none) is skipped
   // One sequence split over GPUs by page range (shard != kShardNone). The

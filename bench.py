@@ -80,7 +80,8 @@ def parse():
                          "longctx / batched: that key alone; model: config 3; kernels: each "
                          "kernel of one headline layer alone, L2 flushed before every launch "
                          "(the workload of the per-kernel ncu summaries)")
-    ap.add_argument("--extras", default="longctx,batched,prefill_metadata,config2,config3,gqa",
+    ap.add_argument("--extras",
+                    default="longctx,batched,prefill_metadata,config2,config3,gqa,prefill_attn",
                     help="comma list of extra keys for the headline line ('' = none)")
     ap.add_argument("--layers", type=int, default=32, help="headline layers per step")
     ap.add_argument("--ctx", type=int, default=32768, help="headline context tokens")
@@ -564,10 +565,11 @@ def run_headline(a):
     for key in extras:
         fn = {"longctx": longctx_key, "batched": batched_key,
               "prefill_metadata": prefill_key, "config2": config2_key,
-              "config3": lambda *x: model_key(*x, steps=5, warmup=2), "gqa": gqa_key}.get(key)
+              "config3": lambda *x: model_key(*x, steps=5, warmup=2), "gqa": gqa_key,
+              "prefill_attn": prefill_attn_key}.get(key)
         if fn is None:
             raise SystemExit(f"unknown extra key {key!r}")
-        if key in ("prefill_metadata", "config2", "config3", "gqa") and world > 1:
+        if key in ("prefill_metadata", "config2", "config3", "gqa", "prefill_attn") and world > 1:
             continue  # single-GPU workloads: reported at N = 1
         val = fn(a, world, rank, dev, peak)
         if line is not None:
@@ -947,6 +949,58 @@ def gqa_key(a, world, rank, dev, peak):
             "config": {"workload": f"{L} layers, Hq 32, Hkv 8, head_dim 128, ctx {ctx}, budget "
                                    f"{budget}, outlier K seed 1; append, group scoring, top-k, "
                                    f"decode (four launches)"}}
+
+
+def prefill_attn_key(a, world, rank, dev, peak):
+    """Prefill attention of config 3's 32K prompt on one layer
+    (aoakv_prefill_paged: causal, 32 heads, head_dim 128, page size 16, pages
+    in a shuffled page table): ms per layer and TFLOP/s, 4 * D * H * S(S+1)/2
+    flops, against the sustained bf16 tensor peak (a ~10 ms kernel). torch's
+    scaled_dot_product_attention on the same q/K/V, contiguous, is timed beside
+    it for context (a library kernel, not this library's)."""
+    import torch
+
+    from aoa_kv_b200 import _lib
+    S = 32768
+    n_pages = S // P
+    cap = n_pages + 4
+    g = torch.Generator(device=dev).manual_seed(6)
+    kv = torch.randn(cap, 2, P, H, D, device=dev, generator=g).half()
+    ids = torch.randperm(cap, device=dev, generator=g)[:n_pages].int()
+    q = torch.randn(S, H, D, device=dev, generator=g).half()
+    o = torch.empty_like(q)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def run():
+        _lib.call("aoakv_prefill_paged", q.data_ptr(), o.data_ptr(), None, kv.data_ptr(), cap,
+                  ids.data_ptr(), n_pages, P, S, H, H, D, P, 0, 1, 0.0, stream)
+    steps = 5
+    ms = time_replays(run, steps, 2, world, dev) / steps
+    _lib.check_device()
+    flops = 4.0 * D * H * S * (S + 1) / 2
+    tf = flops / (ms * 1e-3) / 1e12
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    tpeak = float(peaks.get("bf16_tflops_sustained") or 1400.0)
+    src = ("measured (MEASURED_PEAKS.json bf16_tflops_sustained)"
+           if peaks.get("bf16_tflops_sustained") else "fallback 1400 TFLOP/s sustained")
+    kt = kv[ids.long(), 0].reshape(S, H, D).transpose(0, 1)[None].contiguous()
+    vt = kv[ids.long(), 1].reshape(S, H, D).transpose(0, 1)[None].contiguous()
+    qt = q.transpose(0, 1)[None].contiguous()
+    sdpa = lambda: torch.nn.functional.scaled_dot_product_attention(qt, kt, vt, is_causal=True)
+    ms_t = time_replays(sdpa, steps, 2, world, dev) / steps
+    err = float((sdpa().transpose(1, 2)[0] - o).abs().max())
+    del kv, kt, vt, qt
+    return {"metric": "prefill attention ms/layer @32768 tokens (causal, 32 heads, head_dim 128)",
+            "value": round(ms, 3), "unit": "ms", "tflops": round(tf, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": tpeak,
+                         "unit": "TFLOP/s", "frac": round(tf / tpeak, 4), "peak_source": src,
+                         "flops": flops},
+            "gpu_launches": steps,
+            "torch_sdpa_ms": round(ms_t, 3), "max_abs_diff_vs_torch_sdpa": round(err, 5),
+            "config": {"workload": "one layer, 32768-token causal prefill, q [S, 32, 128] fp16, "
+                                   "KV in 16-token pages of a shuffled page table; tcgen05 MMAs, "
+                                   "accumulators in tensor memory"}}
 
 
 def prefill_key(a, world, rank, dev, peak):

@@ -54,6 +54,7 @@ enum {
   AOAKV_DEV_OK = 0,
   AOAKV_DEV_ERR_BAD_PAGE = 1,  /* a page id outside [0, capacity) was skipped */
   AOAKV_DEV_ERR_TIMEOUT = 2,   /* a bounded device-side wait gave up */
+  AOAKV_DEV_ERR_NO_PAGES = 3,  /* a page-table append found no room; the sequence is unchanged */
 };
 
 enum { AOAKV_DTYPE_F16 = 0, AOAKV_DTYPE_F32 = 1 };
@@ -531,6 +532,63 @@ AOAKV_API int aoakv_decode_step_batched(
     int32_t num_requests, int32_t max_pages, int32_t num_heads, int32_t head_dim,
     int32_t page_size, int32_t page_budget, int32_t score_mode, int32_t sink_first_page,
     int32_t* selected_out, void* stream);
+
+/* ------------------------------------------------ device-resident page table
+ * The reference keeps the page table on the host (quest/utils/kv_cache.py:
+ * 7-133 KvPool / KvCache, controller.py:82-141 rebuilding index tensors from
+ * Python lists every step). Here one device buffer holds, for num_seqs
+ * sequences, each sequence's KV page list (room for max_pages_per_seq) and
+ * metadata page list (room for ceil(max_pages_per_seq / page_size)), its
+ * page count, last-page length and token count, and the free stacks of the
+ * KV pool (kv_capacity_pages) and metadata pool (metadata_capacity_pages).
+ * Pages are allocated on the device, so a whole decode token (append +
+ * every layer's step) can be captured as one CUDA graph and replayed. The
+ * caller owns the buffer (aoakv_page_table_bytes bytes, 16-byte aligned). */
+typedef struct aoakv_page_table_s* aoakv_page_table;
+
+AOAKV_API int aoakv_page_table_bytes(int32_t num_seqs, int32_t max_pages_per_seq,
+                                     int32_t kv_capacity_pages, int32_t metadata_capacity_pages,
+                                     int32_t page_size, size_t* bytes);
+/* Initialises the buffer on `stream` (every sequence empty, both pools
+ * free; a fresh pool hands out page ids 0, 1, 2, ... like the reference's
+ * fresh set) and returns a host handle. */
+AOAKV_API int aoakv_page_table_create(aoakv_page_table* table_out, int32_t num_seqs,
+                                      int32_t max_pages_per_seq, int32_t kv_capacity_pages,
+                                      int32_t metadata_capacity_pages, int32_t page_size,
+                                      void* device_buffer, size_t buffer_bytes, void* stream);
+AOAKV_API int aoakv_page_table_destroy(aoakv_page_table table);
+/* KvCache.append_seq (kv_cache.py:115-126) + the metadata append of
+ * controller.py:82-87 on the device, one launch: num_tokens more tokens for
+ * sequence seq (-1: every sequence, in order). A new KV page when the last
+ * page is full or the sequence is empty; a new metadata page every
+ * page_size KV pages. A sequence that would exceed its room or a pool is
+ * left unchanged and AOAKV_DEV_ERR_NO_PAGES is recorded. */
+AOAKV_API int aoakv_page_table_append(aoakv_page_table table, int32_t seq, int32_t num_tokens,
+                                      void* stream);
+/* KvCache.release (kv_cache.py:128-133): the sequence's pages (seq -1:
+ * every sequence) go back to the pools, last page first, so they are handed
+ * out again in their old order. */
+AOAKV_API int aoakv_page_table_release(aoakv_page_table table, int32_t seq, void* stream);
+/* Word offsets (int32) of the buffer's regions: [0] KV free-stack height,
+ * [1] metadata free-stack height, [2] kv_start[R], [3] kv_end[R] (sequence
+ * r's KV pages are kv_indices[kv_start[r] .. kv_end[r])), [4] last_len[R],
+ * [5] seq_len[R], [6] meta_start[R], [7] meta_count[R], [8] kv_indices,
+ * [9] metadata_indices, [10] KV free stack, [11] metadata free stack,
+ * [12] total words, [13] R, [14] max_pages_per_seq, [15] metadata pages per
+ * sequence. */
+AOAKV_API int aoakv_page_table_layout(aoakv_page_table table, int64_t* words);
+/* aoakv_decode_step_batched over the table's sequences: sequence r's page
+ * count, last-page length and page lists are read on the device, so the
+ * call can be captured in a CUDA graph and replayed after
+ * aoakv_page_table_append(table, -1, 1) for every token. q, k_new, v_new, o
+ * are [num_seqs, num_heads, head_dim] (the new token already counted by the
+ * append); an empty sequence is skipped. Same limits as the batched step. */
+AOAKV_API int aoakv_decode_step_table(
+    aoakv_page_table table, const void* q, const void* k_new, const void* v_new, void* o,
+    void* kv_data, int32_t kv_capacity_pages, void* metadata_data,
+    int32_t metadata_capacity_pages, void* v_log_norm, int32_t num_heads, int32_t head_dim,
+    int32_t page_budget, int32_t score_mode, int32_t sink_first_page, int32_t* selected_out,
+    void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -19,8 +19,17 @@ are plain torch):
   test_approx_attention.py:17-110        _ref_self_approx_attention
   test_v_log_norm_prefill_claude.py:28-66 compute_expected_v_log_norm_cpu
 
+Page table (``pt_*.npz``): the reference's own host allocator, KvCache from
+kernels/aoa_kv/quest/utils/kv_cache.py (imported with a stub quest.utils.utils
+for its TensorLayout import), driven the way controller.py:82-87
+prepare_metadata drives it (a KV cache plus a metadata cache that appends one
+entry per new KV page); after every append the page lists and last-page
+lengths are recorded.
+
 Inputs come from tests/golden/gen.py (seeded, fp16); each file stores the
 input digest, the case parameters and the reference outputs.
+
+``--only page_table`` regenerates just the page-table files.
 """
 from __future__ import annotations
 
@@ -75,6 +84,49 @@ KT_APPROX_CASES = [  # name, seed, kv_len, page_budget (test_approx_attention.py
     ("kt_approx_1541_55", 35, 1541, 55), ("kt_approx_482_71", 36, 482, 71),
 ]
 KT_VLOG_CASES = [("kt_vlog_128", 41, 128), ("kt_vlog_256", 42, 256), ("kt_vlog_200", 43, 200)]
+
+PT_CASES = [  # name, page_size, max_seq_len, appends (prompt, then decode tokens)
+    ("pt_prompt100_decode40", 16, 4096, [100] + [1] * 40),
+    ("pt_pagefill_p16", 16, 4096, [16, 1, 15, 1, 16, 16, 1]),
+    ("pt_many_pages_p8", 8, 8192, [1000, 1, 1, 7, 1, 300]),
+    ("pt_meta_boundary", 16, 16384, [16 * 16, 1, 16 * 16 - 1, 1, 1]),
+]
+
+
+def load_ref_kv_cache():
+    for mod in ("quest", "quest.utils", "quest.utils.utils"):
+        sys.modules.setdefault(mod, types.ModuleType(mod))
+
+    class TensorLayout:  # quest/utils/utils.py's enum, only NHD is read
+        NHD = 0
+        HND = 1
+    sys.modules["quest.utils.utils"].TensorLayout = TensorLayout
+    path = REF / "kernels" / "aoa_kv" / "quest" / "utils" / "kv_cache.py"
+    spec = importlib.util.spec_from_file_location("_ref_kv_cache", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def make_page_table_goldens():
+    kvc = load_ref_kv_cache()
+    for name, P, max_len, appends in PT_CASES:
+        kv = kvc.KvCache(1, 1, 1, max_len, P, torch.float16, torch.device("cpu"))
+        meta = kvc.KvCache(1, 1, 1, (max_len + P - 1) // P, P, torch.float16,
+                           torch.device("cpu"))
+        n_kv, n_meta = (max_len + P - 1) // P, (max_len + P * P - 1) // (P * P)
+        kv_ids = np.full((len(appends), n_kv), -1, np.int32)
+        meta_ids = np.full((len(appends), n_meta), -1, np.int32)
+        last = np.zeros(len(appends), np.int32)
+        for i, n in enumerate(appends):
+            new_pages = kv.append_seq(n)  # controller.py:84-87
+            meta.append_seq(new_pages)
+            kv_ids[i, :len(kv.indicies)] = kv.indicies
+            meta_ids[i, :len(meta.indicies)] = meta.indicies
+            last[i] = kv.last_page_len
+        save(name, dict(page_size=P, max_seq_len=max_len, appends=appends), kv_ids=kv_ids,
+             meta_ids=meta_ids, last_page_len=last)
+        print(name, kv_ids.shape, meta_ids.shape)
 
 
 def load_filter_util():
@@ -151,7 +203,8 @@ def save(name, meta, **arrays):
 
 def main():
     global REF, TESTS
-    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("AOAKV_REFERENCE")
+    root = sys.argv[1] if len(sys.argv) > 1 and not sys.argv[1].startswith("--") else \
+        os.environ.get("AOAKV_REFERENCE")
     if not root:
         sys.exit("usage: make_golden.py <reference checkout> (or set AOAKV_REFERENCE)")
     REF = Path(root).resolve()
@@ -159,6 +212,9 @@ def main():
     if not (REF / "filtering" / "filter_util.py").is_file():
         sys.exit(f"{REF}: no filtering/filter_util.py (not the reference checkout)")
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    make_page_table_goldens()
+    if "--only" in sys.argv and sys.argv[sys.argv.index("--only") + 1] == "page_table":
+        return
     fu = load_filter_util()
     for name, seed, H, S, D, P, budget, method, fixed, dist in SIM_CASES:
         q, K, V = gen_qkv(seed, H, S, D, dist)
