@@ -415,15 +415,16 @@ def workload_config(a, n_gpus):
     }
 
 
-def setup_layers(ctx, layers, budget, seed, method, dev, outlier=True):
+def setup_layers(ctx, layers, budget, seed, method, dev, outlier=True, spare_tokens=P):
     """An InferenceController holding `layers` layers of ctx-1 cached tokens,
-    ready for the decode step of token ctx; returns (ctl, [(q, k, v)])."""
+    ready for the decode step of token ctx, with room for spare_tokens more;
+    returns (ctl, [(q, k, v)])."""
     import torch
 
     import aoa_kv_b200 as ak
     gen = torch.Generator(device=dev).manual_seed(seed)
-    ctl = ak.InferenceController(layers, H, D, P, budget // P, ctx + P, torch.float16, dev,
-                                 method=method)
+    ctl = ak.InferenceController(layers, H, D, P, budget // P, ctx + spare_tokens, torch.float16,
+                                 dev, method=method)
     ctl.prepare_metadata(ctx - 1)
     ctl.begin_forward(ctx - 1)
     news = []
@@ -442,6 +443,65 @@ def setup_layers(ctx, layers, budget, seed, method, dev, outlier=True):
     return ctl, news
 
 
+def graph_token_e2e(a, ctl, pin_qkv, world, dev):
+    """The decode loop through the device-resident page table: per token one
+    H2D copy of every layer's q/k/v (pinned), one CUDA graph replay (device
+    page-table append of the token + the 32 layers' aoakv_decode_step_table)
+    and one D2H copy of every layer's output. The sequence really grows by one
+    token per replay (the headline replays the same token); the page table is
+    built over the headline's caches (a fresh device pool hands out the same
+    page ids as the host pool did)."""
+    import torch
+
+    import aoa_kv_b200 as ak
+    kv0, meta0 = ctl.kv_cache.buf_layer(0), ctl.metadata_cache.buf_layer(0)
+    pt = ak.DevicePageTable(1, kv0.shape[0], kv0.shape[0], meta0.shape[0], P, dev)
+    pt.append(a.ctx - 1)
+    n = (a.ctx - 1 + P - 1) // P
+    same = bool(torch.equal(pt.kv_indices(0)[:n], ctl.kv_indices_with_last[:n]))
+    dev_qkv = torch.empty_like(pin_qkv, device=dev)  # [L, 3, 1, H, D]
+    o_all = torch.empty(a.layers, 1, H, D, dtype=torch.float16, device=dev)
+    host_o = torch.empty(a.layers, 1, H, D, dtype=torch.float16).pin_memory()
+    dev_qkv.copy_(pin_qkv)
+
+    def token():
+        pt.append(1)
+        for layer in range(a.layers):
+            pt.decode_step(dev_qkv[layer, 0], dev_qkv[layer, 1], dev_qkv[layer, 2], o_all[layer],
+                           ctl.kv_cache.buf_layer(layer), ctl.metadata_cache.buf_layer(layer),
+                           ctl.v_log_norm_layer(layer), a.budget // P, ctl.score_mode, False)
+    token()  # once outside capture (kernel attributes)
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        g.capture_begin()
+        token()
+        g.capture_end()
+    torch.cuda.current_stream().wait_stream(side)
+
+    def step():
+        dev_qkv.copy_(pin_qkv, non_blocking=True)
+        g.replay()
+        host_o.copy_(o_all, non_blocking=True)
+    ems = time_replays(step, a.steps, a.warmup, world, dev)
+    dms = time_replays(g.replay, a.steps, 0, world, dev)
+    ak.check_device()
+    tokens = 1 + a.warmup + 2 * a.steps
+    del g
+    pt.close()
+    return {"value": round(ems * 1e3 / (a.steps * a.layers), 3), "unit": "us",
+            "device_only_us": round(dms * 1e3 / (a.steps * a.layers), 3),
+            "h2d_bytes_per_step": a.layers * 3 * H * D * 2,
+            "d2h_bytes_per_step": a.layers * H * D * 2,
+            "context_tokens": f"{a.ctx} .. {a.ctx + tokens - 1} (one more per replay)",
+            "page_ids_match_host_pool": same,
+            "gpu_launches": (1 + a.layers) * a.steps,
+            "api": "DevicePageTable (aoakv_page_table_append + aoakv_decode_step_table per "
+                   "layer) captured once as a CUDA graph of the whole token; per token one H2D "
+                   "of all layers' q/k/v, one replay, one D2H of all outputs"}
+
+
 def run_headline(a):
     import ctypes
 
@@ -453,7 +513,7 @@ def run_headline(a):
     ak._lib.load()
     peak, peak_src = load_peak()
 
-    ctl, news = setup_layers(a.ctx, a.layers, a.budget, a.seed, a.method, dev)
+    ctl, news = setup_layers(a.ctx, a.layers, a.budget, a.seed, a.method, dev, spare_tokens=256)
     outs = [torch.empty(1, H, D, dtype=torch.float16, device=dev) for _ in range(a.layers)]
     nk, ncl = ctypes.c_int32(0), ctypes.c_int32(0)
     ak._lib.call("aoakv_step_plan_info", ctl.step_plan(0)._h, len(ctl.kv_cache.indicies), 0,
@@ -522,6 +582,10 @@ def run_headline(a):
                       "aoakv_step_plan_run); one H2D of the step's q/k/v and one D2H of its "
                       "outputs; no graph; per GPU"}
 
+    e2e_graph = None
+    if not a.no_e2e:
+        e2e_graph = graph_token_e2e(a, ctl, pin_qkv, world, dev)
+
     if sampler:
         sampler.stop()
     clocks = sampler.summary(t_soak, t_timed_end) if sampler else None
@@ -552,7 +616,8 @@ def run_headline(a):
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic", "config": workload_config(a, world),
             "roofline": r, "estimate_roofline": er,
-            "e2e": e2e, "gpu_launches": kernels_per_layer * a.layers * a.steps,
+            "e2e": e2e, "e2e_graph_token": e2e_graph,
+            "gpu_launches": kernels_per_layer * a.layers * a.steps,
             "step_kernels_per_layer": kernels_per_layer, "clocks": clocks,
             "library_md5": lib_md5(), "cpu_baseline": cpu,
         }
