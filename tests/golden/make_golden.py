@@ -29,7 +29,11 @@ lengths are recorded.
 Inputs come from tests/golden/gen.py (seeded, fp16); each file stores the
 input digest, the case parameters and the reference outputs.
 
-``--only page_table`` regenerates just the page-table files.
+Prefill attention (``pf_*.npz``): the reference test's own CPU attention,
+_ref_self_attention of kernels/aoa_kv/quest/tests/test_prefill_attention.py:
+17-40 (causal, fp16 inputs, its softmax cast back to fp16 before P.V).
+
+``--only page_table`` / ``--only prefill`` regenerate just those files.
 """
 from __future__ import annotations
 
@@ -106,6 +110,26 @@ def load_ref_kv_cache():
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     return mod
+
+
+PF_CASES = [  # name, seed, qo_len, kv_len, heads (test_prefill_attention.py:42 grid)
+    ("pf_13_33", 51, 13, 33, 4), ("pf_77_400", 52, 77, 400, 2), ("pf_244_244", 53, 244, 244, 2),
+    ("pf_311_1110", 54, 311, 1110, 1),
+]
+
+
+def make_prefill_goldens():
+    t_pf = load_ref_test("test_prefill_attention")
+    for name, seed, qo, kvl, heads in PF_CASES:
+        g = np.random.default_rng(seed)
+        q = g.standard_normal((qo, heads, 128), dtype=np.float32).astype(np.float16)
+        k = g.standard_normal((kvl, heads, 128), dtype=np.float32).astype(np.float16)
+        v = g.standard_normal((kvl, heads, 128), dtype=np.float32).astype(np.float16)
+        o = t_pf._ref_self_attention(torch.from_numpy(q), torch.from_numpy(k),
+                                     torch.from_numpy(v))
+        save(name, dict(seed=seed, qo_len=qo, kv_len=kvl, heads=heads, D=128), q=q, k=k, v=v,
+             out=o.numpy().astype(np.float16))
+        print(name, tuple(o.shape))
 
 
 def make_page_table_goldens():
@@ -212,8 +236,12 @@ def main():
     if not (REF / "filtering" / "filter_util.py").is_file():
         sys.exit(f"{REF}: no filtering/filter_util.py (not the reference checkout)")
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    make_page_table_goldens()
-    if "--only" in sys.argv and sys.argv[sys.argv.index("--only") + 1] == "page_table":
+    only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
+    if only in (None, "page_table"):
+        make_page_table_goldens()
+    if only in (None, "prefill"):
+        make_prefill_goldens()
+    if only is not None:
         return
     fu = load_filter_util()
     for name, seed, H, S, D, P, budget, method, fixed, dist in SIM_CASES:

@@ -11,6 +11,7 @@ own CPU attention (quest/tests/test_prefill_attention.py:17-40).
     running-max rescale of O in tensor memory), the log-sum-exp output;
   * unused cache slots hold NaN: the last page's tail must not reach O."""
 import math
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -130,3 +131,21 @@ def test_prefill_rejects_qo_longer_than_kv(cuda):
     ids = torch.arange(2, dtype=torch.int32, device="cuda")
     with pytest.raises(_lib.AoaKvError, match="qo_len <= kv_len"):
         ak.prefill_with_paged_kv_cache(q, kv, ids, 16, True, 0)
+
+
+PF_GOLDEN = sorted(p.stem for p in (Path(__file__).resolve().parent / "golden").glob("pf_*.npz"))
+
+
+@pytest.mark.parametrize("name", PF_GOLDEN)
+def test_prefill_matches_reference_test_outputs(cuda, name):
+    """The kernel against outputs of the reference test's own CPU attention
+    (tests/golden/pf_*.npz, test_prefill_attention.py:17-40), at that test's
+    tolerance, with the KV scattered over NaN-filled pages."""
+    g = np.load(Path(__file__).resolve().parent / "golden" / f"{name}.npz")
+    q, K, V = g["q"], g["k"], g["v"]
+    P = 16
+    kv, ids, last = paged(K, V, P, (K.shape[0] + P - 1) // P + 3, len(name))
+    o = ak.prefill_with_paged_kv_cache(torch.from_numpy(q).cuda(), kv, ids, last, True, 0)
+    torch.cuda.synchronize()
+    ok, err = close(o.float().cpu().numpy(), g["out"].astype(np.float32))
+    assert ok, f"max |gpu - reference| = {err}"

@@ -2,6 +2,7 @@
 (tests/golden/make_golden.py): the simulation (filter_util.py) for semantics A
 and the kernel tree's CPU test references for semantics B."""
 import math
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -183,3 +184,18 @@ def test_topk_positions_against_brute_force_sort():
         assert list(got) == want
 
     check()
+
+
+PF_GOLDEN = sorted(p.stem for p in (Path(__file__).resolve().parent / "golden").glob("pf_*.npz"))
+
+
+@pytest.mark.parametrize("name", PF_GOLDEN)
+def test_prefill_oracle_matches_reference_test_attention(name):
+    """oracle.kernel_tree.prefill_attention against the reference test's own
+    CPU attention (test_prefill_attention.py:17-40), which rounds its
+    softmax to fp16 before P.V: equal within that rounding."""
+    g = np.load(Path(__file__).resolve().parent / "golden" / f"{name}.npz")
+    o, _ = kt.prefill_attention(g["q"], g["k"], g["v"], True)
+    ref = g["out"].astype(np.float32)
+    assert np.abs(o - ref).max() <= 2e-3 + 5e-3 * np.abs(ref).max()
+    assert np.abs(o - ref).mean() < 2e-4

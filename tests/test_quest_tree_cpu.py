@@ -41,7 +41,11 @@ def test_tree_resolves_inside_itself_and_exports_reference_names(quest_tree):
         assert hasattr(kernels, name), name
 
 
-def test_out_of_path_ops_raise_not_implemented(quest_tree):
+def test_prefill_is_the_library_op_and_the_model_is_not_provided(quest_tree):
+    import aoa_kv_b200
     utils = importlib.import_module("quest.utils")
+    kernels = importlib.import_module("quest._kernels")
+    assert utils.prefill_forward is aoa_kv_b200.prefill_forward
+    assert callable(kernels.prefill_with_paged_kv_cache)
     with pytest.raises(NotImplementedError):
-        utils.prefill_forward(None, None, 0)
+        quest_tree.LlamaForCausalLM
