@@ -1403,6 +1403,17 @@ def run_kernels(a):
     def chained():
         chain.run(q, k, v, o, ctl.kv_indices_with_last, n, ctl.kv_cache.last_page_len,
                   ctl.metadata_indices, None, sws, sws.numel(), st())
+
+    # prefill attention of an 8192-token prompt over this layer's first pages
+    # (q 67 MB, the pages' K/V 134 MB: larger than L2)
+    pf_s = 8192
+    pf_q = torch.randn(pf_s, H, D, device=dev).half()
+    pf_o = torch.empty_like(pf_q)
+
+    def prefill_attn():
+        _lib.call("aoakv_prefill_paged", pf_q.data_ptr(), pf_o.data_ptr(), None, kv_p, kv_cap,
+                  ctl.kv_indices_with_last.data_ptr(), pf_s // P, P, pf_s, H, H, D, P, 0, 1,
+                  0.0, st())
     sb = step_bytes(a.ctx, a.budget, a.method)
     cases = [
         ("append_decode", append, 2 * H * D * 2 * 2 + 2 * H * D * 2 * 2),
@@ -1431,6 +1442,20 @@ def run_kernels(a):
             ts.append(e0.elapsed_time(e1) * 1e3)
         us = statistics.mean(ts)
         out["kernels"][name] = {"us": round(us, 3), **roof(b, us, peak)}
+    prefill_attn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(5):
+        flush.fill_(1)
+        e0.record()
+        prefill_attn()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    us = statistics.mean(ts)
+    flops = 4.0 * D * H * pf_s * (pf_s + 1) / 2
+    out["kernels"]["prefill_attn_8k"] = {"us": round(us, 3), "bound": "tensor",
+                                         "tflops": round(flops / us / 1e6, 1), "flops": flops}
     _lib.check_device()
     chain.close()
     print(json.dumps(out), flush=True)
