@@ -57,6 +57,12 @@ class DevicePageTable:
         for r in (range(self.num_seqs) if seq < 0 else [seq]):
             self.seq_len[r] += int(num_tokens)
 
+    def sync_mirror(self) -> None:
+        """Re-reads the token counts from the device (synchronises): after an
+        append the device refused (AOAKV_DEV_ERR_NO_PAGES) the host mirror,
+        which assumes every append succeeds, is corrected here."""
+        self.seq_len = self.counts()["seq_len"]
+
     def note_replayed(self, num_tokens: int, seq: int = -1) -> None:
         """Advances the host mirror for appends replayed from a CUDA graph
         (capturing append() advances it once, at capture)."""

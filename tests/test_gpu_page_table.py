@@ -53,9 +53,9 @@ def test_device_allocator_matches_oracle(cuda):
         torch.cuda.synchronize()
         dev = _lib.device_error()
         assert dev == (3 if orc.errors > errors else 0), (kind, n, seq)
-        if orc.errors > errors:  # the host mirror follows the refused append: undo it
-            for r in (range(R) if seq < 0 else [seq]):
-                pt.seq_len[r] = orc.seq_len[r]
+        if orc.errors > errors:  # the host mirror assumed success: re-read it
+            pt.sync_mirror()
+            assert pt.seq_len == orc.seq_len
         check_same(pt, orc)
     pt.close()
 
