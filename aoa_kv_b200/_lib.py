@@ -78,7 +78,7 @@ SIGNATURES = {
     "aoakv_page_table_release": [_c_p, _c_i32, _c_p],
     "aoakv_page_table_layout": [_c_p, ctypes.POINTER(ctypes.c_int64)],
     "aoakv_decode_step_table": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_p, _c_i32, _c_p,
-                                _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p],
+                                _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_f, _c_f, _c_p],
     "aoakv_shard_propose": [_c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_p],
     "aoakv_shard_finish": [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_p,
                            _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_p],

@@ -898,7 +898,9 @@ static int run_batched(const void* q, const void* k_new, const void* v_new, void
                        const int32_t* metadata_indices, void* v_log_norm, int32_t num_requests,
                        int32_t max_pages, int32_t num_heads, int32_t head_dim, int32_t page_size,
                        int32_t page_budget, int32_t score_mode, int32_t sink_first_page,
-                       int32_t* selected_out, void* stream) {
+                       int32_t* selected_out, void* stream, float rope_scale = 0.f,
+                       float rope_theta = 0.f) {
+  AOAKV_CHECK_ARG(rope_scale <= 0.f || rope_theta > 0.f, "step: rope_theta must be > 0");
   AOAKV_CHECK_ARG(q && k_new && v_new && o && kv_data && kv_indptr && kv_indices &&
                       kv_last_page_len && metadata_data && metadata_indptr && metadata_indices &&
                       v_log_norm,
@@ -949,6 +951,12 @@ static int run_batched(const void* q, const void* k_new, const void* v_new, void
   a.err = dev_error_ptr();
   a.kv_indptr = kv_indptr;
   a.kv_ends = kv_ends;
+  if (rope_scale > 0.f) {  // each request's own new-token position (rope_pos < 0)
+    a.rope = 1;
+    a.rope_pos = -1;
+    a.rope_rcp_scale = 1.f / rope_scale;
+    a.rope_log2_rcp_theta = std::log2(1.f / rope_theta);
+  }
   a.meta_indptr = metadata_indptr;
   a.last_lens = kv_last_page_len;
   a.budget = page_budget;
@@ -979,7 +987,7 @@ extern "C" int aoakv_decode_step_table(
     void* kv_data, int32_t kv_capacity_pages, void* metadata_data,
     int32_t metadata_capacity_pages, void* v_log_norm, int32_t num_heads, int32_t head_dim,
     int32_t page_budget, int32_t score_mode, int32_t sink_first_page, int32_t* selected_out,
-    void* stream) {
+    float rope_scale, float rope_theta, void* stream) {
   AOAKV_NVTX("aoakv_decode_step_table");
   AOAKV_CHECK_ARG(table != nullptr, "table step: NULL table");
   const PageTable* pt = reinterpret_cast<const PageTable*>(table);
@@ -991,5 +999,5 @@ extern "C" int aoakv_decode_step_table(
                      b + L.kv_end, b + L.kv_indices, b + L.last_len, metadata_data,
                      metadata_capacity_pages, b + L.meta_start, b + L.meta_indices, v_log_norm,
                      L.R, L.M, num_heads, head_dim, L.P, page_budget, score_mode,
-                     sink_first_page, selected_out, stream);
+                     sink_first_page, selected_out, stream, rope_scale, rope_theta);
 }

@@ -101,15 +101,20 @@ class DevicePageTable:
 
     def decode_step(self, q, k_new, v_new, o, kv_data, metadata_data, v_log_norm, page_budget,
                     score_mode=_lib.SCORE_AOAKV, sink_first_page=False,
-                    selected_out: Optional[torch.Tensor] = None) -> None:
+                    selected_out: Optional[torch.Tensor] = None,
+                    rope_scale: Optional[float] = None, rope_theta: float = 1e4) -> None:
         """One layer's decode step for every sequence (aoakv_decode_step_table):
-        q, k_new, v_new, o [num_seqs, H, D]; counts read on the device."""
+        q, k_new, v_new, o [num_seqs, H, D]; counts read on the device. With
+        rope_scale, q and k_new arrive unrotated and are rotated at each
+        sequence's new-token position (left rotated in place)."""
         H, D = q.shape[-2], q.shape[-1]
         _lib.call("aoakv_decode_step_table", self._h, q.data_ptr(), k_new.data_ptr(),
                   v_new.data_ptr(), o.data_ptr(), kv_data.data_ptr(), kv_data.shape[0],
                   metadata_data.data_ptr(), metadata_data.shape[0], v_log_norm.data_ptr(), H, D,
                   int(page_budget), int(score_mode), int(bool(sink_first_page)),
-                  None if selected_out is None else selected_out.data_ptr(), self._stream())
+                  None if selected_out is None else selected_out.data_ptr(),
+                  0.0 if rope_scale is None else float(rope_scale), float(rope_theta),
+                  self._stream())
 
     def close(self) -> None:
         if self._h:

@@ -582,13 +582,17 @@ AOAKV_API int aoakv_page_table_layout(aoakv_page_table table, int64_t* words);
  * call can be captured in a CUDA graph and replayed after
  * aoakv_page_table_append(table, -1, 1) for every token. q, k_new, v_new, o
  * are [num_seqs, num_heads, head_dim] (the new token already counted by the
- * append); an empty sequence is skipped. Same limits as the batched step. */
+ * append); an empty sequence is skipped. Same limits as the batched step.
+ * rope_scale > 0 fuses RoPE as aoakv_step_plan_set_rope does: q and k_new
+ * arrive unrotated, each sequence's pair is rotated at that sequence's
+ * new-token position (read on the device) and left rotated in place;
+ * rope_scale <= 0: no RoPE. */
 AOAKV_API int aoakv_decode_step_table(
     aoakv_page_table table, const void* q, const void* k_new, const void* v_new, void* o,
     void* kv_data, int32_t kv_capacity_pages, void* metadata_data,
     int32_t metadata_capacity_pages, void* v_log_norm, int32_t num_heads, int32_t head_dim,
     int32_t page_budget, int32_t score_mode, int32_t sink_first_page, int32_t* selected_out,
-    void* stream);
+    float rope_scale, float rope_theta, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -159,3 +159,51 @@ def test_table_decode_token_graph_matches_oracle(cuda, mode, sink):
     assert _lib.device_error() == 0
     del graph
     pt.close()
+
+
+def test_table_step_with_fused_rope_equals_rope_then_step(cuda):
+    """RoPE fused into the page-table step (rope_scale > 0) gives the same bits
+    as aoakv_apply_rope_in_place at each sequence's new-token position
+    followed by the step without RoPE: outputs, selections, the caches after,
+    and q and k left rotated in place."""
+    R, H, D, P, budget = 2, 8, 128, 16, 6
+    S0 = [100, 171]
+    cap, mcap, M = 64, 8, 30
+    runs = []
+    for fused in (False, True):
+        g = np.random.default_rng(5)
+        kv = torch.from_numpy(g.standard_normal((cap, 2, P, H, D), dtype=np.float32)
+                              .astype(np.float16)).cuda()
+        meta = torch.from_numpy(g.standard_normal((mcap, 2, P, H, D), dtype=np.float32)
+                                .astype(np.float16)).cuda()
+        vlog = torch.zeros(cap, H, dtype=torch.float16, device="cuda")
+        pt = ak.DevicePageTable(R, M, cap, mcap, P)
+        for r in range(R):
+            _, K, V = gen_qkv(70 + r, H, S0[r], D, "outlier")
+            pt.append(S0[r], r)
+            n = pt.num_pages(r)
+            Kd, Vd = torch.from_numpy(K).cuda(), torch.from_numpy(V).cuda()
+            _lib.call("aoakv_append_kv_cache_prefill", ptr(Kd), ptr(Vd), S0[r], ptr(kv),
+                      ptr(pt.kv_indices(r)), n, pt.last_page_len(r), cap, ptr(meta),
+                      ptr(pt.metadata_indices(r)), -(-n // P), (n - 1) % P + 1, mcap, ptr(vlog),
+                      H, D, P, 0, stream())
+        q = torch.from_numpy(np.stack([gen_qkv(80 + r, H, 1, D)[0] for r in range(R)])).cuda()
+        kn = torch.from_numpy(np.stack([gen_qkv(90 + r, H, 2, D)[1][0] for r in range(R)])).cuda()
+        vn = torch.from_numpy(np.stack([gen_qkv(90 + r, H, 2, D)[2][0] for r in range(R)])).cuda()
+        o = torch.empty_like(q)
+        sel = torch.full((R, H, budget), -9, dtype=torch.int32, device="cuda")
+        pt.append(1)
+        if not fused:
+            for r in range(R):  # the new token of sequence r sits at position S0[r]
+                _lib.call("aoakv_apply_rope_in_place", ptr(q[r]), ptr(kn[r]), 1, S0[r], H, D,
+                          1.0, 1e4, stream())
+            pt.decode_step(q, kn, vn, o, kv, meta, vlog, budget, selected_out=sel)
+        else:
+            pt.decode_step(q, kn, vn, o, kv, meta, vlog, budget, selected_out=sel,
+                           rope_scale=1.0, rope_theta=1e4)
+        torch.cuda.synchronize()
+        runs.append([x.cpu() for x in (o, sel, q, kn, kv, meta, vlog)])
+        pt.close()
+    for a, b in zip(*runs):
+        assert torch.equal(a, b)
+    assert _lib.device_error() == 0
